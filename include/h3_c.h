@@ -1,0 +1,211 @@
+/* C ABI of the B200 implementation of the MiniMax-H3 transformer step (libh3b200.so).
+ *
+ * Drop-in for the transformer the reference's sampler calls once per schedule point: the C++ class
+ * mako::models::H3 (aliased video::H3, src/video/engine.hpp:22 of jhanssen/mako-video). Each entry point below names
+ * the reference call it replaces. Plain pointers and sizes only; every call returns H3_OK or an error code, and
+ * h3_last_error() gives the message of the last failure on the calling thread (the reference throws
+ * std::runtime_error at the same places; include/models/h3.hpp re-throws).
+ *
+ * One process per GPU. With more than one rank the step is sequence-parallel (Ulysses): every rank passes the same
+ * inputs, holds the same weights, computes a contiguous share of the rows outside attention and all rows for
+ * heads / ranks heads inside it, and returns the full outputs. */
+#ifndef H3_C_H
+#define H3_C_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define H3_OK 0
+#define H3_ERR_ARG 1    /* bad argument or shape */
+#define H3_ERR_CUDA 2   /* a CUDA or NCCL call failed */
+#define H3_ERR_STATE 3  /* call out of order (step before begin) */
+#define H3_ERR_DEVICE 4 /* a kernel reported a device-side failure (a bounded wait ran out) */
+
+typedef struct h3_model h3_model;
+
+/* Model shape. MiniMax-H3: dim 5376, heads 56, ffn 14336, blocks 50, time_dim 2688 (docs/architecture.md:23-27,
+ * 47-67); the benchmark's synthetic 768p stack: 5120, 40, 13824, 48, 2560. Heads are 128 wide. */
+typedef struct h3_config {
+    uint32_t dim, heads, ffn, blocks, time_dim;
+    uint32_t text_dim;       /* the text encoder's width (5120, H3::kText) */
+    uint32_t video_patch;    /* 96 (H3::kVideoPatch: a 2x2 patch of 24 channels) */
+    uint32_t audio_channels; /* 32 (H3::kAudioChannels) */
+    float eps;               /* RMS norm epsilon */
+} h3_config;
+
+/* The packed sequence [text | keyframe rows | audio | generated video] (H3::Layout, src/video/engine.cpp:666-676;
+ * tests/h3_ref_test.cpp:194). References (ref2va) are not supported: a layout with them is refused. */
+typedef struct h3_layout {
+    uint32_t text;        /* text rows T */
+    uint32_t frames;      /* generated latent frames */
+    uint32_t h, w;        /* latent height and width (a row is a 2x2 patch: (h / 2) * (w / 2) rows a frame) */
+    uint32_t audio;       /* audio latents per channel (2 * audio rows) */
+    uint32_t cond_frames; /* keyframe latent frames (rows held at t = 0.999) */
+    const uint8_t* cond_last; /* [cond_frames]: keyframe anchored at the last generated frame (NULL: all first) */
+    const uint8_t* text_tags; /* [text]: modality tag per text row, 1 text or 0 video (NULL: all text) */
+} h3_layout;
+
+typedef struct h3_world {
+    int32_t rank, size;      /* this process's rank and the number of ranks (one GPU each) */
+    uint8_t nccl_id[128];    /* from h3_nccl_unique_id on rank 0, passed to every rank */
+} h3_world;
+
+/* Probe callback (H3::set_probe, tests/h3_ref_test.cpp:215-217): name is one of temb, mod0, x0, block, norm_out;
+ * layer is the block for "block" and -1 otherwise; data is host memory valid during the call. Single-rank only. */
+typedef void (*h3_probe_fn)(void* user, const char* name, int32_t layer, const float* data, uint64_t n);
+
+/* The message of the last failed call on this thread ("" if none). */
+const char* h3_last_error(void);
+
+/* An NCCL unique id for a multi-rank group (rank 0 makes it, every rank passes it in h3_world). */
+int h3_nccl_unique_id(uint8_t out[128]);
+
+/* H3::H3(path, ctx, telemetry, int8) and Engine::transformer (src/video/engine.cpp:105-117).
+ * weights: "synthetic:SEED" for random-init weights (every value a hash of SEED, tensor and index); loading a
+ * checkpoint directory is not built and returns H3_ERR_ARG. int8_mask: bits 1 qkv, 2 out, 4 fc1, 8 fc2
+ * (H3::Int8). sparse_ratio / sparse_local as h3_set_sparse. world: NULL for one rank. device: the CUDA device. */
+int h3_create(const h3_config* cfg, const char* weights, uint32_t int8_mask, float sparse_ratio, uint32_t sparse_local,
+              const h3_world* world, int32_t device, h3_model** out);
+
+/* H3::set_sparse(ratio, local) (src/video/engine.cpp:112): ratio 0 dense attention, else the share of video cubes
+ * each cube attends; local 0, 1 (itself) or 3 (itself and its temporal neighbours). Takes effect at h3_begin. */
+int h3_set_sparse(h3_model* m, float ratio, uint32_t local);
+
+/* H3::parse_int8 (tools/mako_video.cpp:108-114): "none", "all" or a comma list of qkv, out, fc1, fc2. */
+int h3_parse_int8(const char* text, uint32_t* mask);
+
+/* H3::begin(text, layout) (src/video/engine.cpp:700; tests/h3_ref_test.cpp:218): text is [T][text_dim] fp32 host
+ * memory; caches the text rows and the layout's tables for the steps that follow. */
+int h3_begin(h3_model* m, const float* text, uint32_t text_rows, const h3_layout* layout);
+
+/* H3::step(video, audio, t_video, t_audio) (src/video/engine.cpp:714; tests/h3_ref_test.cpp:224): video [V][96]
+ * (keyframe rows first) and audio [A][32] fp32 host memory in; their velocities out (host memory, same shapes). */
+int h3_step(h3_model* m, const float* video, uint64_t video_rows, const float* audio, uint64_t audio_rows, float t_video,
+            float t_audio, float* out_video, float* out_audio);
+
+/* The same with device pointers; the step is queued on the model's stream (h3_stream) and not waited for. */
+int h3_step_device(h3_model* m, const float* video, uint64_t video_rows, const float* audio, uint64_t audio_rows, float t_video,
+                   float t_audio, float* out_video, float* out_audio);
+
+/* Waits for the model's stream and reports a device-side failure of the queued work as H3_ERR_DEVICE. */
+int h3_synchronize(h3_model* m);
+
+/* The model's CUDA stream (a cudaStream_t). */
+void* h3_stream(h3_model* m);
+
+int h3_set_probe(h3_model* m, h3_probe_fn fn, void* user);
+
+/* H3::rows(layout) (tests/h3_ref_test.cpp:484-502): per row the rotary position (t, h, w) [S][3] in double, the
+ * modality tag (0 video, 1 text, 2 audio) and the role (0 text, 1 keyframe video, 3 audio, 4 video). Any output
+ * may be NULL. h3_layout_rows gives S. */
+uint64_t h3_layout_rows(const h3_layout* layout);
+int h3_rows(const h3_layout* layout, double* pos, uint8_t* tags, uint8_t* roles);
+
+/* The rotary table the step uses for a layout: [S][48][2] (cos, sin) of angle = float(pos_axis) * inv_freq (16
+ * frequencies per axis t, h, w of base 10000; docs/architecture.md:35-40, tools/dump_h3_ref.py:140-141). */
+int h3_rope_table(const h3_layout* layout, float* out);
+
+/* This library's kernel launches in the last step. */
+int32_t h3_last_launches(h3_model* m);
+
+/* Device milliseconds of the last step's stages (start..adaln, ..input, ..block 0 parts, ..blocks, ..heads) when
+ * timing is on; returns the number of stages written (at most `cap`), names as a '\0'-separated list. */
+int h3_set_timing(h3_model* m, int32_t on);
+int32_t h3_last_timing(h3_model* m, float* ms, char* names, int32_t names_cap, int32_t cap);
+
+void h3_destroy(h3_model* m);
+
+/* ------------------------------------------------------------------------------------------------------------
+ * Kernel-level entry points: the reference's GPU kernels (mako-common, named in docs/architecture.md:52,64,124-127
+ * and docs/performance.md:39-45,120-126), each as one sm_100a kernel on device pointers. `stream` is a
+ * cudaStream_t (NULL: the legacy default stream). They do not synchronize; h3k_check does. */
+
+/* Gemm::encode / gemm_i8 with a fused epilogue. D[M][N] = A[M][K] B[N][K]^T; A and B row-major with K contiguous. */
+#define H3K_EPI_BF16 0       /* out bf16 [M][ldo] = acc + bias */
+#define H3K_EPI_F32 1        /* out f32 = acc + bias */
+#define H3K_EPI_QKV 2        /* heads_partial fused: q/k per-head RMS norm + rotary, v + bias; [rows][3][heads][128] */
+#define H3K_EPI_GATE_RESID 3 /* gate_add_rows fused: x += gate[mod_idx[r]] * (acc + bias) */
+#define H3K_EPI_SWIGLU 4     /* swiglu_rows fused: out = silu(gate) * value; B rows in 128-row [gate; value] groups */
+#define H3K_EPI_S32 5        /* int8 only: out int32 = the raw integer dot products */
+typedef struct h3k_gemm_args {
+    int32_t M, N, K;
+    int32_t a_chunks, a_rows_stride, lda, ldb; /* A split into a_chunks column chunks ([chunk][rows][K/chunks]) */
+    void* out;
+    int64_t ldo;
+    const float* bias;
+    float* x;
+    int64_t ldx;
+    const float* mod;       /* [n_mod][6][dim] */
+    const uint8_t* mod_idx; /* [M] */
+    int32_t gate_slot, dim;
+    const float* rope; /* [M][48][2] */
+    const float* qn_w;
+    const float* kn_w;
+    float eps;
+    int32_t inner, heads_per_rank, rows_local;
+    const float* a_scale; /* int8: per row of A */
+    const float* b_scale; /* int8: per row of B */
+} h3k_gemm_args;
+int h3k_gemm(const void* A, const void* B, const h3k_gemm_args* args, int32_t epilogue, int32_t int8, void* stream);
+
+/* rms_mod_rows: y = RMSNorm(x) (* w) * (1 + scale) + shift per row; out_kind 0 bf16, 1 f32, 2 int8 + row scale. */
+int h3k_rms_mod(const float* x, int64_t ldx, int32_t rows, int32_t d, const float* w, const float* mod, const uint8_t* mod_idx,
+                int32_t mod_slots, int32_t shift_slot, int32_t scale_slot, float eps, int32_t out_kind, void* out, int64_t ldo,
+                float* out_scale, void* stream);
+/* gate_add_rows: x += gate * y (y bf16). */
+int h3k_gate_add(float* x, int64_t ldx, const void* y, int64_t ldy, int32_t rows, int32_t d, const float* mod, const uint8_t* mod_idx,
+                 int32_t gate_slot, void* stream);
+/* swiglu_rows: out [rows][F] = silu(gv[:, :F]) * gv[:, F:] (bf16). */
+int h3k_swiglu(const void* gv, int32_t rows, int32_t F, void* out, void* stream);
+/* quant_rows_i8: per-row symmetric int8 (scale = max|x| / 127). */
+int h3k_quant_rows_i8(const void* x, int64_t ldx, int32_t rows, int32_t K, int8_t* q, float* scale, void* stream);
+/* Per-output-row int8 quantisation of a weight (what the int8 load does). */
+int h3k_quant_weight(const void* w, int32_t rows, int32_t K, int8_t* q, float* scale, void* stream);
+/* heads_partial (standalone): per-head q/k RMS norm + rotary in a [rows][3][heads][128] bf16 tensor, in place. */
+int h3k_heads_partial(void* qkv, int32_t rows, int32_t heads, const float* qn_w, const float* kn_w, const float* rope, float eps,
+                      void* stream);
+/* flash_attn_coop_128_32: dense bidirectional attention over `rows` rows and `heads` heads of 128. */
+int h3k_attention(const void* q, const void* k, const void* v, int64_t row_stride, int32_t heads, int32_t rows, void* out,
+                  int64_t out_row_stride, void* stream);
+
+/* The sparse attention's cube grid: dense_rows rows (text, keyframe, audio) then frames x ph x pw generated video
+ * rows (a row is a 2x2 patch), cut into 4x4x4 cubes with the grid padded to multiples of 4. */
+typedef struct h3k_cube_grid {
+    int32_t dense_rows, frames, ph, pw;
+} h3k_cube_grid;
+/* Sizes for a grid: cubes, kcap (selected cubes per query cube at most), q_tiles, max_blocks. */
+int h3k_sparse_sizes(const h3k_cube_grid* g, float ratio, int32_t local, int32_t* cubes, int32_t* kcap, int32_t* q_tiles,
+                     int32_t* max_blocks);
+/* cube_pool + cube_scores + cube_topk: mq, mk [heads][cubes][128] f32, scores [heads][cubes][cubes] f32 (any may be
+ * NULL for internal scratch), sel [heads][cubes][kcap] ascending cube indices, nsel [heads][cubes]. */
+int h3k_sparse_select(const void* q, const void* k, int64_t row_stride, int32_t heads, const h3k_cube_grid* g, float ratio,
+                      int32_t local, float* mq, float* mk, float* scores, int32_t* sel, int32_t* nsel, void* stream);
+/* cube_topk alone, on given scores [heads][cubes][cubes]. */
+int h3k_cube_topk(const float* scores, int32_t heads, const h3k_cube_grid* g, float ratio, int32_t local, int32_t* sel, int32_t* nsel,
+                  void* stream);
+/* The whole sparse attention (selection, pass lists, flash_attn_sparse_128); scratch is allocated per call. */
+int h3k_sparse_attention(const void* q, const void* k, const void* v, int64_t row_stride, int32_t heads, const h3k_cube_grid* g,
+                         float ratio, int32_t local, void* out, int64_t out_row_stride, void* stream);
+
+/* Synthetic parameters as the model makes them (value = mean + std * IH4(seed, tensor_id, i)). */
+int h3k_fill_synthetic(void* dst, int32_t is_bf16, uint64_t n, uint64_t seed, uint32_t tensor_id, float mean, float stdev, void* stream);
+
+/* Time-embedding MLP layer (fp32): out[u][n] = act(W[n] . x[u] + b[n]), act 0 none / 1 silu; out2 (optional) gets
+ * bf16(silu(out)). AdaLN projections: out[(g * U + u) * G + j] = W[g * G + j] . x[u] + b (W bf16). Heads (fp32). */
+int h3k_gemv_f32(const float* W, const float* b, const float* x, int32_t U, int32_t N, int32_t K, int32_t act, float* out, float* out2,
+                 void* stream);
+int h3k_adaln(const void* W, const float* b, const float* x, int32_t U, int32_t groups, int32_t G, int32_t K, float* out, void* stream);
+int h3k_heads(const float* x, int64_t ldx, int32_t rows, const float* W, const float* b, int32_t N, int32_t K, float* out, int64_t ldo,
+              void* stream);
+
+/* Waits for `stream` and reports a device-side failure (bounded wait ran out) as H3_ERR_DEVICE. */
+int h3k_check(void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* H3_C_H */

@@ -1,0 +1,416 @@
+// Flash attention on sm_100a: tcgen05.mma with S and O accumulators in TMEM, K/V tiles streamed by TMA.
+//
+// One CTA per (query tile of 128 rows, head). Warp roles:
+//   warp 0      TMA: the Q tile once, then K and V tiles of 128 keys into a 2-stage ring
+//   warp 1      MMA: S_j = Q K_j^T into one of two TMEM S buffers (so S_{j+1} overlaps the softmax of S_j), then
+//               O += P_j V_j (V as an MN-major operand) into the TMEM O accumulator
+//   warps 2..5  softmax: thread = query row; S row from TMEM, online softmax in the exp2 domain, P (bf16) into
+//               128-byte-swizzled shared memory for the PV MMA; O rescaled in TMEM only when a row's running
+//               maximum grows by more than 2^8 (the exponentials then use the stale maximum, exact after the final
+//               division); at the end O / l from TMEM to HBM.
+// Every tile is four 64x64 TMA boxes (two 64-row units x two 64-dim halves), so the same pipeline serves the dense
+// layout (units of 64 consecutive rows) and the sparse one (a unit is a 4x4x4 latent cube read straight from the
+// model-ordered rows by a 5-D tensor map, the grid's padding zero-filled, or 64 dense rows).
+#include "attention.cuh"
+#include "common.hpp"
+#include "ptx.cuh"
+
+#include <cmath>
+
+namespace h3 {
+
+namespace {
+
+constexpr int NT = 192;
+constexpr int HALF = 16384; // 128 rows x 64 dims bf16
+constexpr int TILE = 32768; // 128 rows x 128 dims
+constexpr int OFF_Q = 0;
+constexpr int OFF_K = TILE;
+constexpr int OFF_V = 3 * TILE;
+constexpr int OFF_P = 5 * TILE;
+constexpr int OFF_BAR = 6 * TILE;
+constexpr int SMEM_BYTES = 6 * TILE + 256 + 1024;
+constexpr float kRescaleThreshold = 8.0f; // log2 units
+
+struct Maps {
+    CUtensorMap q, k, v;    // dense rows: (dim, head, row), box 64 x 1 x 64
+    CUtensorMap cq, ck, cv; // cubes: (dim, head, x, y, frame), box 64 x 1 x 4 x 4 x 4
+};
+
+// Issue the TMA loads of one 64-row unit into rows [64 * half, 64 * half + 64) of a 128-row tile (both dim halves).
+template <bool SPARSE>
+__device__ __forceinline__ void load_unit(uint8_t* tile, int half, int unit, int head, const CUtensorMap* dense, const CUtensorMap* cube,
+                                          const CubeGrid& g, uint64_t* bar)
+{
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+        uint8_t* dst = tile + hh * HALF + half * 8192;
+        if (!SPARSE) {
+            tma_load_3d(dst, dense, bar, hh * 64, head, unit * 64);
+        } else if (unit < g.cubes()) {
+            const int cx = unit % g.ncx, cy = (unit / g.ncx) % g.ncy, ct = unit / (g.ncx * g.ncy);
+            tma_load_5d(dst, cube, bar, hh * 64, head, 4 * cx, 4 * cy, 4 * ct);
+        } else {
+            tma_load_3d(dst, dense, bar, hh * 64, head, (unit - g.cubes()) * 64);
+        }
+    }
+}
+
+// Valid key rows of a unit as a 64-bit mask (bit kr: row kr of the unit is a token).
+__device__ __forceinline__ uint64_t unit_valid_mask(int unit, const CubeGrid& g)
+{
+    if (unit < 0)
+        return 0;
+    if (unit < g.cubes()) {
+        const int cx = unit % g.ncx, cy = (unit / g.ncx) % g.ncy, ct = unit / (g.ncx * g.ncy);
+        const int nx = min(4, g.pw - 4 * cx), ny = min(4, g.ph - 4 * cy), nf = min(4, g.frames - 4 * ct);
+        if (nx == 4 && ny == 4 && nf == 4)
+            return ~0ull;
+        const uint64_t xm = (1ull << nx) - 1;                         // within one 4-row run
+        uint64_t ym = 0;
+        for (int y = 0; y < ny; ++y)
+            ym |= xm << (4 * y);                                      // within one 16-row frame slice
+        uint64_t m = 0;
+        for (int f = 0; f < nf; ++f)
+            m |= ym << (16 * f);
+        return m;
+    }
+    const int first = (unit - g.cubes()) * 64;
+    const int n = min(64, g.dense_rows - first);
+    return n >= 64 ? ~0ull : (n <= 0 ? 0ull : ((1ull << n) - 1));
+}
+
+// The model row of row `r` (0..63) of a unit, or -1 when it is padding.
+__device__ __forceinline__ int unit_row(int unit, int r, const CubeGrid& g)
+{
+    if (unit < g.cubes()) {
+        const int cx = unit % g.ncx, cy = (unit / g.ncx) % g.ncy, ct = unit / (g.ncx * g.ncy);
+        const int x = 4 * cx + (r & 3), y = 4 * cy + ((r >> 2) & 3), f = 4 * ct + (r >> 4);
+        if (x >= g.pw || y >= g.ph || f >= g.frames)
+            return -1;
+        return g.dense_rows + (f * g.ph + y) * g.pw + x;
+    }
+    const int row = (unit - g.cubes()) * 64 + r;
+    return row < g.dense_rows ? row : -1;
+}
+
+__device__ __forceinline__ int4 implicit_entry(int j, const CubeGrid& g)
+{
+    return make_int4(2 * j, 2 * j + 1 < g.units() ? 2 * j + 1 : -1, 15, 0);
+}
+
+template <bool SPARSE>
+__global__ void __launch_bounds__(NT, 1) attn_kernel(const __grid_constant__ Maps maps, const AttnParams p)
+{
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    uint8_t* smem = smem_raw + (((raw + 1023) & ~1023u) - raw);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+    uint64_t* q_full = bars + 0;
+    uint64_t* k_full = bars + 1;   // [2]
+    uint64_t* v_full = bars + 3;   // [2]
+    uint64_t* kv_empty = bars + 5; // [2]
+    uint64_t* s_full = bars + 7;   // [2]
+    uint64_t* p_full = bars + 9;
+    uint64_t* pv_done = bars + 10;
+    uint64_t* drain = bars + 11;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+
+    const int warp = warp_id();
+    const int tile = blockIdx.x, head = blockIdx.y;
+    const CubeGrid& g = p.grid;
+    int nkv;
+    int2 qu;
+    const int4* entries = nullptr;
+    bool implicit = false; // sparse mode, dense query rows: every unit, in order, all visible
+    if constexpr (SPARSE) {
+        nkv = p.nblocks[head * p.q_tiles + tile];
+        implicit = nkv < 0;
+        if (implicit)
+            nkv = (g.units() + 1) / 2;
+        qu = p.q_units[tile];
+        entries = p.blocks + (size_t(head) * p.q_tiles + tile) * p.max_blocks;
+    } else {
+        nkv = (p.rows + 127) / 128;
+        qu = make_int2(2 * tile, 2 * tile + 1);
+    }
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&k_full[i], 1);
+            mbar_init(&v_full[i], 1);
+            mbar_init(&kv_empty[i], 1);
+            mbar_init(&s_full[i], 1);
+        }
+        mbar_init(p_full, 4);
+        mbar_init(pv_done, 1);
+        mbar_init(drain, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t T_O = 256;
+
+    if (nkv > 0 && warp == 0 && elect_one_lane()) {
+        // ------------------------------------------------------------------------------------------ TMA
+        mbar_arrive_expect_tx(q_full, TILE);
+        load_unit<SPARSE>(smem + OFF_Q, 0, qu.x, head, &maps.q, &maps.cq, g, q_full);
+        load_unit<SPARSE>(smem + OFF_Q, 1, qu.y < 0 ? qu.x : qu.y, head, &maps.q, &maps.cq, g, q_full);
+        for (int j = 0; j < nkv; ++j) {
+            const int s = j & 1;
+            if (!mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1))
+                break;
+            int ua = 2 * j, ub = 2 * j + 1;
+            if constexpr (SPARSE) {
+                const int4 e = implicit ? implicit_entry(j, g) : entries[j];
+                ua = e.x;
+                ub = e.y < 0 ? e.x : e.y; // a lone unit is loaded twice and its second copy masked
+            }
+            mbar_arrive_expect_tx(&k_full[s], TILE);
+            load_unit<SPARSE>(smem + OFF_K + s * TILE, 0, ua, head, &maps.k, &maps.ck, g, &k_full[s]);
+            load_unit<SPARSE>(smem + OFF_K + s * TILE, 1, ub, head, &maps.k, &maps.ck, g, &k_full[s]);
+            mbar_arrive_expect_tx(&v_full[s], TILE);
+            load_unit<SPARSE>(smem + OFF_V + s * TILE, 0, ua, head, &maps.v, &maps.cv, g, &v_full[s]);
+            load_unit<SPARSE>(smem + OFF_V + s * TILE, 1, ub, head, &maps.v, &maps.cv, g, &v_full[s]);
+        }
+    } else if (nkv > 0 && warp == 1 && elect_one_lane()) {
+        // ------------------------------------------------------------------------------------------ MMA
+        const uint32_t id_s = idesc_bf16(128, 128);
+        const uint32_t id_pv = idesc_bf16(128, 128, false, true);
+        const uint32_t sq = smem_u32(smem + OFF_Q), sp = smem_u32(smem + OFF_P);
+        auto issue_s = [&](int j) {
+            const uint32_t sk = smem_u32(smem + OFF_K + (j & 1) * TILE);
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+                const uint32_t off = (kk >> 2) * HALF + (kk & 3) * 32;
+                mma_bf16_ss(tmem + (j & 1) * 128, sdesc_sw128(sq + off, 16, 1024), sdesc_sw128(sk + off, 16, 1024), id_s, kk > 0);
+            }
+            mma_commit(&s_full[j & 1]);
+        };
+        bool ok = mbar_wait(q_full, 0) && mbar_wait(&k_full[0], 0);
+        if (ok) {
+            tc_fence_after();
+            issue_s(0);
+        }
+        for (int j = 0; j < nkv && ok; ++j) {
+            if (j + 1 < nkv) {
+                if (!(ok = mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1)))
+                    break;
+                tc_fence_after();
+                issue_s(j + 1);
+            }
+            if (!(ok = mbar_wait(p_full, j & 1) && mbar_wait(&v_full[j & 1], (j >> 1) & 1)))
+                break;
+            tc_fence_after();
+            const uint32_t sv = smem_u32(smem + OFF_V + (j & 1) * TILE);
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+                const uint32_t pa = sp + (kk >> 2) * HALF + (kk & 3) * 32;
+                mma_bf16_ss(tmem + T_O, sdesc_sw128(pa, 16, 1024), sdesc_sw128(sv + kk * 2048, HALF, 1024), id_pv, (j | kk) != 0);
+            }
+            mma_commit(pv_done);
+            mma_commit(&kv_empty[j & 1]);
+        }
+        mma_commit(drain);
+        mbar_wait(drain, 0);
+    } else if (nkv > 0 && warp >= 2) {
+        // -------------------------------------------------------------------------------------- softmax
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane_id();
+        const int qh = row >> 6;
+        const uint32_t tl = tmem + (uint32_t(quarter * 32) << 16);
+        const float sl2 = p.scale * 1.4426950408889634f;
+        float m = -INFINITY, l = 0.f;
+        uint8_t* pbuf = smem + OFF_P;
+        bool ok = true;
+        for (int j = 0; j < nkv; ++j) {
+            if (!(ok = mbar_wait(&s_full[j & 1], (j >> 1) & 1)))
+                break;
+            tc_fence_after();
+            float s[128];
+            {
+                uint32_t r[4][32];
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    tmem_ld32(tl + (j & 1) * 128 + c * 32, r[c]);
+                tmem_wait_ld();
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        s[c * 32 + i] = __uint_as_float(r[c][i]);
+            }
+            // Key masks: keys past the sequence (dense), or padding / unselected units (sparse).
+            uint64_t km[2] = {~0ull, ~0ull};
+            if constexpr (SPARSE) {
+                const int4 e = implicit ? implicit_entry(j, g) : entries[j];
+                km[0] = (e.z >> (2 * qh)) & 1 ? unit_valid_mask(e.x, g) : 0ull;
+                km[1] = (e.y >= 0 && ((e.z >> (2 * qh + 1)) & 1)) ? unit_valid_mask(e.y, g) : 0ull;
+            } else {
+                const int left = p.rows - j * 128;
+                if (left < 128) {
+                    km[0] = left >= 64 ? ~0ull : (left <= 0 ? 0ull : (1ull << left) - 1);
+                    km[1] = left >= 128 ? ~0ull : (left <= 64 ? 0ull : (1ull << (left - 64)) - 1);
+                }
+            }
+            if ((km[0] & km[1]) != ~0ull) {
+#pragma unroll
+                for (int c = 0; c < 128; ++c)
+                    if (!((km[c >> 6] >> (c & 63)) & 1))
+                        s[c] = -INFINITY;
+            }
+            float mx = s[0];
+#pragma unroll
+            for (int c = 1; c < 128; ++c)
+                mx = fmaxf(mx, s[c]);
+            const float m_cand = mx * sl2;
+            const bool need = m_cand > m + kRescaleThreshold;
+            const float m_use = need ? m_cand : m;
+            const float alpha = need ? ex2_approx(m - m_use) : 1.f;
+            const float msub = m_use == -INFINITY ? 0.f : m_use;
+            float rs = 0.f;
+#pragma unroll
+            for (int c = 0; c < 128; ++c) {
+                s[c] = ex2_approx(fmaf(s[c], sl2, -msub));
+                rs += s[c];
+            }
+            if (j > 0) {
+                if (!(ok = mbar_wait(pv_done, (j - 1) & 1)))
+                    break;
+                tc_fence_after();
+                if (__any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+                    for (int c = 0; c < 4; ++c) {
+                        uint32_t o[32];
+                        tmem_ld32(tl + T_O + c * 32, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                        tmem_st32(tl + T_O + c * 32, o);
+                    }
+                    tmem_wait_st();
+                }
+            }
+            l = l * alpha + rs;
+            m = m_use;
+            // P row -> shared memory, K-major with the 128-byte swizzle (16-byte chunk index ^ row % 8).
+#pragma unroll
+            for (int kg = 0; kg < 16; ++kg) {
+                const uint4 v = make_uint4(pack_bf16x2(s[kg * 8 + 0], s[kg * 8 + 1]), pack_bf16x2(s[kg * 8 + 2], s[kg * 8 + 3]),
+                                           pack_bf16x2(s[kg * 8 + 4], s[kg * 8 + 5]), pack_bf16x2(s[kg * 8 + 6], s[kg * 8 + 7]));
+                *reinterpret_cast<uint4*>(pbuf + (kg >> 3) * HALF + row * 128 + (((kg & 7) ^ (row & 7)) << 4)) = v;
+            }
+            fence_proxy_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (elect_one_lane())
+                mbar_arrive(p_full);
+        }
+        if (ok && mbar_wait(pv_done, (nkv - 1) & 1)) {
+            tc_fence_after();
+            int out_row;
+            if constexpr (SPARSE) {
+                const int u = qh ? qu.y : qu.x;
+                out_row = u < 0 ? -1 : unit_row(u, row & 63, g);
+            } else {
+                out_row = tile * 128 + row;
+                if (out_row >= p.rows)
+                    out_row = -1;
+            }
+            const float inv = l > 0.f ? 1.f / l : 0.f;
+            __nv_bfloat16* dst = out_row < 0 ? nullptr
+                                             : reinterpret_cast<__nv_bfloat16*>(p.out) + size_t(out_row) * p.out_row_stride + head * 128;
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+                uint32_t o[32];
+                tmem_ld32(tl + T_O + c * 32, o);
+                tmem_wait_ld();
+                if (dst) {
+                    uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        d4[i] = make_uint4(pack_bf16x2(__uint_as_float(o[8 * i]) * inv, __uint_as_float(o[8 * i + 1]) * inv),
+                                           pack_bf16x2(__uint_as_float(o[8 * i + 2]) * inv, __uint_as_float(o[8 * i + 3]) * inv),
+                                           pack_bf16x2(__uint_as_float(o[8 * i + 4]) * inv, __uint_as_float(o[8 * i + 5]) * inv),
+                                           pack_bf16x2(__uint_as_float(o[8 * i + 6]) * inv, __uint_as_float(o[8 * i + 7]) * inv));
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+CUtensorMap dense_map(const void* base, int heads, int rows, int64_t row_stride)
+{
+    const uint64_t dims[3] = {128, uint64_t(heads), uint64_t(rows > 0 ? rows : 1)};
+    const uint64_t str[2] = {256, uint64_t(row_stride) * 2};
+    const uint32_t box[3] = {64, 1, 64};
+    return make_tmap(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, str, box);
+}
+
+CUtensorMap cube_map(const void* base, int heads, const CubeGrid& g, int64_t row_stride)
+{
+    const void* video = static_cast<const uint8_t*>(base) + size_t(g.dense_rows) * row_stride * 2;
+    const uint64_t rs = uint64_t(row_stride) * 2;
+    const uint64_t dims[5] = {128, uint64_t(heads), uint64_t(g.pw), uint64_t(g.ph), uint64_t(g.frames)};
+    const uint64_t str[4] = {256, rs, rs * g.pw, rs * g.pw * g.ph};
+    const uint32_t box[5] = {64, 1, 4, 4, 4};
+    return make_tmap(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, video, dims, str, box);
+}
+
+} // namespace
+
+void attention(const AttnParams& p, cudaStream_t s)
+{
+    if (p.heads <= 0 || !p.q || !p.k || !p.v || !p.out || (p.row_stride * 2) % 16 || (p.out_row_stride * 2) % 16)
+        throw CudaError("attention: bad arguments");
+    const bool sparse = p.blocks != nullptr;
+    Maps maps;
+    if (!sparse) {
+        if (p.rows <= 0)
+            return;
+        maps.q = dense_map(p.q, p.heads, p.rows, p.row_stride);
+        maps.k = dense_map(p.k, p.heads, p.rows, p.row_stride);
+        maps.v = dense_map(p.v, p.heads, p.rows, p.row_stride);
+        maps.cq = maps.q, maps.ck = maps.k, maps.cv = maps.v;
+    } else {
+        const CubeGrid& g = p.grid;
+        if (g.cubes() <= 0 || !p.nblocks || !p.q_units || p.q_tiles <= 0)
+            throw CudaError("attention: bad sparse arguments");
+        maps.q = dense_map(p.q, p.heads, g.dense_rows, p.row_stride);
+        maps.k = dense_map(p.k, p.heads, g.dense_rows, p.row_stride);
+        maps.v = dense_map(p.v, p.heads, g.dense_rows, p.row_stride);
+        maps.cq = cube_map(p.q, p.heads, g, p.row_stride);
+        maps.ck = cube_map(p.k, p.heads, g, p.row_stride);
+        maps.cv = cube_map(p.v, p.heads, g, p.row_stride);
+    }
+    static bool attr[2] = {false, false};
+    if (!attr[sparse]) {
+        if (sparse)
+            H3_CUDA(cudaFuncSetAttribute(attn_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+        else
+            H3_CUDA(cudaFuncSetAttribute(attn_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+        attr[sparse] = true;
+    }
+    const dim3 grid(sparse ? p.q_tiles : (p.rows + 127) / 128, p.heads);
+    if (sparse)
+        attn_kernel<true><<<grid, NT, SMEM_BYTES, s>>>(maps, p);
+    else
+        attn_kernel<false><<<grid, NT, SMEM_BYTES, s>>>(maps, p);
+    H3_CUDA(cudaGetLastError());
+}
+
+} // namespace h3

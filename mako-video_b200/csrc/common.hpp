@@ -1,0 +1,33 @@
+// Host-side helpers shared by the kernels' launchers: CUDA error checks that throw, tensor-map encoding through the
+// driver entry point (no link-time dependency on libcuda), and the launch-parameter structs of every kernel.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+
+namespace h3 {
+
+struct CudaError : std::runtime_error {
+    using std::runtime_error::runtime_error;
+};
+
+inline void cuda_check(cudaError_t e, const char* what)
+{
+    if (e != cudaSuccess)
+        throw CudaError(std::string(what) + ": " + cudaGetErrorString(e));
+}
+#define H3_CUDA(x) ::h3::cuda_check((x), #x)
+
+// A 2-D or 3-D row-major tensor described for TMA: dims[0] is the contiguous extent, strides in bytes for dims 1..
+// `box` gives the tile copied per load (box[0] * element size must be 128 bytes for the 128-byte swizzle).
+CUtensorMap make_tmap(CUtensorMapDataType type, int rank, const void* base, const uint64_t* dims, const uint64_t* strides_bytes,
+                      const uint32_t* box, bool swizzle128 = true);
+
+// Reads and clears the device error word (nonzero: a kernel's bounded wait ran out or a shape check failed).
+uint32_t take_device_error(cudaStream_t s);
+
+int num_sms();
+
+} // namespace h3

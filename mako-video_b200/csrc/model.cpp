@@ -1,0 +1,756 @@
+// The H3 step's host runtime: weights, per-layout tables, the step's kernel sequence and, with more than one rank,
+// the Ulysses all-to-alls over NCCL (sequence split outside attention, head split inside it).
+#include "model.hpp"
+
+#include "common.hpp"
+#include "embed.cuh"
+#include "gemm.cuh"
+#include "rows.cuh"
+
+#include <nccl.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <sstream>
+
+namespace h3 {
+
+// ------------------------------------------------------------------------------------------------ layout rows
+namespace {
+
+// Time position of generated latent frame f, in audio-latent units (40 a second): the frames before it at 24 fps,
+// the video VAE packing 17 frames into 5 latents as (1, 4, 4, 4, 4).
+double video_time(int f)
+{
+    static const int within[5] = {0, 1, 5, 9, 13};
+    const int frames_before = 17 * (f / 5) + within[f % 5];
+    return 5.0 / 3.0 * frames_before;
+}
+
+} // namespace
+
+Rows layout_rows(const Layout& l)
+{
+    Rows r;
+    const int S = l.rows();
+    r.pos.assign(size_t(S) * 3, 0.0);
+    r.tags.assign(S, 0);
+    r.roles.assign(S, 0);
+    const int ph = l.h / 2, pw = l.w / 2;
+    const double norm = std::sqrt(double(ph) * pw);
+    auto hpos = [&](int y) { return (y + 0.5 - ph / 2.0) / norm * 32.0; };
+    auto wpos = [&](int x) { return (x + 0.5 - pw / 2.0) / norm * 32.0; };
+    int row = 0;
+    for (int i = 0; i < l.text; ++i, ++row) {
+        r.pos[3 * row] = i;
+        r.tags[row] = l.text_tags.empty() ? 1 : l.text_tags[i];
+        r.roles[row] = 0;
+    }
+    const double t0 = l.text;
+    for (int k = 0; k < l.cond_frames; ++k) {
+        const bool last = k < int(l.cond_last.size()) && l.cond_last[k];
+        const double t = t0 + video_time(last ? std::max(l.frames - 1, 0) : 0);
+        for (int y = 0; y < ph; ++y)
+            for (int x = 0; x < pw; ++x, ++row) {
+                r.pos[3 * row] = t, r.pos[3 * row + 1] = hpos(y), r.pos[3 * row + 2] = wpos(x);
+                r.tags[row] = 0, r.roles[row] = 1;
+            }
+    }
+    for (int c = 0; c < 2; ++c)
+        for (int a = 0; a < l.audio; ++a, ++row) {
+            r.pos[3 * row] = t0 + a, r.pos[3 * row + 1] = 0.0, r.pos[3 * row + 2] = wpos(c == 0 ? 0 : pw - 1);
+            r.tags[row] = 2, r.roles[row] = 3;
+        }
+    for (int f = 0; f < l.frames; ++f)
+        for (int y = 0; y < ph; ++y)
+            for (int x = 0; x < pw; ++x, ++row) {
+                r.pos[3 * row] = t0 + video_time(f), r.pos[3 * row + 1] = hpos(y), r.pos[3 * row + 2] = wpos(x);
+                r.tags[row] = 0, r.roles[row] = 4;
+            }
+    return r;
+}
+
+void rope_inv_freq(float out[16])
+{
+    // In float throughout, as torch evaluates 1 / 10000 ** (arange(0, 32, 2, float32) / 32).
+    for (int i = 0; i < 16; ++i) {
+        const float e = float(2 * i) / 32.0f;
+        out[i] = 1.0f / powf(10000.0f, e);
+    }
+}
+
+std::vector<float> rope_table(const Rows& r)
+{
+    float f[16];
+    rope_inv_freq(f);
+    const size_t S = r.tags.size();
+    std::vector<float> t(S * 96);
+    for (size_t i = 0; i < S; ++i)
+        for (int a = 0; a < 3; ++a)
+            for (int k = 0; k < 16; ++k) {
+                const float ang = float(r.pos[3 * i + a]) * f[k];
+                t[i * 96 + (a * 16 + k) * 2] = float(std::cos(double(ang)));
+                t[i * 96 + (a * 16 + k) * 2 + 1] = float(std::sin(double(ang)));
+            }
+    return t;
+}
+
+bool parse_int8(const std::string& s, uint32_t& mask)
+{
+    if (s == "none" || s.empty()) {
+        mask = 0;
+        return true;
+    }
+    if (s == "all") {
+        mask = kInt8Qkv | kInt8Out | kInt8Fc1 | kInt8Fc2;
+        return true;
+    }
+    uint32_t m = 0;
+    std::stringstream ss(s);
+    std::string item;
+    while (std::getline(ss, item, ',')) {
+        if (item == "qkv")
+            m |= kInt8Qkv;
+        else if (item == "out")
+            m |= kInt8Out;
+        else if (item == "fc1")
+            m |= kInt8Fc1;
+        else if (item == "fc2")
+            m |= kInt8Fc2;
+        else
+            return false;
+    }
+    mask = m;
+    return true;
+}
+
+// -------------------------------------------------------------------------------------------------- buffers
+namespace {
+
+struct DevBuf {
+    void* p = nullptr;
+    size_t bytes = 0;
+    DevBuf() = default;
+    DevBuf(const DevBuf&) = delete;
+    DevBuf& operator=(const DevBuf&) = delete;
+    DevBuf(DevBuf&& o) noexcept : p(o.p), bytes(o.bytes) { o.p = nullptr, o.bytes = 0; }
+    DevBuf& operator=(DevBuf&& o) noexcept
+    {
+        if (this != &o) {
+            release();
+            p = o.p, bytes = o.bytes;
+            o.p = nullptr, o.bytes = 0;
+        }
+        return *this;
+    }
+    ~DevBuf() { release(); }
+    void release()
+    {
+        if (p)
+            cudaFree(p);
+        p = nullptr;
+        bytes = 0;
+    }
+    void ensure(size_t n)
+    {
+        if (n <= bytes)
+            return;
+        release();
+        H3_CUDA(cudaMalloc(&p, n));
+        H3_CUDA(cudaMemset(p, 0, n));
+        bytes = n;
+    }
+    template <class T>
+    T* as() const
+    {
+        return static_cast<T*>(p);
+    }
+};
+
+// Synthetic tensor ids (fixed: the CPU oracle regenerates the same values from them).
+enum : uint32_t {
+    kTInW = 1, kTInB, kTOutW, kTOutB, kVpW, kVpB, kApW, kApB, kCondW, kCondB, kFadaW, kFadaB, kHvW, kHvB, kHaW, kHaB,
+    kBlockBase = 100, kBlockStride = 20,
+};
+enum : uint32_t { kAdaW = 0, kAdaB, kNorm1, kQkvW, kQkvB, kQn, kKn, kOutW, kOutB, kNorm2, kFc1W, kFc1B, kFc2W, kFc2B };
+
+constexpr float kStd = 0.02f;
+
+} // namespace
+
+struct Model::Impl {
+    // weights
+    DevBuf t_in_w, t_in_b, t_out_w, t_out_b;
+    DevBuf vp_w, vp_b, ap_w, ap_b, cond_w, cond_b;
+    DevBuf ada_w, ada_b;   // all blocks: [L][18 d][t_dim] bf16, [L][18 d] f32
+    DevBuf fada_w, fada_b; // [2 d][t_dim], [2 d]
+    DevBuf hv_w, hv_b, ha_w, ha_b;
+    struct Block {
+        DevBuf norm1, qkv_w, qkv_b, qn, kn, out_w, out_b, norm2, fc1_w, fc1_b, fc2_w, fc2_b;
+        DevBuf qkv_q, qkv_s, out_q, out_s, fc1_q, fc1_s, fc2_q, fc2_s; // int8 rows and scales
+    };
+    std::vector<Block> blocks;
+    // per layout
+    DevBuf x_text;     // [T][d] f32
+    DevBuf rope;       // [S_local][48][2]
+    DevBuf mod_idx;    // [S_local] u8: level * 3 + tag
+    DevBuf lvl_idx;    // [S_local] u8: level
+    std::vector<uint8_t> h_tags, h_roles, h_lvl_kind; // per global row; lvl_kind: 0 video/text level, 1 audio, 2 cond
+    // per step
+    DevBuf emb, th, temb, tsilu, mods, fmods;
+    DevBuf x, h, hq, hs, qkv, qkv_recv, o, o_recv, act;
+    DevBuf in_video, in_audio, pk_video, pk_audio, rows_out, rows_all;
+    SparseBuffers sp;
+    DevBuf sp_mq, sp_mk, sp_scores, sp_sel, sp_nsel, sp_blocks, sp_nblocks, sp_qunits;
+    ncclComm_t comm = nullptr;
+    std::vector<cudaEvent_t> ev;
+};
+
+#define H3_NCCL(x)                                                                                                       \
+    do {                                                                                                                 \
+        const ncclResult_t r_ = (x);                                                                                     \
+        if (r_ != ncclSuccess)                                                                                           \
+            throw CudaError(std::string("NCCL: ") + #x + ": " + ncclGetErrorString(r_));                                  \
+    } while (0)
+
+Model::Model(const Config& c, uint64_t seed, uint32_t int8_mask, const World& world)
+    : d_(new Impl), c_(c), world_(world), int8_(int8_mask)
+{
+    if (c.dim % 256 || c.inner() % 256 || c.ffn % 128 || (2 * c.ffn) % 256 || c.time_dim % 8 || c.text_dim % 8 || c.dim > 8192)
+        throw CudaError("config: dim and heads*128 multiples of 256, ffn of 128, time_dim and text_dim of 8, dim <= 8192");
+    if (world.size < 1 || world.rank < 0 || world.rank >= world.size || c.heads % world.size)
+        throw CudaError("world: heads must divide evenly over the ranks");
+    H3_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+    if (world.size > 1) {
+        ncclUniqueId id;
+        static_assert(sizeof(id) == 128, "ncclUniqueId size");
+        std::memcpy(&id, world.nccl_id, 128);
+        H3_NCCL(ncclCommInitRank(&d_->comm, world.size, id, world.rank));
+    }
+    const int d = c.dim, L = c.blocks, inner = c.inner(), F = c.ffn, td = c.time_dim;
+    cudaStream_t s = stream_;
+    auto fill = [&](DevBuf& b, size_t n, bool bf16, uint32_t id, float mean, float stdev) {
+        b.ensure(n * (bf16 ? 2 : 4));
+        fill_synthetic(b.p, bf16, n, seed, id, mean, stdev, s);
+    };
+    fill(d_->t_in_w, size_t(d) * 256, false, kTInW, 0.f, kStd);
+    fill(d_->t_in_b, d, false, kTInB, 0.f, kStd);
+    fill(d_->t_out_w, size_t(td) * d, false, kTOutW, 0.f, kStd);
+    fill(d_->t_out_b, td, false, kTOutB, 0.f, kStd);
+    fill(d_->vp_w, size_t(d) * c.video_patch, true, kVpW, 0.f, kStd);
+    fill(d_->vp_b, d, false, kVpB, 0.f, kStd);
+    fill(d_->ap_w, size_t(d) * 64, true, kApW, 0.f, 0.f); // padded to 64 inputs; the first 32 columns filled below
+    {
+        DevBuf tmp;
+        fill(tmp, size_t(d) * c.audio_channels, true, kApW, 0.f, kStd);
+        H3_CUDA(cudaMemcpy2DAsync(d_->ap_w.p, 64 * 2, tmp.p, c.audio_channels * 2, c.audio_channels * 2, d, cudaMemcpyDeviceToDevice, s));
+        H3_CUDA(cudaStreamSynchronize(s));
+    }
+    fill(d_->ap_b, d, false, kApB, 0.f, kStd);
+    fill(d_->cond_w, size_t(d) * c.text_dim, true, kCondW, 0.f, kStd);
+    fill(d_->cond_b, d, false, kCondB, 0.f, kStd);
+    fill(d_->fada_w, size_t(2) * d * td, true, kFadaW, 0.f, kStd);
+    fill(d_->fada_b, size_t(2) * d, false, kFadaB, 0.f, kStd);
+    fill(d_->hv_w, size_t(c.video_patch) * d, false, kHvW, 0.f, kStd);
+    fill(d_->hv_b, c.video_patch, false, kHvB, 0.f, kStd);
+    fill(d_->ha_w, size_t(c.audio_channels) * d, false, kHaW, 0.f, kStd);
+    fill(d_->ha_b, c.audio_channels, false, kHaB, 0.f, kStd);
+    // AdaLN projections of every block in one tensor (one GEMV reads them all): block l at offset l * 18 d * td.
+    d_->ada_w.ensure(size_t(L) * 18 * d * td * 2);
+    d_->ada_b.ensure(size_t(L) * 18 * d * 4);
+    d_->blocks.resize(L);
+    for (int l = 0; l < L; ++l) {
+        const uint32_t base = kBlockBase + kBlockStride * l;
+        fill_synthetic(d_->ada_w.as<uint8_t>() + size_t(l) * 18 * d * td * 2, 1, size_t(18) * d * td, seed, base + kAdaW, 0.f, kStd, s);
+        fill_synthetic(d_->ada_b.as<float>() + size_t(l) * 18 * d, 0, size_t(18) * d, seed, base + kAdaB, 0.f, kStd, s);
+        Impl::Block& b = d_->blocks[l];
+        fill(b.norm1, d, false, base + kNorm1, 1.f, kStd);
+        fill(b.qkv_w, size_t(3) * inner * d, true, base + kQkvW, 0.f, kStd);
+        fill(b.qkv_b, size_t(3) * inner, false, base + kQkvB, 0.f, kStd);
+        fill(b.qn, 128, false, base + kQn, 1.f, kStd);
+        fill(b.kn, 128, false, base + kKn, 1.f, kStd);
+        fill(b.out_w, size_t(d) * inner, true, base + kOutW, 0.f, kStd);
+        fill(b.out_b, d, false, base + kOutB, 0.f, kStd);
+        fill(b.norm2, d, false, base + kNorm2, 1.f, kStd);
+        {
+            // fc1 as stored ([gate; value] rows), then regrouped for the fused SwiGLU epilogue.
+            DevBuf w, bias;
+            fill(w, size_t(2) * F * d, true, base + kFc1W, 0.f, kStd);
+            fill(bias, size_t(2) * F, false, base + kFc1B, 0.f, kStd);
+            b.fc1_w.ensure(size_t(2) * F * d * 2);
+            b.fc1_b.ensure(size_t(2) * F * 4);
+            interleave_gate_value(w.p, F, d, b.fc1_w.p, s);
+            interleave_gate_value_f32(bias.as<float>(), F, b.fc1_b.as<float>(), s);
+            H3_CUDA(cudaStreamSynchronize(s));
+        }
+        fill(b.fc2_w, size_t(d) * F, true, base + kFc2W, 0.f, kStd);
+        fill(b.fc2_b, d, false, base + kFc2B, 0.f, kStd);
+        auto quant = [&](DevBuf& w, DevBuf& q, DevBuf& sc, int rows, int K) {
+            q.ensure(size_t(rows) * K);
+            sc.ensure(size_t(rows) * 4);
+            quant_weight_rows(w.p, rows, K, q.as<int8_t>(), sc.as<float>(), s);
+            H3_CUDA(cudaStreamSynchronize(s));
+            w.release(); // the int8 rows replace the bf16 ones
+        };
+        if (int8_ & kInt8Qkv)
+            quant(b.qkv_w, b.qkv_q, b.qkv_s, 3 * inner, d);
+        if (int8_ & kInt8Out)
+            quant(b.out_w, b.out_q, b.out_s, d, inner);
+        if (int8_ & kInt8Fc1)
+            quant(b.fc1_w, b.fc1_q, b.fc1_s, 2 * F, d);
+        if (int8_ & kInt8Fc2)
+            quant(b.fc2_w, b.fc2_q, b.fc2_s, d, F);
+    }
+    H3_CUDA(cudaStreamSynchronize(s));
+    if (take_device_error(s))
+        throw CudaError("device error during weight set-up");
+}
+
+Model::~Model()
+{
+    if (d_ && d_->comm)
+        ncclCommDestroy(d_->comm);
+    if (d_)
+        for (cudaEvent_t e : d_->ev)
+            cudaEventDestroy(e);
+    d_.reset();
+    if (stream_)
+        cudaStreamDestroy(stream_);
+}
+
+void Model::set_sparse(float ratio, int local)
+{
+    if (!(ratio >= 0.f) || ratio > 1.f)
+        throw CudaError("sparse ratio must be within [0, 1]");
+    if (local != 0 && local != 1 && local != 3)
+        throw CudaError("sparse-local must be 0, 1 or 3");
+    sparse_ratio_ = ratio;
+    sparse_local_ = local;
+}
+
+void Model::alloc_activations()
+{
+    const int d = c_.dim, inner = c_.inner(), F = c_.ffn, P = world_.size, Hp = c_.heads / P;
+    const size_t M = size_t(S_local_);
+    const size_t Spad = M * P;
+    d_->x.ensure(M * d * 4);
+    d_->h.ensure(M * d * 2);
+    const size_t qkv_elems = std::max(M * 3 * inner, M * F);
+    // also holds the final norm's fp32 rows
+    d_->qkv.ensure(std::max(qkv_elems * 2, M * d * 4));
+    if (P > 1) {
+        d_->qkv_recv.ensure(Spad * 3 * Hp * 128 * 2);
+        d_->o_recv.ensure(M * inner * 2);
+    }
+    d_->o.ensure(Spad * Hp * 128 * 2);
+    if (int8_) {
+        d_->hq.ensure(M * std::max({d, F, inner}));
+        d_->hs.ensure(M * 4);
+    }
+    d_->rows_out.ensure(M * 128 * 4);
+    d_->rows_all.ensure(Spad * 128 * 4);
+}
+
+void Model::begin(const float* text, int T, const Layout& l)
+{
+    if (T != l.text)
+        throw CudaError("begin: the text rows do not match the layout");
+    if (l.h % 2 || l.w % 2 || l.frames < 0 || l.audio < 0 || l.cond_frames < 0)
+        throw CudaError("begin: the latent grid must have even sides");
+    if (!l.text_tags.empty() && int(l.text_tags.size()) != T)
+        throw CudaError("begin: one text tag per text row");
+    layout_ = l;
+    S_ = l.rows();
+    if (S_ <= 0)
+        throw CudaError("begin: empty sequence");
+    const int P = world_.size;
+    S_local_ = (S_ + P - 1) / P;
+    row0_ = world_.rank * S_local_;
+    alloc_activations();
+    cudaStream_t s = stream_;
+    const int d = c_.dim;
+    // text rows: condition_proj (text_dim -> d) of the bf16-rounded embeddings
+    d_->x_text.ensure(size_t(std::max(T, 1)) * d * 4);
+    if (T > 0) {
+        DevBuf tin, tpk;
+        tin.ensure(size_t(T) * c_.text_dim * 4);
+        tpk.ensure(size_t(T) * c_.text_dim * 2);
+        H3_CUDA(cudaMemcpyAsync(tin.p, text, size_t(T) * c_.text_dim * 4, cudaMemcpyDefault, s));
+        pack_bf16_rows(tin.as<float>(), T, c_.text_dim, tpk.p, c_.text_dim, s);
+        GemmParams g;
+        g.M = T, g.N = d, g.K = c_.text_dim;
+        g.out = d_->x_text.p, g.ldo = d, g.bias = d_->cond_b.as<float>();
+        gemm_bf16(tpk.p, d_->cond_w.p, g, Epi::f32, s);
+        H3_CUDA(cudaStreamSynchronize(s));
+    }
+    // row tables for this rank's rows
+    const Rows r = layout_rows(l);
+    d_->h_tags = r.tags;
+    d_->h_roles = r.roles;
+    d_->h_lvl_kind.assign(S_, 0);
+    for (int i = 0; i < S_; ++i)
+        d_->h_lvl_kind[i] = r.roles[i] == 3 ? 1 : (r.roles[i] == 1 ? 2 : 0);
+    const std::vector<float> rope = rope_table(r);
+    std::vector<float> local(size_t(S_local_) * 96, 0.f);
+    for (int i = 0; i < S_local_ && row0_ + i < S_; ++i)
+        std::memcpy(&local[size_t(i) * 96], &rope[size_t(row0_ + i) * 96], 96 * 4);
+    d_->rope.ensure(local.size() * 4);
+    H3_CUDA(cudaMemcpyAsync(d_->rope.p, local.data(), local.size() * 4, cudaMemcpyHostToDevice, s));
+    d_->mod_idx.ensure(S_local_);
+    d_->lvl_idx.ensure(S_local_);
+    // sparse buffers
+    if (sparse_ratio_ > 0.f) {
+        CubeGrid g;
+        g.dense_rows = l.dense_rows();
+        g.frames = l.frames, g.ph = l.h / 2, g.pw = l.w / 2;
+        g.nct = (g.frames + 3) / 4, g.ncy = (g.ph + 3) / 4, g.ncx = (g.pw + 3) / 4;
+        if (g.cubes() > 0) {
+            const int Hp = c_.heads / P;
+            SparseBuffers& b = d_->sp;
+            sparse_sizes(g, sparse_ratio_, sparse_local_, b.kcap, b.q_tiles, b.max_blocks);
+            const size_t nc = g.cubes();
+            d_->sp_mq.ensure(size_t(Hp) * nc * 128 * 4);
+            d_->sp_mk.ensure(size_t(Hp) * nc * 128 * 4);
+            d_->sp_scores.ensure(size_t(Hp) * nc * nc * 4);
+            d_->sp_sel.ensure(size_t(Hp) * nc * b.kcap * 4);
+            d_->sp_nsel.ensure(size_t(Hp) * nc * 4);
+            d_->sp_blocks.ensure(size_t(Hp) * b.q_tiles * b.max_blocks * 16);
+            d_->sp_nblocks.ensure(size_t(Hp) * b.q_tiles * 4);
+            d_->sp_qunits.ensure(size_t(b.q_tiles) * 8);
+            b.mq = d_->sp_mq.as<float>(), b.mk = d_->sp_mk.as<float>(), b.scores = d_->sp_scores.as<float>();
+            b.sel = d_->sp_sel.as<int32_t>(), b.nsel = d_->sp_nsel.as<int32_t>();
+            b.blocks = d_->sp_blocks.as<int4>(), b.nblocks = d_->sp_nblocks.as<int32_t>(), b.q_units = d_->sp_qunits.as<int2>();
+        }
+    }
+    H3_CUDA(cudaStreamSynchronize(s));
+    begun_ = true;
+}
+
+void Model::emit_probe(const char* name, int layer, const float* dev, size_t n)
+{
+    if (!probe_)
+        return;
+    std::vector<float> h(n);
+    H3_CUDA(cudaMemcpyAsync(h.data(), dev, n * 4, cudaMemcpyDeviceToHost, stream_));
+    H3_CUDA(cudaStreamSynchronize(stream_));
+    probe_(name, layer, h.data(), n);
+}
+
+void Model::step(const float* video, const float* audio, float t_video, float t_audio, float* out_video, float* out_audio, bool device_io)
+{
+    if (!begun_)
+        throw CudaError("step before begin");
+    cudaStream_t s = stream_;
+    const Layout& l = layout_;
+    const int d = c_.dim, inner = c_.inner(), F = c_.ffn, td = c_.time_dim, L = c_.blocks;
+    const int P = world_.size, Hp = c_.heads / P;
+    const int T = l.text, C = l.cond_rows(), A = l.audio_rows(), V = l.video_rows(), D = l.dense_rows();
+    const int M = S_local_;
+    launches_ = 0;
+    stage_ms_.clear();
+
+    // ---- noise levels: the video / text level, the audio level, the conditioning level (max(t_video, 0.999))
+    const float t_cond = std::max(t_video, 0.999f);
+    std::vector<float> levels;
+    auto level_of = [&](float t) {
+        for (size_t i = 0; i < levels.size(); ++i)
+            if (levels[i] == t)
+                return int(i);
+        levels.push_back(t);
+        return int(levels.size() - 1);
+    };
+    const int lv_video = level_of(t_video);
+    const int lv_audio = A > 0 ? level_of(t_audio) : lv_video;
+    const int lv_cond = C > 0 ? level_of(t_cond) : lv_video;
+    const int U = int(levels.size());
+    {
+        std::vector<uint8_t> midx(M, 0), lidx(M, 0);
+        for (int i = 0; i < M && row0_ + i < S_; ++i) {
+            const int g = row0_ + i;
+            const int kind = d_->h_lvl_kind[g];
+            const int lv = kind == 1 ? lv_audio : (kind == 2 ? lv_cond : lv_video);
+            lidx[i] = uint8_t(lv);
+            midx[i] = uint8_t(lv * 3 + d_->h_tags[g]);
+        }
+        H3_CUDA(cudaMemcpyAsync(d_->mod_idx.p, midx.data(), M, cudaMemcpyHostToDevice, s));
+        H3_CUDA(cudaMemcpyAsync(d_->lvl_idx.p, lidx.data(), M, cudaMemcpyHostToDevice, s));
+        // sinusoidal embeddings [U][256]: cos half first, freq_i = exp(-ln(10000) * i / 128)
+        std::vector<float> emb(size_t(U) * 256);
+        for (int u = 0; u < U; ++u)
+            for (int i = 0; i < 128; ++i) {
+                const float fr = float(std::exp(-std::log(10000.0) * i / 128.0));
+                const float a = levels[u] * fr;
+                emb[u * 256 + i] = float(std::cos(double(a)));
+                emb[u * 256 + 128 + i] = float(std::sin(double(a)));
+            }
+        d_->emb.ensure(emb.size() * 4);
+        H3_CUDA(cudaMemcpyAsync(d_->emb.p, emb.data(), emb.size() * 4, cudaMemcpyHostToDevice, s));
+        // host vectors must outlive the async copies
+        H3_CUDA(cudaStreamSynchronize(s));
+    }
+
+    // ---- inputs
+    const float* dv = video;
+    const float* da = audio;
+    if (!device_io) {
+        d_->in_video.ensure(size_t(std::max(V, 1)) * c_.video_patch * 4);
+        d_->in_audio.ensure(size_t(std::max(A, 1)) * c_.audio_channels * 4);
+        if (V)
+            H3_CUDA(cudaMemcpyAsync(d_->in_video.p, video, size_t(V) * c_.video_patch * 4, cudaMemcpyHostToDevice, s));
+        if (A)
+            H3_CUDA(cudaMemcpyAsync(d_->in_audio.p, audio, size_t(A) * c_.audio_channels * 4, cudaMemcpyHostToDevice, s));
+        dv = d_->in_video.as<float>();
+        da = d_->in_audio.as<float>();
+    }
+    // Timing: an event after each kernel class (from a pool reused across steps); stage i is the time between
+    // events i - 1 and i, named by what ran in between.
+    size_t ev_used = 0;
+    auto mark = [&](const char* name) {
+        if (!timing_)
+            return;
+        if (ev_used == d_->ev.size()) {
+            cudaEvent_t e;
+            H3_CUDA(cudaEventCreate(&e));
+            d_->ev.push_back(e);
+        }
+        H3_CUDA(cudaEventRecord(d_->ev[ev_used++], s));
+        stage_ms_.push_back({name, 0.f});
+    };
+    mark("start");
+
+    // ---- time embedding and modulation
+    d_->th.ensure(size_t(U) * d * 4);
+    d_->temb.ensure(size_t(U) * td * 4);
+    d_->tsilu.ensure(size_t(U) * td * 4);
+    d_->mods.ensure(size_t(L) * U * 18 * d * 4);
+    d_->fmods.ensure(size_t(U) * 2 * d * 4);
+    gemv_f32(d_->t_in_w.as<float>(), d_->t_in_b.as<float>(), d_->emb.as<float>(), U, d, 256, Act::silu, d_->th.as<float>(), nullptr, s);
+    gemv_f32(d_->t_out_w.as<float>(), d_->t_out_b.as<float>(), d_->th.as<float>(), U, td, d, Act::none, d_->temb.as<float>(),
+             d_->tsilu.as<float>(), s);
+    adaln_gemv(d_->ada_w.p, d_->ada_b.as<float>(), d_->tsilu.as<float>(), U, L, 18 * d, td, d_->mods.as<float>(), s);
+    adaln_gemv(d_->fada_w.p, d_->fada_b.as<float>(), d_->tsilu.as<float>(), U, 1, 2 * d, td, d_->fmods.as<float>(), s);
+    launches_ += 4;
+    mark("adaln");
+    emit_probe("temb", -1, d_->temb.as<float>(), size_t(U) * td);
+    emit_probe("mod0", -1, d_->mods.as<float>(), size_t(U) * 18 * d);
+
+    // ---- packed input x0 for this rank's rows [row0, row0 + M)
+    float* x = d_->x.as<float>();
+    H3_CUDA(cudaMemsetAsync(x, 0, size_t(M) * d * 4, s));
+    const int r0 = row0_, r1 = std::min(S_, row0_ + M);
+    auto overlap = [&](int a, int b, int& lo, int& hi) {
+        lo = std::max(a, r0), hi = std::min(b, r1);
+        return lo < hi;
+    };
+    int lo, hi;
+    if (overlap(0, T, lo, hi))
+        H3_CUDA(cudaMemcpyAsync(x + size_t(lo - r0) * d, d_->x_text.as<float>() + size_t(lo) * d, size_t(hi - lo) * d * 4,
+                                cudaMemcpyDeviceToDevice, s));
+    d_->pk_video.ensure(size_t(std::max(V, 1)) * c_.video_patch * 2);
+    d_->pk_audio.ensure(size_t(std::max(A, 1)) * 64 * 2);
+    if (V) {
+        pack_bf16_rows(dv, V, c_.video_patch, d_->pk_video.p, c_.video_patch, s);
+        ++launches_;
+    }
+    if (A) {
+        pack_bf16_rows(da, A, c_.audio_channels, d_->pk_audio.p, 64, s);
+        ++launches_;
+    }
+    auto proj = [&](const void* pk, int ld, int first_in, int model_row0, int n, const DevBuf& w, const DevBuf& b, int K) {
+        int a, bnd;
+        if (!overlap(model_row0, model_row0 + n, a, bnd))
+            return;
+        GemmParams g;
+        g.M = bnd - a, g.N = d, g.K = K, g.lda = ld;
+        g.out = x + size_t(a - r0) * d, g.ldo = d, g.bias = b.as<float>();
+        const void* A0 = static_cast<const uint8_t*>(pk) + size_t(first_in + (a - model_row0)) * ld * 2;
+        gemm_bf16(A0, w.p, g, Epi::f32, s);
+        ++launches_;
+    };
+    proj(d_->pk_video.p, c_.video_patch, 0, T, C, d_->vp_w, d_->vp_b, c_.video_patch);           // keyframe rows
+    proj(d_->pk_audio.p, 64, 0, T + C, A, d_->ap_w, d_->ap_b, 64);                               // audio rows
+    proj(d_->pk_video.p, c_.video_patch, C, D, V - C, d_->vp_w, d_->vp_b, c_.video_patch);       // generated video
+    mark("input");
+    if (P == 1)
+        emit_probe("x0", -1, x, size_t(S_) * d);
+
+    // ---- blocks
+    const bool sparse = sparse_ratio_ > 0.f && d_->sp.blocks != nullptr;
+    CubeGrid grid;
+    grid.dense_rows = D, grid.frames = l.frames, grid.ph = l.h / 2, grid.pw = l.w / 2;
+    grid.nct = (grid.frames + 3) / 4, grid.ncy = (grid.ph + 3) / 4, grid.ncx = (grid.pw + 3) / 4;
+    const uint8_t* midx = d_->mod_idx.as<uint8_t>();
+    __nv_bfloat16* qkv = d_->qkv.as<__nv_bfloat16>();
+    for (int bl = 0; bl < L; ++bl) {
+        Impl::Block& B = d_->blocks[bl];
+        const float* mod = d_->mods.as<float>() + size_t(bl) * U * 18 * d;
+        // attention half
+        RmsModParams rp;
+        rp.x = x, rp.ldx = d, rp.rows = M, rp.d = d, rp.w = B.norm1.as<float>(), rp.mod = mod, rp.mod_idx = midx;
+        rp.mod_slots = 6, rp.shift_slot = 0, rp.scale_slot = 1, rp.eps = c_.eps;
+        GemmParams gq;
+        gq.M = M, gq.N = 3 * inner, gq.K = d;
+        gq.out = qkv, gq.bias = B.qkv_b.as<float>(), gq.rope = d_->rope.as<float>(), gq.qn_w = B.qn.as<float>(),
+        gq.kn_w = B.kn.as<float>(), gq.eps = c_.eps, gq.inner = inner, gq.heads_per_rank = Hp, gq.rows_local = M;
+        if (int8_ & kInt8Qkv) {
+            rp.out_kind = RowOut::s8, rp.out = d_->hq.p, rp.ldo = d, rp.out_scale = d_->hs.as<float>();
+            rms_mod_rows(rp, s);
+            mark("norm");
+            gq.a_scale = d_->hs.as<float>(), gq.b_scale = B.qkv_s.as<float>();
+            gemm_s8(d_->hq.p, B.qkv_q.p, gq, Epi::qkv, s);
+        } else {
+            rp.out_kind = RowOut::bf16, rp.out = d_->h.p, rp.ldo = d;
+            rms_mod_rows(rp, s);
+            mark("norm");
+            gemm_bf16(d_->h.p, B.qkv_w.p, gq, Epi::qkv, s);
+        }
+        launches_ += 2;
+        mark("qkv");
+        const __nv_bfloat16* qsrc = qkv;
+        if (P > 1) {
+            const size_t chunk = size_t(M) * 3 * Hp * 128;
+            H3_NCCL(ncclGroupStart());
+            for (int r = 0; r < P; ++r) {
+                H3_NCCL(ncclSend(qkv + r * chunk, chunk, ncclBfloat16, r, d_->comm, s));
+                H3_NCCL(ncclRecv(d_->qkv_recv.as<__nv_bfloat16>() + r * chunk, chunk, ncclBfloat16, r, d_->comm, s));
+            }
+            H3_NCCL(ncclGroupEnd());
+            qsrc = d_->qkv_recv.as<__nv_bfloat16>();
+            mark("a2a");
+        }
+        AttnParams ap;
+        ap.q = qsrc, ap.k = qsrc + Hp * 128, ap.v = qsrc + 2 * Hp * 128;
+        ap.row_stride = 3 * Hp * 128, ap.heads = Hp, ap.rows = S_;
+        ap.out = d_->o.p, ap.out_row_stride = Hp * 128;
+        if (sparse) {
+            // coarse pass (cube_pool, cube_scores, cube_topk, pass lists), then the sparse flash kernel
+            const SparseBuffers& b = d_->sp;
+            cube_pool(ap.q, ap.k, ap.row_stride, Hp, grid, b.mq, b.mk, s);
+            cube_scores(b.mq, b.mk, Hp, grid.cubes(), b.scores, s);
+            cube_topk(b.scores, Hp, grid, sparse_k(sparse_ratio_, grid.cubes()), sparse_local_, b.sel, b.nsel, b.kcap, s);
+            build_passes(b.sel, b.nsel, b.kcap, Hp, grid, b.blocks, b.nblocks, b.q_units, b.q_tiles, b.max_blocks, s);
+            mark("select");
+            ap.blocks = b.blocks, ap.nblocks = b.nblocks, ap.q_units = b.q_units, ap.q_tiles = b.q_tiles;
+            ap.max_blocks = b.max_blocks, ap.grid = grid;
+            attention(ap, s);
+            launches_ += 5;
+        } else {
+            attention(ap, s);
+            launches_ += 1;
+        }
+        mark("attn");
+        const void* oin = d_->o.p;
+        GemmParams go;
+        go.M = M, go.N = d, go.K = inner;
+        if (P > 1) {
+            const size_t chunk = size_t(M) * Hp * 128;
+            H3_NCCL(ncclGroupStart());
+            for (int r = 0; r < P; ++r) {
+                H3_NCCL(ncclSend(d_->o.as<__nv_bfloat16>() + r * chunk, chunk, ncclBfloat16, r, d_->comm, s));
+                H3_NCCL(ncclRecv(d_->o_recv.as<__nv_bfloat16>() + r * chunk, chunk, ncclBfloat16, r, d_->comm, s));
+            }
+            H3_NCCL(ncclGroupEnd());
+            oin = d_->o_recv.p;
+            go.a_chunks = P, go.lda = Hp * 128, go.a_rows_stride = M;
+            mark("a2a");
+        }
+        go.x = x, go.ldx = d, go.bias = B.out_b.as<float>(), go.mod = mod, go.mod_idx = midx, go.gate_slot = 2, go.dim = d;
+        if (int8_ & kInt8Out) {
+            if (P > 1)
+                throw CudaError("int8 out projection with sequence parallelism is not supported");
+            quant_rows_i8(oin, inner, M, inner, d_->hq.as<int8_t>(), d_->hs.as<float>(), s);
+            go.a_scale = d_->hs.as<float>(), go.b_scale = B.out_s.as<float>();
+            gemm_s8(d_->hq.p, B.out_q.p, go, Epi::gate_resid, s);
+            launches_ += 2;
+        } else {
+            gemm_bf16(oin, B.out_w.p, go, Epi::gate_resid, s);
+            launches_ += 1;
+        }
+        mark("out");
+        // FFN half
+        rp.w = B.norm2.as<float>(), rp.shift_slot = 3, rp.scale_slot = 4;
+        GemmParams g1;
+        g1.M = M, g1.N = 2 * F, g1.K = d, g1.out = qkv, g1.ldo = F, g1.bias = B.fc1_b.as<float>();
+        if (int8_ & kInt8Fc1) {
+            rp.out_kind = RowOut::s8, rp.out = d_->hq.p, rp.ldo = d, rp.out_scale = d_->hs.as<float>();
+            rms_mod_rows(rp, s);
+            mark("norm");
+            g1.a_scale = d_->hs.as<float>(), g1.b_scale = B.fc1_s.as<float>();
+            gemm_s8(d_->hq.p, B.fc1_q.p, g1, Epi::swiglu, s);
+        } else {
+            rp.out_kind = RowOut::bf16, rp.out = d_->h.p, rp.ldo = d;
+            rms_mod_rows(rp, s);
+            mark("norm");
+            gemm_bf16(d_->h.p, B.fc1_w.p, g1, Epi::swiglu, s);
+        }
+        launches_ += 2;
+        mark("fc1");
+        GemmParams g2;
+        g2.M = M, g2.N = d, g2.K = F;
+        g2.x = x, g2.ldx = d, g2.bias = B.fc2_b.as<float>(), g2.mod = mod, g2.mod_idx = midx, g2.gate_slot = 5, g2.dim = d;
+        if (int8_ & kInt8Fc2) {
+            quant_rows_i8(qkv, F, M, F, d_->hq.as<int8_t>(), d_->hs.as<float>(), s);
+            mark("quant");
+            g2.a_scale = d_->hs.as<float>(), g2.b_scale = B.fc2_s.as<float>();
+            gemm_s8(d_->hq.p, B.fc2_q.p, g2, Epi::gate_resid, s);
+            launches_ += 2;
+        } else {
+            gemm_bf16(qkv, B.fc2_w.p, g2, Epi::gate_resid, s);
+            launches_ += 1;
+        }
+        mark("fc2");
+        if (probe_ && P == 1)
+            emit_probe("block", bl, x, size_t(S_) * d);
+    }
+
+    // ---- final norm (per level shift and scale, no weight) and the heads
+    float* xn = reinterpret_cast<float*>(d_->qkv.p);
+    RmsModParams fp;
+    fp.x = x, fp.ldx = d, fp.rows = M, fp.d = d, fp.w = nullptr, fp.mod = d_->fmods.as<float>(), fp.mod_idx = d_->lvl_idx.as<uint8_t>();
+    fp.mod_slots = 2, fp.shift_slot = 0, fp.scale_slot = 1, fp.eps = c_.eps, fp.out_kind = RowOut::f32, fp.out = xn, fp.ldo = d;
+    rms_mod_rows(fp, s);
+    ++launches_;
+    if (P == 1)
+        emit_probe("norm_out", -1, xn, size_t(S_) * d);
+    float* ro = d_->rows_out.as<float>();
+    // rows_out: 128 floats a row (a video row's 96 values or an audio row's 32)
+    auto head = [&](int first, int n, const DevBuf& w, const DevBuf& b, int N) {
+        int a, bnd;
+        if (!overlap(first, first + n, a, bnd))
+            return;
+        heads_f32(xn + size_t(a - r0) * d, d, bnd - a, w.as<float>(), b.as<float>(), N, d, ro + size_t(a - r0) * 128, 128, s);
+        ++launches_;
+    };
+    head(T, C, d_->hv_w, d_->hv_b, c_.video_patch);
+    head(T + C, A, d_->ha_w, d_->ha_b, c_.audio_channels);
+    head(D, V - C, d_->hv_w, d_->hv_b, c_.video_patch);
+    const float* all = ro;
+    if (P > 1) {
+        H3_NCCL(ncclAllGather(ro, d_->rows_all.p, size_t(M) * 128, ncclFloat32, d_->comm, s));
+        all = d_->rows_all.as<float>();
+    }
+    mark("final");
+    // ---- outputs: video rows (keyframe rows first, then generated) and audio rows
+    const cudaMemcpyKind kind = device_io ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost;
+    if (C)
+        H3_CUDA(cudaMemcpy2DAsync(out_video, c_.video_patch * 4, all + size_t(T) * 128, 128 * 4, c_.video_patch * 4, C, kind, s));
+    if (V - C)
+        H3_CUDA(cudaMemcpy2DAsync(out_video + size_t(C) * c_.video_patch, c_.video_patch * 4, all + size_t(D) * 128, 128 * 4,
+                                  c_.video_patch * 4, V - C, kind, s));
+    if (A)
+        H3_CUDA(cudaMemcpy2DAsync(out_audio, c_.audio_channels * 4, all + size_t(T + C) * 128, 128 * 4, c_.audio_channels * 4, A, kind, s));
+    if (timing_) {
+        H3_CUDA(cudaStreamSynchronize(s));
+        for (size_t i = 1; i < ev_used; ++i)
+            H3_CUDA(cudaEventElapsedTime(&stage_ms_[i].second, d_->ev[i - 1], d_->ev[i]));
+    }
+    if (!device_io) {
+        H3_CUDA(cudaStreamSynchronize(s));
+        if (const uint32_t e = take_device_error(s))
+            throw CudaError("device error " + std::to_string(e) + " during the step (a bounded wait ran out)");
+    }
+}
+
+} // namespace h3

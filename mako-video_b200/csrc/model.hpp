@@ -1,0 +1,113 @@
+// The H3 transformer step on one B200 (or one rank of a sequence-parallel group): weights resident in HBM, the
+// packed sequence's layout, and the step that turns the noisy video and audio rows into their velocities.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <functional>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "attention.cuh"
+#include "sparse.cuh"
+
+namespace h3 {
+
+struct Config {
+    int dim = 5120, heads = 40, ffn = 13824, blocks = 48, time_dim = 2560;
+    int text_dim = 5120, video_patch = 96, audio_channels = 32;
+    float eps = 1e-6f;
+    int inner() const { return heads * 128; }
+};
+
+// The packed sequence [text | conditioning video | audio | generated video] of one request
+// (mirrors the reference's H3::Layout; references are not supported).
+struct Layout {
+    int text = 0;              // text rows T
+    int frames = 0, h = 0, w = 0; // generated video: latent frames and latent height / width (2x2 patches a row)
+    int audio = 0;             // audio latents per channel (rows = 2 * audio: left channel then right)
+    int cond_frames = 0;       // keyframe latent frames (each h/2 * w/2 rows at t = 0.999), ahead of the audio rows
+    std::vector<uint8_t> cond_last; // per keyframe: anchored at the last generated frame (else the first)
+    std::vector<uint8_t> text_tags; // per text row: modality tag (1 text, 0 video); empty: all text
+    int patch_rows() const { return (h / 2) * (w / 2); }
+    int video_rows() const { return (cond_frames + frames) * patch_rows(); } // conditioning + generated
+    int cond_rows() const { return cond_frames * patch_rows(); }
+    int audio_rows() const { return 2 * audio; }
+    int rows() const { return text + video_rows() + audio_rows(); }
+    int dense_rows() const { return text + cond_rows() + audio_rows(); }
+};
+
+// Per-row metadata of a layout (the reference's H3::rows): rotary positions (t, h, w) in double, modality tag
+// (0 video, 1 text, 2 audio) and role (0 text, 1 reference video, 2 reference audio, 3 audio, 4 video).
+struct Rows {
+    std::vector<double> pos; // [S][3]
+    std::vector<uint8_t> tags, roles;
+};
+Rows layout_rows(const Layout& l);
+
+// The rotary frequencies: 16 per axis, base 10000 (1 / 10000^(2i/32) in float).
+void rope_inv_freq(float out[16]);
+// Per-row (cos, sin) of the 48 rotary angles (16 per axis, angle = float(pos) * inv_freq in float).
+std::vector<float> rope_table(const Rows& r);
+
+struct World {
+    int rank = 0, size = 1;
+    uint8_t nccl_id[128] = {};
+};
+
+using Probe = std::function<void(const std::string& name, int layer, const float* data, size_t n)>;
+
+enum Int8Mask : uint32_t { kInt8Qkv = 1, kInt8Out = 2, kInt8Fc1 = 4, kInt8Fc2 = 8 };
+// "none", "all" or a comma list of qkv, out, fc1, fc2; false when the text is not one of these.
+bool parse_int8(const std::string& s, uint32_t& mask);
+
+class Model {
+public:
+    // Synthetic weights from `seed` (every value a hash of seed, tensor and index; see fill_synthetic).
+    Model(const Config& c, uint64_t seed, uint32_t int8_mask, const World& world);
+    ~Model();
+    Model(const Model&) = delete;
+    Model& operator=(const Model&) = delete;
+
+    void set_sparse(float ratio, int local);
+    void set_probe(Probe p) { probe_ = std::move(p); }
+    // Caches the text rows (condition_proj of the text embeddings [T][text_dim]) and the layout's row tables.
+    void begin(const float* text, int T, const Layout& l);
+    // One forward: video [V][96] and audio [A][32] rows (host or device memory) to velocities of the same shapes.
+    // With `device_io` the pointers are device pointers and the step stays on `stream` (no host synchronisation
+    // beyond the error check).
+    void step(const float* video, const float* audio, float t_video, float t_audio, float* out_video, float* out_audio,
+              bool device_io = false);
+
+    const Config& config() const { return c_; }
+    const Layout& layout() const { return layout_; }
+    int rows() const { return S_; }
+    cudaStream_t stream() const { return stream_; }
+    // Kernel launches of the last step (this library's kernels, counted at launch).
+    int last_launches() const { return launches_; }
+    // Device timings (ms) of the last step by stage when timing is on.
+    void set_timing(bool on) { timing_ = on; }
+    const std::vector<std::pair<std::string, float>>& last_timing() const { return stage_ms_; }
+
+private:
+    struct Impl;
+    std::unique_ptr<Impl> d_;
+    Config c_;
+    Layout layout_;
+    World world_;
+    int S_ = 0, S_local_ = 0, row0_ = 0;
+    uint32_t int8_ = 0;
+    float sparse_ratio_ = 0;
+    int sparse_local_ = 1;
+    Probe probe_;
+    cudaStream_t stream_ = nullptr;
+    int launches_ = 0;
+    bool timing_ = false;
+    std::vector<std::pair<std::string, float>> stage_ms_;
+    bool begun_ = false;
+    void alloc_activations();
+    void emit_probe(const char* name, int layer, const float* dev, size_t n);
+};
+
+} // namespace h3

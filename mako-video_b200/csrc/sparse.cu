@@ -1,0 +1,302 @@
+// The sparse attention's coarse pass (cube_pool, cube_scores, cube_topk) and its pass lists.
+#include "common.hpp"
+#include "ptx.cuh"
+#include "sparse.cuh"
+
+#include <algorithm>
+#include <cmath>
+
+namespace h3 {
+
+int sparse_k(float ratio, int cubes)
+{
+    const int k = int(std::ceil(double(ratio) * cubes - 1e-6));
+    return std::max(1, std::min(cubes, k));
+}
+
+int sparse_forced(int local) { return local <= 0 ? 0 : (local >= 3 ? 3 : 1); }
+
+void sparse_sizes(const CubeGrid& g, float ratio, int local, int& kcap, int& q_tiles, int& max_blocks)
+{
+    kcap = std::max(sparse_k(ratio, g.cubes()), sparse_forced(local));
+    kcap = std::min(kcap, g.cubes());
+    q_tiles = (g.cubes() + 1) / 2 + (g.dense_units() + 1) / 2;
+    max_blocks = (2 * kcap + g.dense_units() + 1) / 2;
+}
+
+namespace {
+
+__global__ void cube_pool_kernel(const __nv_bfloat16* q, const __nv_bfloat16* k, int64_t rs, CubeGrid g, float* mq, float* mk)
+{
+    const int c = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+    const int cx = c % g.ncx, cy = (c / g.ncx) % g.ncy, ct = c / (g.ncx * g.ncy);
+    float sq = 0.f, sk = 0.f;
+    int n = 0;
+    for (int kr = 0; kr < 64; ++kr) {
+        const int x = 4 * cx + (kr & 3), y = 4 * cy + ((kr >> 2) & 3), f = 4 * ct + (kr >> 4);
+        if (x >= g.pw || y >= g.ph || f >= g.frames)
+            continue;
+        const size_t row = size_t(g.dense_rows) + (size_t(f) * g.ph + y) * g.pw + x;
+        sq = __fadd_rn(sq, __bfloat162float(q[row * rs + h * 128 + d]));
+        sk = __fadd_rn(sk, __bfloat162float(k[row * rs + h * 128 + d]));
+        ++n;
+    }
+    const size_t o = (size_t(h) * g.cubes() + c) * 128 + d;
+    mq[o] = __fdiv_rn(sq, float(n));
+    mk[o] = __fdiv_rn(sk, float(n));
+}
+
+__global__ void __launch_bounds__(1024) cube_scores_kernel(const float* mq, const float* mk, int cubes, float* scores)
+{
+    __shared__ float A[32][128];
+    __shared__ float B[32][129];
+    const int h = blockIdx.z, i0 = blockIdx.y * 32, j0 = blockIdx.x * 32;
+    const int tj = threadIdx.x, ti = threadIdx.y;
+    const float* qa = mq + size_t(h) * cubes * 128;
+    const float* kb = mk + size_t(h) * cubes * 128;
+    for (int e = ti * 32 + tj; e < 32 * 128; e += 1024) {
+        const int r = e / 128, d = e % 128;
+        A[r][d] = i0 + r < cubes ? qa[size_t(i0 + r) * 128 + d] : 0.f;
+        B[r][d] = j0 + r < cubes ? kb[size_t(j0 + r) * 128 + d] : 0.f;
+    }
+    __syncthreads();
+    float acc = 0.f;
+#pragma unroll 8
+    for (int d = 0; d < 128; ++d)
+        acc = __fmaf_rn(A[ti][d], B[tj][d], acc);
+    if (i0 + ti < cubes && j0 + tj < cubes)
+        scores[(size_t(h) * cubes + i0 + ti) * cubes + j0 + tj] = acc;
+}
+
+__device__ __forceinline__ uint32_t orderable(float f)
+{
+    const uint32_t u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+constexpr int TK_NT = 256;
+
+// Block-wide exclusive prefix sum of one value per thread; returns the thread's offset, `total` gets the sum.
+__device__ __forceinline__ int block_exscan(int v, int* buf, int& total)
+{
+    buf[threadIdx.x] = v;
+    __syncthreads();
+    for (int o = 1; o < TK_NT; o <<= 1) {
+        const int t = threadIdx.x >= o ? buf[threadIdx.x - o] : 0;
+        __syncthreads();
+        buf[threadIdx.x] += t;
+        __syncthreads();
+    }
+    total = buf[TK_NT - 1];
+    const int ex = buf[threadIdx.x] - v;
+    __syncthreads();
+    return ex;
+}
+
+__global__ void __launch_bounds__(TK_NT) cube_topk_kernel(const float* scores, CubeGrid g, int k, int local, int32_t* sel, int32_t* nsel,
+                                                           int kcap)
+{
+    extern __shared__ uint32_t keys[]; // [cubes]
+    __shared__ int hist[256];
+    __shared__ int scan[TK_NT];
+    __shared__ int sh_digit, sh_acc;
+    const int n = g.cubes();
+    const int i = blockIdx.x, h = blockIdx.y;
+    const int cx = i % g.ncx, cy = (i / g.ncx) % g.ncy, ct = i / (g.ncx * g.ncy);
+    const int per_plane = g.ncx * g.ncy;
+    auto forced = [&](int j) {
+        if (local <= 0)
+            return false;
+        if (j == i)
+            return true;
+        return local >= 3 && ((ct > 0 && j == i - per_plane) || (ct + 1 < g.nct && j == i + per_plane));
+    };
+    int n_forced = local <= 0 ? 0 : 1 + (local >= 3 ? int(ct > 0) + int(ct + 1 < g.nct) : 0);
+    const float* row = scores + (size_t(h) * n + i) * n;
+    for (int j = threadIdx.x; j < n; j += TK_NT)
+        keys[j] = orderable(row[j]);
+    __syncthreads();
+    const int want = max(k, n_forced);
+    int remaining = want - n_forced; // to pick among the non-forced cubes
+    uint32_t prefix = 0, mask = 0;
+    if (remaining > 0) {
+        for (int shift = 24; shift >= 0; shift -= 8) {
+            hist[threadIdx.x] = 0;
+            __syncthreads();
+            for (int j = threadIdx.x; j < n; j += TK_NT)
+                if (!forced(j) && (keys[j] & mask) == prefix)
+                    atomicAdd(&hist[(keys[j] >> shift) & 255], 1);
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                int acc = 0, dg = 255;
+                for (; dg > 0; --dg) {
+                    if (acc + hist[dg] >= remaining)
+                        break;
+                    acc += hist[dg];
+                }
+                sh_digit = dg;
+                sh_acc = acc;
+            }
+            __syncthreads();
+            remaining -= sh_acc;
+            prefix |= uint32_t(sh_digit) << shift;
+            mask |= 255u << shift;
+            __syncthreads();
+        }
+    }
+    // Selected: forced; key above the threshold; or key equal to it among the first `remaining` such by index.
+    const int chunk = (n + TK_NT - 1) / TK_NT;
+    const int j0 = threadIdx.x * chunk, j1 = min(n, j0 + chunk);
+    const bool pick = want - n_forced > 0;
+    int ties = 0;
+    for (int j = j0; j < j1; ++j)
+        ties += pick && !forced(j) && keys[j] == prefix;
+    int total;
+    int tie_rank = block_exscan(ties, scan, total);
+    int count = 0;
+    for (int j = j0; j < j1; ++j) {
+        bool s = forced(j);
+        if (!s && pick) {
+            if (keys[j] > prefix)
+                s = true;
+            else if (keys[j] == prefix)
+                s = tie_rank++ < remaining;
+        }
+        count += s;
+    }
+    int out = block_exscan(count, scan, total);
+    tie_rank = block_exscan(ties, scan, total); // recompute for the write pass
+    int32_t* dst = sel + (size_t(h) * n + i) * kcap;
+    for (int j = j0; j < j1; ++j) {
+        bool s = forced(j);
+        if (!s && pick) {
+            if (keys[j] > prefix)
+                s = true;
+            else if (keys[j] == prefix)
+                s = tie_rank++ < remaining;
+        }
+        if (s && out < kcap)
+            dst[out++] = j;
+    }
+    if (threadIdx.x == 0)
+        nsel[size_t(h) * n + i] = min(want, kcap);
+}
+
+// One thread per (head, video query tile): merge the two cubes' selections, append the dense units, pair them.
+__global__ void build_passes_kernel(const int32_t* sel, const int32_t* nsel, int kcap, int heads, CubeGrid g, int4* blocks,
+                                    int32_t* nblocks, int2* q_units, int q_tiles, int max_blocks)
+{
+    const int nc = g.cubes(), nd = g.dense_units();
+    const int vt = (nc + 1) / 2;
+    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx < q_tiles) {
+        if (idx < vt)
+            q_units[idx] = make_int2(2 * idx, 2 * idx + 1 < nc ? 2 * idx + 1 : -1);
+        else {
+            const int t = idx - vt;
+            q_units[idx] = make_int2(nc + 2 * t, 2 * t + 1 < nd ? nc + 2 * t + 1 : -1);
+        }
+    }
+    if (idx >= heads * q_tiles)
+        return;
+    const int h = idx / q_tiles, t = idx % q_tiles;
+    if (t >= vt) {
+        nblocks[idx] = -1; // dense query rows attend every unit
+        return;
+    }
+    const int c0 = 2 * t, c1 = 2 * t + 1;
+    const int32_t* A = sel + (size_t(h) * nc + c0) * kcap;
+    const int na = nsel[size_t(h) * nc + c0];
+    const int32_t* B = c1 < nc ? sel + (size_t(h) * nc + c1) * kcap : nullptr;
+    const int nb = c1 < nc ? nsel[size_t(h) * nc + c1] : 0;
+    int4* out = blocks + size_t(idx) * max_blocks;
+    int ia = 0, ib = 0, nout = 0;
+    int pend_u = -1, pend_bits = 0; // a unit waiting for its pair partner
+    auto emit = [&](int u, int bits) {
+        if (pend_u < 0) {
+            pend_u = u, pend_bits = bits;
+        } else {
+            // keep bit (2 * qh + kh): unit a is kh 0, unit b is kh 1
+            const int keep = (pend_bits & 1) | ((bits & 1) << 1) | ((pend_bits & 2) << 1) | ((bits & 2) << 2);
+            if (nout < max_blocks)
+                out[nout] = make_int4(pend_u, u, keep, 0);
+            ++nout;
+            pend_u = -1;
+        }
+    };
+    while (ia < na || ib < nb) {
+        const int a = ia < na ? A[ia] : 0x7fffffff, b = ib < nb ? B[ib] : 0x7fffffff;
+        if (a == b) {
+            emit(a, 3), ++ia, ++ib;
+        } else if (a < b) {
+            emit(a, 1), ++ia;
+        } else {
+            emit(b, 2), ++ib;
+        }
+    }
+    for (int u = 0; u < nd; ++u)
+        emit(nc + u, 3);
+    if (pend_u >= 0) {
+        const int keep = (pend_bits & 1) | ((pend_bits & 2) << 1);
+        if (nout < max_blocks)
+            out[nout] = make_int4(pend_u, -1, keep, 0);
+        ++nout;
+    }
+    nblocks[idx] = min(nout, max_blocks);
+}
+
+} // namespace
+
+void cube_pool(const void* q, const void* k, int64_t rs, int heads, const CubeGrid& g, float* mq, float* mk, cudaStream_t s)
+{
+    cube_pool_kernel<<<dim3(g.cubes(), heads), 128, 0, s>>>(static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
+                                                            rs, g, mq, mk);
+    H3_CUDA(cudaGetLastError());
+}
+
+void cube_scores(const float* mq, const float* mk, int heads, int cubes, float* scores, cudaStream_t s)
+{
+    const dim3 grid((cubes + 31) / 32, (cubes + 31) / 32, heads);
+    cube_scores_kernel<<<grid, dim3(32, 32), 0, s>>>(mq, mk, cubes, scores);
+    H3_CUDA(cudaGetLastError());
+}
+
+void cube_topk(const float* scores, int heads, const CubeGrid& g, int k, int local, int32_t* sel, int32_t* nsel, int kcap, cudaStream_t s)
+{
+    const size_t smem = size_t(g.cubes()) * 4;
+    if (smem > 160 * 1024)
+        throw CudaError("cube_topk: too many cubes");
+    static bool attr = false;
+    if (!attr) {
+        H3_CUDA(cudaFuncSetAttribute(cube_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
+        attr = true;
+    }
+    cube_topk_kernel<<<dim3(g.cubes(), heads), TK_NT, smem, s>>>(scores, g, k, local, sel, nsel, kcap);
+    H3_CUDA(cudaGetLastError());
+}
+
+void build_passes(const int32_t* sel, const int32_t* nsel, int kcap, int heads, const CubeGrid& g, int4* blocks, int32_t* nblocks,
+                  int2* q_units, int q_tiles, int max_blocks, cudaStream_t s)
+{
+    const int n = std::max(heads * q_tiles, q_tiles);
+    build_passes_kernel<<<(n + 127) / 128, 128, 0, s>>>(sel, nsel, kcap, heads, g, blocks, nblocks, q_units, q_tiles, max_blocks);
+    H3_CUDA(cudaGetLastError());
+}
+
+void sparse_attention(const AttnParams& a, const CubeGrid& g, float ratio, int local, const SparseBuffers& b, cudaStream_t s)
+{
+    cube_pool(a.q, a.k, a.row_stride, a.heads, g, b.mq, b.mk, s);
+    cube_scores(b.mq, b.mk, a.heads, g.cubes(), b.scores, s);
+    cube_topk(b.scores, a.heads, g, sparse_k(ratio, g.cubes()), local, b.sel, b.nsel, b.kcap, s);
+    build_passes(b.sel, b.nsel, b.kcap, a.heads, g, b.blocks, b.nblocks, b.q_units, b.q_tiles, b.max_blocks, s);
+    AttnParams p = a;
+    p.blocks = b.blocks;
+    p.nblocks = b.nblocks;
+    p.q_units = b.q_units;
+    p.q_tiles = b.q_tiles;
+    p.max_blocks = b.max_blocks;
+    p.grid = g;
+    attention(p, s);
+}
+
+} // namespace h3

@@ -1,0 +1,207 @@
+"""CPU tests: the oracle against the reference's golden vectors, the oracle's exact sparse selection against a
+brute-force restatement, the library's host-side functions (layout rows, rotary table, int8 mask parsing, sparse
+sizes) against the oracle, and that the library exports every symbol include/h3_c.h declares. No GPU is used."""
+import ctypes
+import json
+import math
+import os
+import re
+
+import numpy as np
+import pytest
+import torch
+
+import h3b200
+from oracle import exact, h3_oracle as O
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+GOLDEN = os.path.join(REPO, "tests", "golden")
+
+
+# ------------------------------------------------------------------------------------ oracle vs golden vectors
+
+def test_time_embedding_and_adaln_match_reference_formula():
+    """tools/check_pruned_curve.py:58-67 (executed from the reference file) vs the oracle's time MLP + AdaLN."""
+    g = np.load(os.path.join(GOLDEN, "time_adaln.npz"))
+    w = {"t_in_w": torch.from_numpy(g["p_in_w"]).float(), "t_in_b": torch.from_numpy(g["p_in_b"]).float(),
+         "t_out_w": torch.from_numpy(g["p_out_w"]).float(), "t_out_b": torch.from_numpy(g["p_out_b"]).float()}
+    temb, s = O.time_embedding([float(t) for t in g["t"]], w)
+    rel = np.linalg.norm(temb.numpy() - g["temb"]) / np.linalg.norm(g["temb"])
+    assert rel < 1e-5, rel
+    # AdaLN: the reference's mods_full has no bf16 rounding of silu(temb); the oracle applies it (dump_h3_ref.py:150)
+    silu = torch.nn.functional.silu(temb)
+    mods = silu @ torch.from_numpy(g["Wf"]).float().T + torch.from_numpy(g["bf"]).float()
+    rel = np.linalg.norm(mods.numpy() - g["mods"]) / np.linalg.norm(g["mods"])
+    assert rel < 1e-5, rel
+    mods_r = s @ torch.from_numpy(g["Wf"]).float().T + torch.from_numpy(g["bf"]).float()
+    rel_r = np.linalg.norm(mods_r.numpy() - g["mods"]) / np.linalg.norm(g["mods"])
+    assert rel_r < 1e-2, rel_r  # bf16 rounding of the projection input only
+
+
+def test_rope_frequencies_match_reference_expression():
+    """tools/dump_h3_ref.py:140-141 evaluated from the reference file, bit for bit."""
+    want = np.load(os.path.join(GOLDEN, "rope_freq.npy"))
+    assert want.shape == (16,)
+    np.testing.assert_array_equal(O.rope_inv_freq(), want)
+
+
+def test_geometry_known_answers_are_consistent():
+    """tests/geometry_test.cpp:22-27: the latent-frame and audio-latent counts the layouts are built from."""
+    g = json.load(open(os.path.join(GOLDEN, "geometry.json")))
+    for f, lf in g["latent_frames"]:
+        assert (f - 5) // 17 * 5 + 2 == lf
+    for f, a in g["audio_latents"]:
+        assert round(f / 24 * 40) == a
+
+
+def test_synthetic_values_are_deterministic_and_normal_like():
+    a = O.synthetic(200000, 0, 7, 0.0, 0.02)
+    b = O.synthetic(200000, 0, 7, 0.0, 0.02)
+    np.testing.assert_array_equal(a, b)
+    assert abs(a.mean()) < 2e-4 and abs(a.std() - 0.02) < 2e-4
+    c = O.synthetic(1000, 1, 7)
+    assert not np.array_equal(a[:1000], c)
+    bf = O.synthetic(1000, 0, 7, bf16=True)
+    assert (bf.view(np.uint32) & 0xFFFF).max() == 0
+
+
+def test_bf16_round_half_even():
+    x = np.array([1.0, 1.00390625, 1.01171875, -2.5, 3.0e-39], np.float32)  # exact halves at bf16 spacing 2^-7
+    r = O.bf16_round(x)
+    assert r[0] == 1.0 and r[1] == 1.0 and r[2] == 1.015625 and r[3] == -2.5
+
+
+def test_diff_metric_matches_reference_definition():
+    got = np.array([[1.0, 0.0], [0.0, 2.0]])
+    want = np.array([[1.0, 0.0], [0.0, 1.0]])
+    rel, cos = O.diff(got, want, 2)
+    assert abs(rel - math.sqrt(1 / 2)) < 1e-12 and abs(cos - 1.0) < 1e-12
+
+
+# --------------------------------------------------------------------------- exact sparse selection (oracle)
+
+def brute_topk(scores, frames, ph, pw, ratio, local):
+    nct, ncy, ncx = (frames + 3) // 4, (ph + 3) // 4, (pw + 3) // 4
+    nc = nct * ncy * ncx
+    k = exact.sparse_k(ratio, nc)
+    out = []
+    for h in range(scores.shape[0]):
+        rows = []
+        for i in range(nc):
+            ct = i // (ncx * ncy)
+            forced = set()
+            if local > 0:
+                forced.add(i)
+            if local >= 3:
+                if ct > 0:
+                    forced.add(i - ncx * ncy)
+                if ct + 1 < nct:
+                    forced.add(i + ncx * ncy)
+            rest = sorted((j for j in range(nc) if j not in forced), key=lambda j: (-scores[h, i, j], j))
+            want = max(k, len(forced))
+            rows.append(sorted(list(forced) + rest[:want - len(forced)]))
+        out.append(rows)
+    return out
+
+
+@pytest.mark.parametrize("ratio,local", [(0.1, 1), (0.25, 3), (0.5, 0), (1.0, 0), (0.01, 3)])
+def test_exact_topk_matches_brute_force_with_ties(ratio, local):
+    rng = np.random.default_rng(3)
+    frames, ph, pw = 9, 6, 10
+    nc = 3 * 2 * 3
+    # quantised scores: many exact ties, which go to the lower cube index
+    scores = (rng.integers(-4, 5, size=(2, nc, nc)) * 0.25).astype(np.float32)
+    sel, nsel = exact.cube_topk(scores, frames, ph, pw, ratio, local)
+    want = brute_topk(scores, frames, ph, pw, ratio, local)
+    for h in range(2):
+        for i in range(nc):
+            assert list(sel[h, i, :nsel[h, i]]) == want[h][i]
+
+
+def test_exact_pool_means_over_valid_rows_only():
+    frames, ph, pw, D, H = 5, 6, 7, 11, 2
+    S = D + frames * ph * pw
+    rng = np.random.default_rng(0)
+    q = O.bf16_round(rng.standard_normal((S, H, 128)).astype(np.float32))
+    k = O.bf16_round(rng.standard_normal((S, H, 128)).astype(np.float32))
+    bits = lambda a: (a.view(np.uint32) >> 16).astype(np.uint16).reshape(-1)
+    mq, mk = exact.cube_pool(bits(q), bits(k), H * 128, H, D, frames, ph, pw)
+    vid = q[D:].reshape(frames, ph, pw, H, 128)
+    # cube (1, 1, 1): frames 4.., rows 4..5, cols 4..6 (padding beyond the grid)
+    ncx, ncy = 2, 2
+    c = (1 * ncy + 1) * ncx + 1
+    ref = vid[4:8, 4:8, 4:8].reshape(-1, H, 128).astype(np.float64).mean(0)
+    assert np.allclose(mq[:, c], ref.T.T, atol=1e-5)
+    scores = exact.cube_scores(mq, mk)
+    assert np.allclose(scores[0, 3, 5], float(np.dot(mq[0, 3].astype(np.float64), mk[0, 5])), rtol=1e-5)
+
+
+# -------------------------------------------------------------------------------- library host-side functions
+
+def test_library_exports_every_declared_symbol():
+    header = open(os.path.join(REPO, "include", "h3_c.h")).read()
+    declared = set(re.findall(r"^\s*(?:const\s+)?[\w\s\*]+?\b(h3k?_\w+)\(", header, re.M))
+    declared -= {"h3_c"}
+    L = h3b200.lib()
+    for name in sorted(declared):
+        assert hasattr(L, name), name
+    assert declared <= set(h3b200.SIGNATURES), sorted(declared - set(h3b200.SIGNATURES))
+
+
+@pytest.mark.parametrize("name", ["c1", "c2", "c5"])
+def test_layout_rows_match_oracle(name):
+    lay = h3b200.Layout.named(name)
+    pos, tags, roles = h3b200.rows(lay)
+    p2, t2, r2 = O.layout_rows(dict(h3b200.LAYOUTS[name]))
+    np.testing.assert_array_equal(pos, p2)
+    np.testing.assert_array_equal(tags, t2)
+    np.testing.assert_array_equal(roles, r2)
+    assert pos.shape[0] == lay.rows
+
+
+def test_layout_with_keyframes_and_tags():
+    tags = np.array([1, 1, 0, 0, 1], np.uint8)
+    lay = h3b200.Layout(text=5, frames=6, h=8, w=12, audio=3, cond_frames=2, cond_last=[0, 1], text_tags=tags)
+    pos, t, r = h3b200.rows(lay)
+    d = dict(text=5, frames=6, h=8, w=12, audio=3, cond_frames=2, cond_last=[0, 1], text_tags=list(tags))
+    p2, t2, r2 = O.layout_rows(d)
+    np.testing.assert_array_equal(pos, p2)
+    np.testing.assert_array_equal(t, t2)
+    np.testing.assert_array_equal(r, r2)
+    assert list(r[:5]) == [0] * 5 and (r[5:5 + 2 * 24] == 1).all()
+
+
+def test_rope_table_matches_oracle():
+    lay = h3b200.Layout.named("c1")
+    got = h3b200.rope_table(lay)
+    pos, _, _ = O.layout_rows(dict(h3b200.LAYOUTS["c1"]))
+    np.testing.assert_array_equal(got, O.rope_table(pos))
+
+
+def test_parse_int8():
+    L = h3b200.lib()
+    m = ctypes.c_uint32()
+    for text, want in [("none", 0), ("all", 15), ("qkv", 1), ("out,fc2", 10), ("fc1,qkv", 5)]:
+        assert L.h3_parse_int8(text.encode(), ctypes.byref(m)) == 0 and m.value == want
+    assert L.h3_parse_int8(b"qkv,bogus", ctypes.byref(m)) == h3b200.H3_ERR_ARG
+    assert b"comma list" in L.h3_last_error()
+
+
+def test_sparse_sizes_for_768p():
+    g = h3b200.h3k_cube_grid(768, 32, 24, 42)
+    cubes, kcap, qt, mb = (ctypes.c_int32() for _ in range(4))
+    h3b200.check(h3b200.lib().h3k_sparse_sizes(ctypes.byref(g), 0.1, 1, ctypes.byref(cubes), ctypes.byref(kcap),
+                                                ctypes.byref(qt), ctypes.byref(mb)))
+    assert cubes.value == 8 * 6 * 11 == 528  # the grid padded to multiples of 4 (architecture.md:122-124)
+    assert kcap.value == 53                  # ceil(0.1 * 528)
+    assert qt.value == 264 + 6               # cube pairs + dense-unit pairs
+    assert exact.sparse_k(0.1, 528) == 53
+
+
+def test_create_refuses_checkpoint_paths_without_touching_the_gpu():
+    L = h3b200.lib()
+    cfg = h3b200.make_config("c1")
+    h = ctypes.c_void_p()
+    rc = L.h3_create(ctypes.byref(cfg), b"/models/minimax-h3/FL2VA/transformer", 0, 0.0, 1, None, 0, ctypes.byref(h))
+    assert rc == h3b200.H3_ERR_ARG and not h.value
+    assert b"synthetic" in L.h3_last_error()

@@ -1,0 +1,115 @@
+"""The whole step through the C ABI (h3_create / h3_begin / h3_step) against the CPU oracle on the same synthetic
+weights and inputs, probe by probe as the reference's harness compares the Diffusers tensors
+(tests/h3_ref_test.cpp:214-250): time embedding, block-0 modulation, packed input, blocks, final norm, velocities."""
+import numpy as np
+import pytest
+
+import h3b200 as H
+from oracle import h3_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+# tests/h3_ref_test.cpp:228-249
+TOL = {"temb": 1e-4, "mod0": 5e-3, "x0": 5e-3, "block": 1e-2, "norm_out": 6e-2}
+# north star: bf16 path vs the fp32 oracle
+VEL_REL, VEL_COS = 1e-2, 0.999
+
+
+def inputs(layout, cfg, seed=11):
+    lay = H.Layout(**layout)
+    text = O.synthetic(layout["text"] * cfg["text_dim"], seed, 1, 0.0, 1.0).reshape(layout["text"], cfg["text_dim"])
+    video = O.synthetic(lay.video_rows * 96, seed, 2, 0.0, 1.0).reshape(lay.video_rows, 96)
+    audio = O.synthetic(lay.audio_rows * 32, seed, 3, 0.0, 1.0).reshape(lay.audio_rows, 32)
+    return lay, text, video, audio
+
+
+def run_both(cfg, layout, t_video, t_audio, int8=0, sparse=0.0, local=1, seed=0):
+    lay, text, video, audio = inputs(layout, cfg)
+    m = H.Model(cfg, seed=seed, int8_mask=int8, sparse_ratio=sparse, sparse_local=local)
+    got = {}
+    m.set_probe(lambda name, layer, a: got.__setitem__(name if layer < 0 else f"{name}{layer}", a))
+    m.begin(text, lay)
+    gv, ga = m.step(video, audio, t_video, t_audio)
+    launches = m.last_launches()
+    m.close()
+    w = O.make_weights(cfg, seed)
+    want = {}
+    ov, oa = O.step(cfg, w, layout, text, video, audio, t_video, t_audio, int8=int8,
+                    probes=lambda n, l, a: want.__setitem__(n if l < 0 else f"{n}{l}", a))
+    return got, want, (gv, ga), (ov, oa), launches
+
+
+def check_probes(got, want, d, blocks, tol_scale=1.0):
+    for name, tol in TOL.items():
+        keys = [f"block{l}" for l in range(blocks)] if name == "block" else [name]
+        for k in keys:
+            width = d if k != "temb" else want[k].size // max(1, want[k].shape[0] if want[k].ndim > 1 else 1)
+            g = got[k].reshape(want[k].shape)
+            rel, cos = O.diff(g, want[k], want[k].shape[-1] if want[k].ndim > 1 else want[k].size)
+            assert rel < tol * tol_scale, (k, rel, cos)
+
+
+def test_step_c1_matches_oracle(cuda):
+    """one d=1024 block, 8 heads, SwiGLU 2816, 512 video + 64 text rows, t = 0.5."""
+    cfg = H.CONFIGS["c1"]
+    got, want, (gv, ga), (ov, oa), launches = run_both(cfg, H.LAYOUTS["c1"], 0.5, 0.5)
+    check_probes(got, want, cfg["dim"], cfg["blocks"])
+    rel, cos = O.diff(gv, ov, 96)
+    assert rel < VEL_REL and cos > VEL_COS, (rel, cos)
+    assert launches > 5
+
+
+MINI = dict(dim=512, heads=4, ffn=1280, blocks=3, time_dim=256, text_dim=512)
+MINI_LAYOUT = dict(text=40, frames=6, h=12, w=14, audio=24, cond_frames=1, cond_last=[1])
+
+
+def test_step_with_audio_keyframes_and_three_levels(cuda):
+    """Three noise levels in one forward (video/text, audio, keyframe rows at 0.999), three modalities."""
+    got, want, (gv, ga), (ov, oa), _ = run_both(MINI, MINI_LAYOUT, 0.7, 0.4)
+    check_probes(got, want, MINI["dim"], MINI["blocks"])
+    for g, o, wdt in ((gv, ov, 96), (ga, oa, 32)):
+        rel, cos = O.diff(g, o, wdt)
+        assert rel < VEL_REL and cos > VEL_COS, (rel, cos)
+
+
+def test_step_sparse_every_cube_equals_dense(cuda):
+    """--sparse 1.0 --sparse-local 0: every cube selected, so the sparse path must give the dense model's velocities
+    (the reference's h3_dit_sparse_all, tests/CMakeLists.txt:9-12)."""
+    lay = dict(text=40, frames=9, h=12, w=18, audio=16)
+    _, _, (gv, ga), (ov, oa), _ = run_both(MINI, lay, 0.6, 0.6, sparse=1.0, local=0)
+    rel, cos = O.diff(gv, ov, 96)
+    assert rel < VEL_REL and cos > VEL_COS, (rel, cos)
+
+
+def test_step_int8_all_matches_int8_oracle(cuda):
+    """--int8 all: the W8A8 path against the oracle's int8 dequant path (the integer products are exact; the
+    activations' int8 roundings can differ where fp32 paths differ by an ulp, hence a tolerance)."""
+    _, _, (gv, ga), (ov, oa), _ = run_both(MINI, MINI_LAYOUT, 0.7, 0.4, int8=15)
+    rel, cos = O.diff(gv, ov, 96)
+    assert rel < 2e-2 and cos > 0.998, (rel, cos)
+
+
+def test_step_is_deterministic_and_reuses_begin(cuda):
+    lay, text, video, audio = inputs(MINI_LAYOUT, MINI)
+    m = H.Model(MINI, seed=4)
+    m.begin(text, lay)
+    a = m.step(video, audio, 0.7, 0.4)
+    b = m.step(video, audio, 0.7, 0.4)
+    c = m.step(video, audio, 0.2, 0.1)
+    m.close()
+    np.testing.assert_array_equal(a[0], b[0])
+    np.testing.assert_array_equal(a[1], b[1])
+    assert not np.array_equal(a[0], c[0])
+
+
+def test_step_errors(cuda):
+    m = H.Model(MINI, seed=4)
+    lay, text, video, audio = inputs(MINI_LAYOUT, MINI)
+    with pytest.raises(H.H3Error) as e:
+        m.step(video, audio, 0.5, 0.5)
+    assert e.value.code in (H.H3_ERR_STATE, H.H3_ERR_ARG, H.H3_ERR_CUDA)
+    m.begin(text, lay)
+    with pytest.raises(H.H3Error) as e:
+        m.step(video[:-1], audio, 0.5, 0.5)
+    assert e.value.code == H.H3_ERR_ARG
+    m.close()
