@@ -1,0 +1,148 @@
+// Drop-in for mako-common's models/h3.hpp: the class mako::models::H3 that jhanssen/mako-video's sampler uses
+// (src/video/engine.hpp:22 `using H3 = models::H3;`), with the member signatures its call sites need
+// (src/video/engine.cpp:105-117, 666-676, 700, 714; tests/h3_ref_test.cpp:194, 215-224, 484-502), implemented over
+// the C ABI of libh3b200.so (include/h3_c.h). Header-only; link with -lh3b200. Failures throw std::runtime_error, as
+// the reference does.
+#pragma once
+
+#include "../h3_c.h"
+
+#include <cstdint>
+#include <functional>
+#include <optional>
+#include <span>
+#include <stdexcept>
+#include <string>
+#include <string_view>
+#include <vector>
+
+namespace mako::models {
+
+class H3 {
+public:
+    // Widths of the rows the step reads and writes (H3::kText, kVideoPatch, kAudioChannels).
+    static constexpr uint32_t kText = 5120, kVideoPatch = 96, kAudioChannels = 32;
+    static constexpr uint8_t kVideoTag = 0, kTextTag = 1, kAudioTag = 2;
+    // MiniMax-H3's shape (docs/architecture.md:23-27, 47-67).
+    static constexpr uint32_t kDim = 5376, kTimeDim = 2688;
+
+    enum Int8 : uint32_t { qkv = 1, out = 2, fc1 = 4, fc2 = 8 };
+
+    struct Layout {
+        uint32_t text = 0, frames = 0, h = 0, w = 0, audio = 0, cond_frames = 0;
+        std::vector<uint8_t> cond_last; // per keyframe: anchored at the last generated frame
+        std::vector<uint8_t> text_tags; // per text row: 1 text, 0 video (a vision block's rows)
+        uint32_t patch_rows() const { return (h / 2) * (w / 2); }
+        uint32_t cond_rows() const { return cond_frames * patch_rows(); }
+        uint32_t video_rows() const { return (cond_frames + frames) * patch_rows(); }
+        uint32_t audio_rows() const { return 2 * audio; }
+        uint32_t cond_audio_rows() const { return 0; } // references are not supported
+        uint32_t rows() const { return text + video_rows() + audio_rows(); }
+        h3_layout c() const
+        {
+            return h3_layout{text, frames, h, w, audio, cond_frames, cond_last.empty() ? nullptr : cond_last.data(),
+                             text_tags.empty() ? nullptr : text_tags.data()};
+        }
+    };
+
+    struct Rows {
+        std::vector<double> pos; // [S][3]: t, h, w
+        std::vector<uint8_t> tags, roles;
+    };
+
+    struct Velocities {
+        std::vector<float> video, audio;
+    };
+
+    using ProbeFn = std::function<void(const std::string& name, int layer, const float* data, size_t n)>;
+
+    // H3(path, ctx, telemetry, int8) (src/video/engine.cpp:109-110). `path` is "synthetic:SEED" (random-init weights);
+    // a checkpoint directory is refused (the safetensors loader is not built). The context and telemetry arguments
+    // of mako-common's runtime are accepted and unused: the GPU is the current CUDA device.
+    template <class Context, class Telemetry>
+    H3(const std::string& path, Context&, Telemetry, uint32_t int8, h3_config cfg = h3_mini_h3(), const h3_world* world = nullptr,
+       int device = 0)
+    {
+        check(h3_create(&cfg, path.c_str(), int8, 0.0f, 1, world, device, &m_));
+    }
+    explicit H3(const std::string& path, uint32_t int8 = 0, h3_config cfg = h3_mini_h3(), const h3_world* world = nullptr, int device = 0)
+    {
+        check(h3_create(&cfg, path.c_str(), int8, 0.0f, 1, world, device, &m_));
+    }
+    ~H3() { h3_destroy(m_); }
+    H3(const H3&) = delete;
+    H3& operator=(const H3&) = delete;
+
+    // MiniMax-H3's shape.
+    static h3_config h3_mini_h3() { return h3_config{kDim, 56, 14336, 50, kTimeDim, kText, kVideoPatch, kAudioChannels, 1e-6f}; }
+
+    // set_sparse(ratio, local) (src/video/engine.cpp:112).
+    void set_sparse(float ratio, uint32_t local) { check(h3_set_sparse(m_, ratio, local)); }
+    // add_lora (src/video/engine.cpp:114): merging adapters is a load-time step that is not built.
+    void add_lora(const std::string&, float, bool) { throw std::runtime_error("H3::add_lora: LoRA merging is not built"); }
+
+    // begin(text [T][5120], layout) (src/video/engine.cpp:700).
+    void begin(std::span<const float> text, const Layout& l)
+    {
+        const h3_layout c = l.c();
+        check(h3_begin(m_, text.data(), uint32_t(text.size() / kText), &c));
+        layout_ = l;
+    }
+
+    // step(video [V][96], audio [A][32], t_video, t_audio) (src/video/engine.cpp:714).
+    Velocities step(std::span<const float> video, std::span<const float> audio, float t_video, float t_audio)
+    {
+        Velocities v;
+        v.video.resize(video.size());
+        v.audio.resize(audio.size());
+        check(h3_step(m_, video.data(), video.size() / kVideoPatch, audio.data(), audio.size() / kAudioChannels, t_video, t_audio,
+                      v.video.data(), v.audio.data()));
+        return v;
+    }
+
+    // set_probe (tests/h3_ref_test.cpp:215-217): temb, mod0, x0, block (layer), norm_out.
+    void set_probe(ProbeFn fn)
+    {
+        probe_ = std::move(fn);
+        check(h3_set_probe(m_, probe_ ? &H3::probe_thunk : nullptr, this));
+    }
+
+    // H3::rows(layout) (tests/h3_ref_test.cpp:484-502).
+    static Rows rows(const Layout& l)
+    {
+        const h3_layout c = l.c();
+        const uint64_t S = h3_layout_rows(&c);
+        Rows r;
+        r.pos.resize(S * 3);
+        r.tags.resize(S);
+        r.roles.resize(S);
+        check(h3_rows(&c, r.pos.data(), r.tags.data(), r.roles.data()));
+        return r;
+    }
+
+    // parse_int8 (tools/mako_video.cpp:108-114).
+    static std::optional<uint32_t> parse_int8(std::string_view s)
+    {
+        uint32_t m = 0;
+        if (h3_parse_int8(std::string(s).c_str(), &m) != H3_OK)
+            return std::nullopt;
+        return m;
+    }
+
+private:
+    h3_model* m_ = nullptr;
+    Layout layout_;
+    ProbeFn probe_;
+
+    static void check(int rc)
+    {
+        if (rc != H3_OK)
+            throw std::runtime_error(h3_last_error());
+    }
+    static void probe_thunk(void* user, const char* name, int32_t layer, const float* data, uint64_t n)
+    {
+        static_cast<H3*>(user)->probe_(name, layer, data, n);
+    }
+};
+
+} // namespace mako::models
