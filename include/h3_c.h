@@ -190,6 +190,16 @@ int h3k_cube_topk(const float* scores, int32_t heads, const h3k_cube_grid* g, fl
 int h3k_sparse_attention(const void* q, const void* k, const void* v, int64_t row_stride, int32_t heads, const h3k_cube_grid* g,
                          float ratio, int32_t local, void* out, int64_t out_row_stride, void* stream);
 
+/* The same sparse attention without any device allocation (no counterpart in the reference, whose Metal runtime
+ * owns its buffers). For callers that cannot call cudaMalloc around an attention call: a serving stack that has
+ * reserved nearly all device memory for its own pool, or one whose other streams must not stall on the device-wide
+ * synchronisation of cudaMalloc / cudaFree. The scratch is a fixed 16 MiB array inside the library, held by every GPU
+ * that loads it until the process exits; a grid and head count that need more return H3_ERR_ARG with the sizes.
+ * Every call shares that array: calls whose work overlaps on the GPU race. The first call on a device looks up the
+ * array's device address; make it before any stream capture. Queued on `stream`, not waited for (h3k_check). */
+int h3k_sparse_attention_noalloc(const void* q, const void* k, const void* v, int64_t row_stride, int32_t heads,
+                                 const h3k_cube_grid* g, float ratio, int32_t local, void* out, int64_t out_row_stride, void* stream);
+
 /* Synthetic parameters as the model makes them (value = mean + std * IH4(seed, tensor_id, i)). */
 int h3k_fill_synthetic(void* dst, int32_t is_bf16, uint64_t n, uint64_t seed, uint32_t tensor_id, float mean, float stdev, void* stream);
 

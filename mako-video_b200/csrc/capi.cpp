@@ -119,6 +119,11 @@ struct Scratch {
 
 } // namespace
 
+namespace h3 {
+// For entry points defined in other translation units (noalloc.cu): sets what h3_last_error() returns.
+void set_last_error(const std::string& msg) { g_error = msg; }
+} // namespace h3
+
 extern "C" {
 
 const char* h3_last_error(void) { return g_error.c_str(); }
