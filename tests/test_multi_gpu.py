@@ -1,0 +1,65 @@
+"""Sequence-parallel (Ulysses) step on 2 GPUs, one process per GPU over NCCL: every rank must return the velocities the
+single-GPU step returns (the same kernels see the same rows and keys; only the rows' placement differs). Skipped
+with fewer than two GPUs."""
+import os
+import sys
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+CFG = dict(dim=512, heads=4, ffn=1280, blocks=2, time_dim=256, text_dim=512)
+LAYOUT = dict(text=40, frames=6, h=12, w=14, audio=24, cond_frames=1, cond_last=[1])
+
+
+def _inputs():
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "mako-video_b200"))
+    import h3b200 as H
+    lay = H.Layout(**LAYOUT)
+    rng = np.random.default_rng(5)
+    text = rng.standard_normal((LAYOUT["text"], CFG["text_dim"]), dtype=np.float32)
+    video = rng.standard_normal((lay.video_rows, 96), dtype=np.float32)
+    audio = rng.standard_normal((lay.audio_rows, 32), dtype=np.float32)
+    return H, lay, text, video, audio
+
+
+def _rank(rank, world, nccl_id, sparse, q):
+    H, lay, text, video, audio = _inputs()
+    torch.cuda.set_device(rank)
+    m = H.Model(CFG, seed=1, rank=rank, world=world, nccl_id=nccl_id, device=rank, sparse_ratio=sparse, sparse_local=1)
+    m.begin(text, lay)
+    v, a = m.step(video, audio, 0.7, 0.4)
+    v2, a2 = m.step(video, audio, 0.3, 0.2)
+    m.close()
+    q.put((rank, v, a, v2, a2))
+
+
+@pytest.mark.parametrize("sparse", [0.0, 0.5])
+def test_two_rank_step_matches_one_rank(cuda, sparse):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    H, *_ = _inputs()
+    nccl_id = H.nccl_unique_id()
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank, args=(r, 2, nccl_id, sparse, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(2):
+        r = q.get(timeout=300)
+        res[r[0]] = r[1:]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    one = ctx.Process(target=_rank, args=(0, 1, None, sparse, q))
+    one.start()
+    ref = q.get(timeout=300)[1:]
+    one.join(timeout=120)
+    for rank in (0, 1):
+        for got, want in zip(res[rank], ref):
+            rel = np.linalg.norm(got - want) / max(np.linalg.norm(want), 1e-30)
+            assert rel < 1e-5, (rank, rel)
