@@ -353,6 +353,239 @@ __global__ void __launch_bounds__(NT, 1) attn_kernel(const __grid_constant__ Map
     }
 }
 
+// ------------------------------------------------------------------------------------------------------------
+// Dense attention, two query tiles per CTA (256 query rows of one head) sharing every K/V tile.
+//   warp 0      TMA: Q0 and Q1 once, then K_j and V_j (2-stage ring each)
+//   warp 1      MMA, in the order S0(0) S1(0) | PV0(j) S0(j+1) PV1(j) S1(j+1) | ...: while one tile's softmax runs
+//               the tensor core works on the other tile
+//   warps 2..5  softmax of tile 0, warps 6..9 softmax of tile 1 (thread = query row)
+// TMEM (512 columns): S0 | S1 | O0 | O1, 128 each. P_t (bf16, two per column) is written back over the first 64
+// columns of S_t and the PV MMA reads it from TMEM (A operand in TMEM), so P never touches shared memory. The
+// tensor core executes one thread's MMAs in issue order, so S_t(j+1) overwrites P_t(j) only after PV_t(j) read it;
+// and s_full_t(j) tracks every earlier MMA, so once S_t(j) is complete, PV_t(j-1) is too and the softmax may write
+// P_t(j) and rescale O_t.
+constexpr int NT2 = 320;
+constexpr int A2_OFF_Q = 0;        // Q0, Q1
+constexpr int A2_OFF_K = 2 * TILE; // 2 stages
+constexpr int A2_OFF_V = 4 * TILE; // 2 stages
+constexpr int A2_OFF_BAR = 6 * TILE;
+constexpr int A2_SMEM = 6 * TILE + 256 + 1024;
+
+__global__ void __launch_bounds__(NT2, 1) attn2_kernel(const __grid_constant__ Maps maps, const AttnParams p)
+{
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    uint8_t* smem = smem_raw + (((raw + 1023) & ~1023u) - raw);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + A2_OFF_BAR);
+    uint64_t* q_full = bars + 0;
+    uint64_t* k_full = bars + 1;   // [2]
+    uint64_t* v_full = bars + 3;   // [2]
+    uint64_t* kv_empty = bars + 5; // [2]
+    uint64_t* s_full = bars + 7;   // [2] per tile
+    uint64_t* p_full = bars + 9;   // [2] per tile
+    uint64_t* pv_done = bars + 11; // [2] per tile
+    uint64_t* drain = bars + 13;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+
+    const int warp = warp_id();
+    const int pair = blockIdx.x, head = blockIdx.y;
+    const int nkv = (p.rows + 127) / 128;
+    const CubeGrid& g = p.grid;
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&k_full[i], 1);
+            mbar_init(&v_full[i], 1);
+            mbar_init(&kv_empty[i], 1);
+            mbar_init(&s_full[i], 1);
+            mbar_init(&p_full[i], 4);
+            mbar_init(&pv_done[i], 1);
+        }
+        mbar_init(drain, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0 && elect_one_lane()) {
+        // ------------------------------------------------------------------------------------------ TMA
+        mbar_arrive_expect_tx(q_full, 2 * TILE);
+        for (int u = 0; u < 4; ++u)
+            load_unit<false>(smem + A2_OFF_Q + (u >> 1) * TILE, u & 1, 4 * pair + u, head, &maps.q, &maps.cq, g, q_full);
+        for (int j = 0; j < nkv; ++j) {
+            const int s = j & 1;
+            if (!mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1))
+                break;
+            mbar_arrive_expect_tx(&k_full[s], TILE);
+            load_unit<false>(smem + A2_OFF_K + s * TILE, 0, 2 * j, head, &maps.k, &maps.ck, g, &k_full[s]);
+            load_unit<false>(smem + A2_OFF_K + s * TILE, 1, 2 * j + 1, head, &maps.k, &maps.ck, g, &k_full[s]);
+            mbar_arrive_expect_tx(&v_full[s], TILE);
+            load_unit<false>(smem + A2_OFF_V + s * TILE, 0, 2 * j, head, &maps.v, &maps.cv, g, &v_full[s]);
+            load_unit<false>(smem + A2_OFF_V + s * TILE, 1, 2 * j + 1, head, &maps.v, &maps.cv, g, &v_full[s]);
+        }
+    } else if (warp == 1 && elect_one_lane()) {
+        // ------------------------------------------------------------------------------------------ MMA
+        const uint32_t id_s = idesc_bf16(128, 128);
+        const uint32_t id_pv = idesc_bf16(128, 128, false, true);
+        auto issue_s = [&](int t, int j) {
+            const uint32_t sq = smem_u32(smem + A2_OFF_Q + t * TILE);
+            const uint32_t sk = smem_u32(smem + A2_OFF_K + (j & 1) * TILE);
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+                const uint32_t off = (kk >> 2) * HALF + (kk & 3) * 32;
+                mma_bf16_ss(tmem + t * 128, sdesc_sw128(sq + off, 16, 1024), sdesc_sw128(sk + off, 16, 1024), id_s, kk > 0);
+            }
+            mma_commit(&s_full[t]);
+        };
+        auto issue_pv = [&](int t, int j) {
+            const uint32_t sv = smem_u32(smem + A2_OFF_V + (j & 1) * TILE);
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+                mma_bf16_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8, sdesc_sw128(sv + kk * 2048, HALF, 1024), id_pv, (j | kk) != 0);
+            mma_commit(&pv_done[t]);
+        };
+        bool ok = mbar_wait(q_full, 0) && mbar_wait(&k_full[0], 0);
+        if (ok) {
+            tc_fence_after();
+            issue_s(0, 0);
+            issue_s(1, 0);
+        }
+        for (int j = 0; j < nkv && ok; ++j) {
+            if (!(ok = mbar_wait(&v_full[j & 1], (j >> 1) & 1) && mbar_wait(&p_full[0], j & 1)))
+                break;
+            tc_fence_after();
+            issue_pv(0, j);
+            const bool more = j + 1 < nkv;
+            if (more) {
+                if (!(ok = mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1)))
+                    break;
+                tc_fence_after();
+                issue_s(0, j + 1);
+            }
+            if (!(ok = mbar_wait(&p_full[1], j & 1)))
+                break;
+            tc_fence_after();
+            issue_pv(1, j);
+            mma_commit(&kv_empty[j & 1]);
+            if (more)
+                issue_s(1, j + 1);
+        }
+        mma_commit(drain);
+        mbar_wait(drain, 0);
+    } else if (warp >= 2) {
+        // -------------------------------------------------------------------------------------- softmax
+        const int t = (warp - 2) >> 2;
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane_id();
+        const uint32_t lane_base = uint32_t(quarter * 32) << 16;
+        const uint32_t tS = tmem + lane_base + t * 128;
+        const uint32_t tO = tmem + lane_base + 256 + t * 128;
+        const float sl2 = p.scale * 1.4426950408889634f;
+        float m = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < nkv; ++j) {
+            if (!(ok = mbar_wait(&s_full[t], j & 1)))
+                break;
+            tc_fence_after();
+            float s[128];
+            {
+                uint32_t r[4][32];
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    tmem_ld32(tS + c * 32, r[c]);
+                tmem_wait_ld();
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        s[c * 32 + i] = __uint_as_float(r[c][i]);
+            }
+            const int left = p.rows - j * 128;
+            if (left < 128) {
+#pragma unroll
+                for (int c = 0; c < 128; ++c)
+                    if (c >= left)
+                        s[c] = -INFINITY;
+            }
+            float mx = s[0];
+#pragma unroll
+            for (int c = 1; c < 128; ++c)
+                mx = fmaxf(mx, s[c]);
+            const float m_cand = mx * sl2;
+            const bool need = m_cand > m + kRescaleThreshold;
+            const float m_use = need ? m_cand : m;
+            const float alpha = need ? ex2_approx(m - m_use) : 1.f;
+            const float msub = m_use == -INFINITY ? 0.f : m_use;
+            float rs = 0.f;
+            uint32_t pk[64];
+#pragma unroll
+            for (int c = 0; c < 64; ++c) {
+                const float a = ex2_approx(fmaf(s[2 * c], sl2, -msub));
+                const float b = ex2_approx(fmaf(s[2 * c + 1], sl2, -msub));
+                rs += a + b;
+                pk[c] = pack_bf16x2(a, b);
+            }
+            if (j > 0 && __any_sync(0xffffffffu, need)) {
+                // O_t holds PV_t(0..j-1), complete (S_t(j) was issued after PV_t(j-1))
+#pragma unroll 1
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t o[32];
+                    tmem_ld32(tO + c * 32, o);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                    tmem_st32(tO + c * 32, o);
+                }
+            }
+            l = l * alpha + rs;
+            m = m_use;
+            tmem_st32(tS, *reinterpret_cast<uint32_t(*)[32]>(pk));
+            tmem_st32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(pk + 32));
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (elect_one_lane())
+                mbar_arrive(&p_full[t]);
+        }
+        if (ok && mbar_wait(&pv_done[t], (nkv - 1) & 1)) {
+            tc_fence_after();
+            const int out_row = pair * 256 + t * 128 + row;
+            const float inv = l > 0.f ? 1.f / l : 0.f;
+            __nv_bfloat16* dst =
+                out_row < p.rows ? reinterpret_cast<__nv_bfloat16*>(p.out) + size_t(out_row) * p.out_row_stride + head * 128 : nullptr;
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+                uint32_t o[32];
+                tmem_ld32(tO + c * 32, o);
+                tmem_wait_ld();
+                if (dst) {
+                    uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        d4[i] = make_uint4(pack_bf16x2(__uint_as_float(o[8 * i]) * inv, __uint_as_float(o[8 * i + 1]) * inv),
+                                           pack_bf16x2(__uint_as_float(o[8 * i + 2]) * inv, __uint_as_float(o[8 * i + 3]) * inv),
+                                           pack_bf16x2(__uint_as_float(o[8 * i + 4]) * inv, __uint_as_float(o[8 * i + 5]) * inv),
+                                           pack_bf16x2(__uint_as_float(o[8 * i + 6]) * inv, __uint_as_float(o[8 * i + 7]) * inv));
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
 CUtensorMap dense_map(const void* base, int heads, int rows, int64_t row_stride)
 {
     const uint64_t dims[3] = {128, uint64_t(heads), uint64_t(rows > 0 ? rows : 1)};
@@ -402,14 +635,14 @@ void attention(const AttnParams& p, cudaStream_t s)
         if (sparse)
             H3_CUDA(cudaFuncSetAttribute(attn_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
         else
-            H3_CUDA(cudaFuncSetAttribute(attn_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+            H3_CUDA(cudaFuncSetAttribute(attn2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, A2_SMEM));
         attr[sparse] = true;
     }
-    const dim3 grid(sparse ? p.q_tiles : (p.rows + 127) / 128, p.heads);
-    if (sparse)
-        attn_kernel<true><<<grid, NT, SMEM_BYTES, s>>>(maps, p);
-    else
-        attn_kernel<false><<<grid, NT, SMEM_BYTES, s>>>(maps, p);
+    if (sparse) {
+        attn_kernel<true><<<dim3(p.q_tiles, p.heads), NT, SMEM_BYTES, s>>>(maps, p);
+    } else {
+        attn2_kernel<<<dim3((p.rows + 255) / 256, p.heads), NT2, A2_SMEM, s>>>(maps, p);
+    }
     H3_CUDA(cudaGetLastError());
 }
 
