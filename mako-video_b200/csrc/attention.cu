@@ -514,24 +514,30 @@ __global__ void __launch_bounds__(NT2, 1) attn2_kernel(const __grid_constant__ M
                     if (c >= left)
                         s[c] = -INFINITY;
             }
-            float mx = s[0];
+            // row maximum and sum over 8 independent partial chains (a single chain would serialise 128 latencies)
+            float mp[8];
 #pragma unroll
-            for (int c = 1; c < 128; ++c)
-                mx = fmaxf(mx, s[c]);
+            for (int i = 0; i < 8; ++i)
+                mp[i] = s[i];
+#pragma unroll
+            for (int c = 8; c < 128; ++c)
+                mp[c & 7] = fmaxf(mp[c & 7], s[c]);
+            const float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
             const float m_cand = mx * sl2;
             const bool need = m_cand > m + kRescaleThreshold;
             const float m_use = need ? m_cand : m;
             const float alpha = need ? ex2_approx(m - m_use) : 1.f;
             const float msub = m_use == -INFINITY ? 0.f : m_use;
-            float rs = 0.f;
+            float sp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
             uint32_t pk[64];
 #pragma unroll
             for (int c = 0; c < 64; ++c) {
                 const float a = ex2_approx(fmaf(s[2 * c], sl2, -msub));
                 const float b = ex2_approx(fmaf(s[2 * c + 1], sl2, -msub));
-                rs += a + b;
+                sp[c & 7] += a + b;
                 pk[c] = pack_bf16x2(a, b);
             }
+            const float rs = ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
             if (j > 0 && __any_sync(0xffffffffu, need)) {
                 // O_t holds PV_t(0..j-1), complete (S_t(j) was issued after PV_t(j-1))
 #pragma unroll 1

@@ -246,6 +246,22 @@ __device__ __forceinline__ float ex2_approx(float x)
     return y;
 }
 
+// 2^x on the FMA and integer pipes (for x >= -125; smaller x gives 2^-125): split x = r + f with r = round(x) by
+// adding 1.5 * 2^23 (the sum's low mantissa bits then hold r), approximate 2^f on [-0.5, 0.5] by a cubic, and add r
+// to the exponent field. The cubic's coefficients are a reweighted least-squares fit of 2^f on Chebyshev nodes of
+// [-0.5, 0.5] (max relative error 7.5e-5 in fp32, below bf16's 3.9e-3 resolution). Used for part of the softmax's
+// exponentials so that they do not all queue on the MUFU pipe.
+__device__ __forceinline__ float ex2_poly(float x)
+{
+    x = fmaxf(x, -125.0f);
+    const float t = x + 12582912.0f;
+    const float j = t - 12582912.0f;
+    const float f = x - j;
+    const float p = fmaf(fmaf(fmaf(0.05517161f, f, 0.24261111f), f, 0.69326097f), f, 0.99992806f);
+    const int r = __float_as_int(t) - 0x4B400000;
+    return __int_as_float(__float_as_int(p) + (r << 23));
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi)
 {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
