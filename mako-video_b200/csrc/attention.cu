@@ -1,14 +1,12 @@
-// Flash attention on sm_100a: tcgen05.mma with S and O accumulators in TMEM, K/V tiles streamed by TMA.
-//
-// One CTA per (query tile of 128 rows, head). Warp roles:
-//   warp 0      TMA: the Q tile once, then K and V tiles of 128 keys into a 2-stage ring
-//   warp 1      MMA: S_j = Q K_j^T into one of two TMEM S buffers (so S_{j+1} overlaps the softmax of S_j), then
-//               O += P_j V_j (V as an MN-major operand) into the TMEM O accumulator
-//   warps 2..5  softmax: thread = query row; S row from TMEM, online softmax in the exp2 domain, P (bf16) into
-//               128-byte-swizzled shared memory for the PV MMA; O rescaled in TMEM only when a row's running
-//               maximum grows by more than 2^8 (the exponentials then use the stale maximum, exact after the final
-//               division); at the end O / l from TMEM to HBM.
-// Every tile is four 64x64 TMA boxes (two 64-row units x two 64-dim halves), so the same pipeline serves the dense
+// Flash attention on sm_100a: tcgen05.mma with the scores S and the output O accumulated in TMEM, P (bf16) written
+// back into TMEM and read from there by the PV MMA, K/V tiles streamed by TMA, online softmax in the exp2 domain
+// with O rescaled only when a row's running maximum grows by more than 2^8 (the exponentials use the stale maximum
+// meanwhile, exact after the final division).
+//   attn2_kernel  dense: two 128-row query tiles per CTA share each K/V tile; the tensor core alternates between the
+//                 tiles so one tile's MMAs overlap the other tile's softmax.
+//   attn3_kernel  sparse (and usable dense): one query tile per CTA with two S buffers, so S_{j+1} is computed while
+//                 the softmax works on S_j; query tiles carry their own key lists.
+// Every tile is four 64x64 TMA boxes (two 64-row units x two 64-dim halves), so the same loads serve the dense
 // layout (units of 64 consecutive rows) and the sparse one (a unit is a 4x4x4 latent cube read straight from the
 // model-ordered rows by a 5-D tensor map, the grid's padding zero-filled, or 64 dense rows).
 #include "attention.cuh"
@@ -21,15 +19,8 @@ namespace h3 {
 
 namespace {
 
-constexpr int NT = 192;
 constexpr int HALF = 16384; // 128 rows x 64 dims bf16
 constexpr int TILE = 32768; // 128 rows x 128 dims
-constexpr int OFF_Q = 0;
-constexpr int OFF_K = TILE;
-constexpr int OFF_V = 3 * TILE;
-constexpr int OFF_P = 5 * TILE;
-constexpr int OFF_BAR = 6 * TILE;
-constexpr int SMEM_BYTES = 6 * TILE + 256 + 1024;
 constexpr float kRescaleThreshold = 8.0f; // log2 units
 
 struct Maps {
@@ -99,260 +90,6 @@ __device__ __forceinline__ int4 implicit_entry(int j, const CubeGrid& g)
     return make_int4(2 * j, 2 * j + 1 < g.units() ? 2 * j + 1 : -1, 15, 0);
 }
 
-template <bool SPARSE>
-__global__ void __launch_bounds__(NT, 1) attn_kernel(const __grid_constant__ Maps maps, const AttnParams p)
-{
-    extern __shared__ uint8_t smem_raw[];
-    const uint32_t raw = smem_u32(smem_raw);
-    uint8_t* smem = smem_raw + (((raw + 1023) & ~1023u) - raw);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
-    uint64_t* q_full = bars + 0;
-    uint64_t* k_full = bars + 1;   // [2]
-    uint64_t* v_full = bars + 3;   // [2]
-    uint64_t* kv_empty = bars + 5; // [2]
-    uint64_t* s_full = bars + 7;   // [2]
-    uint64_t* p_full = bars + 9;
-    uint64_t* pv_done = bars + 10;
-    uint64_t* drain = bars + 11;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
-
-    const int warp = warp_id();
-    const int tile = blockIdx.x, head = blockIdx.y;
-    const CubeGrid& g = p.grid;
-    int nkv;
-    int2 qu;
-    const int4* entries = nullptr;
-    bool implicit = false; // sparse mode, dense query rows: every unit, in order, all visible
-    if constexpr (SPARSE) {
-        nkv = p.nblocks[head * p.q_tiles + tile];
-        implicit = nkv < 0;
-        if (implicit)
-            nkv = (g.units() + 1) / 2;
-        qu = p.q_units[tile];
-        entries = p.blocks + (size_t(head) * p.q_tiles + tile) * p.max_blocks;
-    } else {
-        nkv = (p.rows + 127) / 128;
-        qu = make_int2(2 * tile, 2 * tile + 1);
-    }
-
-    if (threadIdx.x == 0) {
-        mbar_init(q_full, 1);
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(&k_full[i], 1);
-            mbar_init(&v_full[i], 1);
-            mbar_init(&kv_empty[i], 1);
-            mbar_init(&s_full[i], 1);
-        }
-        mbar_init(p_full, 4);
-        mbar_init(pv_done, 1);
-        mbar_init(drain, 1);
-        fence_barrier_init();
-    }
-    if (warp == 1) {
-        tmem_alloc(tmem_slot, 512);
-        tmem_relinquish();
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
-    const uint32_t T_O = 256;
-
-    if (nkv > 0 && warp == 0 && elect_one_lane()) {
-        // ------------------------------------------------------------------------------------------ TMA
-        mbar_arrive_expect_tx(q_full, TILE);
-        load_unit<SPARSE>(smem + OFF_Q, 0, qu.x, head, &maps.q, &maps.cq, g, q_full);
-        load_unit<SPARSE>(smem + OFF_Q, 1, qu.y < 0 ? qu.x : qu.y, head, &maps.q, &maps.cq, g, q_full);
-        for (int j = 0; j < nkv; ++j) {
-            const int s = j & 1;
-            if (!mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1))
-                break;
-            int ua = 2 * j, ub = 2 * j + 1;
-            if constexpr (SPARSE) {
-                const int4 e = implicit ? implicit_entry(j, g) : entries[j];
-                ua = e.x;
-                ub = e.y < 0 ? e.x : e.y; // a lone unit is loaded twice and its second copy masked
-            }
-            mbar_arrive_expect_tx(&k_full[s], TILE);
-            load_unit<SPARSE>(smem + OFF_K + s * TILE, 0, ua, head, &maps.k, &maps.ck, g, &k_full[s]);
-            load_unit<SPARSE>(smem + OFF_K + s * TILE, 1, ub, head, &maps.k, &maps.ck, g, &k_full[s]);
-            mbar_arrive_expect_tx(&v_full[s], TILE);
-            load_unit<SPARSE>(smem + OFF_V + s * TILE, 0, ua, head, &maps.v, &maps.cv, g, &v_full[s]);
-            load_unit<SPARSE>(smem + OFF_V + s * TILE, 1, ub, head, &maps.v, &maps.cv, g, &v_full[s]);
-        }
-    } else if (nkv > 0 && warp == 1 && elect_one_lane()) {
-        // ------------------------------------------------------------------------------------------ MMA
-        const uint32_t id_s = idesc_bf16(128, 128);
-        const uint32_t id_pv = idesc_bf16(128, 128, false, true);
-        const uint32_t sq = smem_u32(smem + OFF_Q), sp = smem_u32(smem + OFF_P);
-        auto issue_s = [&](int j) {
-            const uint32_t sk = smem_u32(smem + OFF_K + (j & 1) * TILE);
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk) {
-                const uint32_t off = (kk >> 2) * HALF + (kk & 3) * 32;
-                mma_bf16_ss(tmem + (j & 1) * 128, sdesc_sw128(sq + off, 16, 1024), sdesc_sw128(sk + off, 16, 1024), id_s, kk > 0);
-            }
-            mma_commit(&s_full[j & 1]);
-        };
-        bool ok = mbar_wait(q_full, 0) && mbar_wait(&k_full[0], 0);
-        if (ok) {
-            tc_fence_after();
-            issue_s(0);
-        }
-        for (int j = 0; j < nkv && ok; ++j) {
-            if (j + 1 < nkv) {
-                if (!(ok = mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1)))
-                    break;
-                tc_fence_after();
-                issue_s(j + 1);
-            }
-            if (!(ok = mbar_wait(p_full, j & 1) && mbar_wait(&v_full[j & 1], (j >> 1) & 1)))
-                break;
-            tc_fence_after();
-            const uint32_t sv = smem_u32(smem + OFF_V + (j & 1) * TILE);
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk) {
-                const uint32_t pa = sp + (kk >> 2) * HALF + (kk & 3) * 32;
-                mma_bf16_ss(tmem + T_O, sdesc_sw128(pa, 16, 1024), sdesc_sw128(sv + kk * 2048, HALF, 1024), id_pv, (j | kk) != 0);
-            }
-            mma_commit(pv_done);
-            mma_commit(&kv_empty[j & 1]);
-        }
-        mma_commit(drain);
-        mbar_wait(drain, 0);
-    } else if (nkv > 0 && warp >= 2) {
-        // -------------------------------------------------------------------------------------- softmax
-        const int quarter = warp & 3;
-        const int row = quarter * 32 + lane_id();
-        const int qh = row >> 6;
-        const uint32_t tl = tmem + (uint32_t(quarter * 32) << 16);
-        const float sl2 = p.scale * 1.4426950408889634f;
-        float m = -INFINITY, l = 0.f;
-        uint8_t* pbuf = smem + OFF_P;
-        bool ok = true;
-        for (int j = 0; j < nkv; ++j) {
-            if (!(ok = mbar_wait(&s_full[j & 1], (j >> 1) & 1)))
-                break;
-            tc_fence_after();
-            float s[128];
-            {
-                uint32_t r[4][32];
-#pragma unroll
-                for (int c = 0; c < 4; ++c)
-                    tmem_ld32(tl + (j & 1) * 128 + c * 32, r[c]);
-                tmem_wait_ld();
-#pragma unroll
-                for (int c = 0; c < 4; ++c)
-#pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        s[c * 32 + i] = __uint_as_float(r[c][i]);
-            }
-            // Key masks: keys past the sequence (dense), or padding / unselected units (sparse).
-            uint64_t km[2] = {~0ull, ~0ull};
-            if constexpr (SPARSE) {
-                const int4 e = implicit ? implicit_entry(j, g) : entries[j];
-                km[0] = (e.z >> (2 * qh)) & 1 ? unit_valid_mask(e.x, g) : 0ull;
-                km[1] = (e.y >= 0 && ((e.z >> (2 * qh + 1)) & 1)) ? unit_valid_mask(e.y, g) : 0ull;
-            } else {
-                const int left = p.rows - j * 128;
-                if (left < 128) {
-                    km[0] = left >= 64 ? ~0ull : (left <= 0 ? 0ull : (1ull << left) - 1);
-                    km[1] = left >= 128 ? ~0ull : (left <= 64 ? 0ull : (1ull << (left - 64)) - 1);
-                }
-            }
-            if ((km[0] & km[1]) != ~0ull) {
-#pragma unroll
-                for (int c = 0; c < 128; ++c)
-                    if (!((km[c >> 6] >> (c & 63)) & 1))
-                        s[c] = -INFINITY;
-            }
-            float mx = s[0];
-#pragma unroll
-            for (int c = 1; c < 128; ++c)
-                mx = fmaxf(mx, s[c]);
-            const float m_cand = mx * sl2;
-            const bool need = m_cand > m + kRescaleThreshold;
-            const float m_use = need ? m_cand : m;
-            const float alpha = need ? ex2_approx(m - m_use) : 1.f;
-            const float msub = m_use == -INFINITY ? 0.f : m_use;
-            float rs = 0.f;
-#pragma unroll
-            for (int c = 0; c < 128; ++c) {
-                s[c] = ex2_approx(fmaf(s[c], sl2, -msub));
-                rs += s[c];
-            }
-            if (j > 0) {
-                if (!(ok = mbar_wait(pv_done, (j - 1) & 1)))
-                    break;
-                tc_fence_after();
-                if (__any_sync(0xffffffffu, need)) {
-#pragma unroll 1
-                    for (int c = 0; c < 4; ++c) {
-                        uint32_t o[32];
-                        tmem_ld32(tl + T_O + c * 32, o);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int i = 0; i < 32; ++i)
-                            o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-                        tmem_st32(tl + T_O + c * 32, o);
-                    }
-                    tmem_wait_st();
-                }
-            }
-            l = l * alpha + rs;
-            m = m_use;
-            // P row -> shared memory, K-major with the 128-byte swizzle (16-byte chunk index ^ row % 8).
-#pragma unroll
-            for (int kg = 0; kg < 16; ++kg) {
-                const uint4 v = make_uint4(pack_bf16x2(s[kg * 8 + 0], s[kg * 8 + 1]), pack_bf16x2(s[kg * 8 + 2], s[kg * 8 + 3]),
-                                           pack_bf16x2(s[kg * 8 + 4], s[kg * 8 + 5]), pack_bf16x2(s[kg * 8 + 6], s[kg * 8 + 7]));
-                *reinterpret_cast<uint4*>(pbuf + (kg >> 3) * HALF + row * 128 + (((kg & 7) ^ (row & 7)) << 4)) = v;
-            }
-            fence_proxy_async_smem();
-            tc_fence_before();
-            __syncwarp();
-            if (elect_one_lane())
-                mbar_arrive(p_full);
-        }
-        if (ok && mbar_wait(pv_done, (nkv - 1) & 1)) {
-            tc_fence_after();
-            int out_row;
-            if constexpr (SPARSE) {
-                const int u = qh ? qu.y : qu.x;
-                out_row = u < 0 ? -1 : unit_row(u, row & 63, g);
-            } else {
-                out_row = tile * 128 + row;
-                if (out_row >= p.rows)
-                    out_row = -1;
-            }
-            const float inv = l > 0.f ? 1.f / l : 0.f;
-            __nv_bfloat16* dst = out_row < 0 ? nullptr
-                                             : reinterpret_cast<__nv_bfloat16*>(p.out) + size_t(out_row) * p.out_row_stride + head * 128;
-#pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
-                uint32_t o[32];
-                tmem_ld32(tl + T_O + c * 32, o);
-                tmem_wait_ld();
-                if (dst) {
-                    uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
-#pragma unroll
-                    for (int i = 0; i < 4; ++i)
-                        d4[i] = make_uint4(pack_bf16x2(__uint_as_float(o[8 * i]) * inv, __uint_as_float(o[8 * i + 1]) * inv),
-                                           pack_bf16x2(__uint_as_float(o[8 * i + 2]) * inv, __uint_as_float(o[8 * i + 3]) * inv),
-                                           pack_bf16x2(__uint_as_float(o[8 * i + 4]) * inv, __uint_as_float(o[8 * i + 5]) * inv),
-                                           pack_bf16x2(__uint_as_float(o[8 * i + 6]) * inv, __uint_as_float(o[8 * i + 7]) * inv));
-                }
-            }
-        }
-    }
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 1) {
-        tc_fence_after();
-        tmem_dealloc(tmem, 512);
-    }
-}
-
 // ------------------------------------------------------------------------------------------------------------
 // Dense attention, two query tiles per CTA (256 query rows of one head) sharing every K/V tile.
 //   warp 0      TMA: Q0 and Q1 once, then K_j and V_j (2-stage ring each)
@@ -364,14 +101,17 @@ __global__ void __launch_bounds__(NT, 1) attn_kernel(const __grid_constant__ Map
 // tensor core executes one thread's MMAs in issue order, so S_t(j+1) overwrites P_t(j) only after PV_t(j) read it;
 // and s_full_t(j) tracks every earlier MMA, so once S_t(j) is complete, PV_t(j-1) is too and the softmax may write
 // P_t(j) and rescale O_t.
-constexpr int NT2 = 320;
+constexpr int A2_SPLIT = 1;        // warps sharing a query row in the softmax (2 measured no faster)
+constexpr int NT2 = 64 + 256 * A2_SPLIT;
 constexpr int A2_OFF_Q = 0;        // Q0, Q1
 constexpr int A2_OFF_K = 2 * TILE; // 2 stages
 constexpr int A2_OFF_V = 4 * TILE; // 2 stages
 constexpr int A2_OFF_BAR = 6 * TILE;
-constexpr int A2_SMEM = 6 * TILE + 256 + 1024;
+constexpr int A2_OFF_RED = 6 * TILE + 256; // row maxima and sums exchanged between a row's warps
+constexpr int A2_SMEM = 6 * TILE + 256 + 2 * 3 * 4 * 128 * 4 + 1024;
 
-__global__ void __launch_bounds__(NT2, 1) attn2_kernel(const __grid_constant__ Maps maps, const AttnParams p)
+template <int SPLIT>
+__global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid_constant__ Maps maps, const AttnParams p)
 {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
@@ -385,7 +125,8 @@ __global__ void __launch_bounds__(NT2, 1) attn2_kernel(const __grid_constant__ M
     uint64_t* p_full = bars + 9;   // [2] per tile
     uint64_t* pv_done = bars + 11; // [2] per tile
     uint64_t* drain = bars + 13;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+    uint64_t* xchg = bars + 14;    // [2] per tile: the row-maximum / row-sum exchange between a row's warps
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
 
     const int warp = warp_id();
     const int pair = blockIdx.x, head = blockIdx.y;
@@ -399,8 +140,9 @@ __global__ void __launch_bounds__(NT2, 1) attn2_kernel(const __grid_constant__ M
             mbar_init(&v_full[i], 1);
             mbar_init(&kv_empty[i], 1);
             mbar_init(&s_full[i], 1);
-            mbar_init(&p_full[i], 4);
+            mbar_init(&p_full[i], 4 * SPLIT);
             mbar_init(&pv_done[i], 1);
+            mbar_init(&xchg[i], 4 * SPLIT);
         }
         mbar_init(drain, 1);
         fence_barrier_init();
@@ -481,12 +223,17 @@ __global__ void __launch_bounds__(NT2, 1) attn2_kernel(const __grid_constant__ M
         mbar_wait(drain, 0);
     } else if (warp >= 2) {
         // -------------------------------------------------------------------------------------- softmax
-        const int t = (warp - 2) >> 2;
+        // SPLIT warps share each row: the warps of (tile t, slice hc) handle keys [hc NC, hc NC + NC) of their rows
+        // and agree on the row maximum through shared memory.
+        constexpr int NC = 128 / SPLIT;
+        const int t = (warp - 2) / (4 * SPLIT);
+        const int hc = ((warp - 2) % (4 * SPLIT)) / 4;
         const int quarter = warp & 3;
         const int row = quarter * 32 + lane_id();
         const uint32_t lane_base = uint32_t(quarter * 32) << 16;
         const uint32_t tS = tmem + lane_base + t * 128;
-        const uint32_t tO = tmem + lane_base + 256 + t * 128;
+        const uint32_t tO = tmem + lane_base + 256 + t * 128 + hc * NC;
+        float* red = reinterpret_cast<float*>(smem + A2_OFF_RED) + t * (3 * SPLIT * 128); // [3 slots][SPLIT][128 rows]
         const float sl2 = p.scale * 1.4426950408889634f;
         float m = -INFINITY, l = 0.f;
         bool ok = true;
@@ -494,54 +241,394 @@ __global__ void __launch_bounds__(NT2, 1) attn2_kernel(const __grid_constant__ M
             if (!(ok = mbar_wait(&s_full[t], j & 1)))
                 break;
             tc_fence_after();
-            float s[128];
+            float s[NC];
             {
-                uint32_t r[4][32];
+                uint32_t r[NC / 32][32];
 #pragma unroll
-                for (int c = 0; c < 4; ++c)
-                    tmem_ld32(tS + c * 32, r[c]);
+                for (int c = 0; c < NC / 32; ++c)
+                    tmem_ld32(tS + hc * NC + c * 32, r[c]);
                 tmem_wait_ld();
 #pragma unroll
-                for (int c = 0; c < 4; ++c)
+                for (int c = 0; c < NC / 32; ++c)
 #pragma unroll
                     for (int i = 0; i < 32; ++i)
                         s[c * 32 + i] = __uint_as_float(r[c][i]);
             }
-            const int left = p.rows - j * 128;
-            if (left < 128) {
+            const int left = p.rows - j * 128 - hc * NC;
+            if (left < NC) {
 #pragma unroll
-                for (int c = 0; c < 128; ++c)
+                for (int c = 0; c < NC; ++c)
                     if (c >= left)
                         s[c] = -INFINITY;
             }
-            // row maximum and sum over 8 independent partial chains (a single chain would serialise 128 latencies)
+            // Row maximum over 8 independent chains of three-input maxima (a single chain would serialise the
+            // latencies); the exponent arguments and the row sum as packed fp32 pairs.
             float mp[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i)
-                mp[i] = s[i];
+                mp[i] = fmaxf(s[2 * i], s[2 * i + 1]);
 #pragma unroll
-            for (int c = 8; c < 128; ++c)
-                mp[c & 7] = fmaxf(mp[c & 7], s[c]);
-            const float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
+            for (int c = 16; c < NC; c += 16)
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    mp[i] = max3f(mp[i], s[c + 2 * i], s[c + 2 * i + 1]);
+            float mx = max3f(max3f(mp[0], mp[1], mp[2]), max3f(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7]));
+            if constexpr (SPLIT > 1) {
+                // Every slice has loaded its scores once this exchange completes, so P may then overwrite them.
+                float* slot = red + (j & 1) * SPLIT * 128;
+                slot[hc * 128 + row] = mx;
+                __syncwarp();
+                if (elect_one_lane())
+                    mbar_arrive(&xchg[t]);
+                if (!(ok = mbar_wait(&xchg[t], j & 1)))
+                    break;
+#pragma unroll
+                for (int o = 0; o < SPLIT; ++o)
+                    if (o != hc)
+                        mx = fmaxf(mx, slot[o * 128 + row]);
+            }
             const float m_cand = mx * sl2;
             const bool need = m_cand > m + kRescaleThreshold;
             const float m_use = need ? m_cand : m;
             const float alpha = need ? ex2_approx(m - m_use) : 1.f;
             const float msub = m_use == -INFINITY ? 0.f : m_use;
-            float sp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            uint32_t pk[64];
+            const float2 scale2 = make_float2(sl2, sl2), neg2 = make_float2(-msub, -msub);
+            float2 sp[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+            uint32_t pk[NC / 2];
 #pragma unroll
-            for (int c = 0; c < 64; ++c) {
-                const float a = ex2_approx(fmaf(s[2 * c], sl2, -msub));
-                const float b = ex2_approx(fmaf(s[2 * c + 1], sl2, -msub));
-                sp[c & 7] += a + b;
-                pk[c] = pack_bf16x2(a, b);
+            for (int c = 0; c < NC / 2; ++c) {
+                const float2 x = fma2(make_float2(s[2 * c], s[2 * c + 1]), scale2, neg2);
+                const float2 e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+                sp[c & 3] = add2(sp[c & 3], e);
+                pk[c] = pack_bf16x2(e.x, e.y);
             }
-            const float rs = ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
+            const float2 s01 = add2(add2(sp[0], sp[1]), add2(sp[2], sp[3]));
+            const float rs = s01.x + s01.y;
             if (j > 0 && __any_sync(0xffffffffu, need)) {
-                // O_t holds PV_t(0..j-1), complete (S_t(j) was issued after PV_t(j-1))
+                // O_t holds PV_t(0..j-1), complete (S_t(j) was issued after PV_t(j-1)); each slice rescales its columns
 #pragma unroll 1
-                for (int c = 0; c < 4; ++c) {
+                for (int c = 0; c < NC / 32; ++c) {
+                    uint32_t o[32];
+                    tmem_ld32(tO + c * 32, o);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                    tmem_st32(tO + c * 32, o);
+                }
+            }
+            l = l * alpha + rs; // this slice's share of the row sum
+            m = m_use;
+#pragma unroll
+            for (int c = 0; c < NC / 64; ++c)
+                tmem_st32(tS + hc * (NC / 2) + c * 32, *reinterpret_cast<uint32_t(*)[32]>(pk + c * 32));
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (elect_one_lane())
+                mbar_arrive(&p_full[t]);
+        }
+        if constexpr (SPLIT > 1) {
+            if (ok) {
+                float* slot = red + 2 * SPLIT * 128;
+                slot[hc * 128 + row] = l;
+                __syncwarp();
+                if (elect_one_lane())
+                    mbar_arrive(&xchg[t]);
+                ok = mbar_wait(&xchg[t], nkv & 1);
+                l = 0.f;
+#pragma unroll
+                for (int o = 0; o < SPLIT; ++o)
+                    l += slot[o * 128 + row];
+            }
+        }
+        if (ok && mbar_wait(&pv_done[t], (nkv - 1) & 1)) {
+            tc_fence_after();
+            const int out_row = pair * 256 + t * 128 + row;
+            const float inv = l > 0.f ? 1.f / l : 0.f;
+            __nv_bfloat16* dst = out_row < p.rows
+                                     ? reinterpret_cast<__nv_bfloat16*>(p.out) + size_t(out_row) * p.out_row_stride + head * 128 + hc * NC
+                                     : nullptr;
+#pragma unroll 1
+            for (int c = 0; c < NC / 32; ++c) {
+                uint32_t o[32];
+                tmem_ld32(tO + c * 32, o);
+                tmem_wait_ld();
+                if (dst) {
+                    uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        d4[i] = make_uint4(pack_bf16x2(__uint_as_float(o[8 * i]) * inv, __uint_as_float(o[8 * i + 1]) * inv),
+                                           pack_bf16x2(__uint_as_float(o[8 * i + 2]) * inv, __uint_as_float(o[8 * i + 3]) * inv),
+                                           pack_bf16x2(__uint_as_float(o[8 * i + 4]) * inv, __uint_as_float(o[8 * i + 5]) * inv),
+                                           pack_bf16x2(__uint_as_float(o[8 * i + 6]) * inv, __uint_as_float(o[8 * i + 7]) * inv));
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+// ------------------------------------------------------------------------------------------------------------
+// One query tile (128 rows) per CTA with double-buffered scores, dense or sparse.
+//   warp 0      TMA: Q once; K_j into a 3-stage ring (freed as soon as S_j is done), V_j into a 2-stage ring
+//   warp 1      MMA: S_0, S_1 up front; then per block PV_j (A = P_j from TMEM) and S_{j+2} into the buffer S_j
+//               leaves, so S_{j+1} is always ready when the softmax finishes block j
+//   warps 2..9  softmax: two warps per query row, each over one 64-key unit of the block (hc = 0, 1), agreeing on
+//               the row maximum through shared memory; P_j (bf16) written back over S_j's first 64 columns.
+// TMEM: S buffer 0 | S buffer 1 | O (128 columns each). S_{j+2} overwrites P_j only after PV_j read it (one thread
+// issues both, and the tensor core runs them in order). The softmax of block j may rescale O only once PV_{j-1} is
+// done (it waits for that only when a rescale is needed).
+constexpr int A3_KST = 3, A3_VST = 2;
+constexpr int NT3 = 64 + 256;
+constexpr int A3_OFF_Q = 0;
+constexpr int A3_OFF_K = TILE;
+constexpr int A3_OFF_V = A3_OFF_K + A3_KST * TILE;
+constexpr int A3_OFF_BAR = A3_OFF_V + A3_VST * TILE;
+constexpr int A3_OFF_RED = A3_OFF_BAR + 256;
+constexpr int A3_SMEM = A3_OFF_RED + 3 * 2 * 128 * 4 + 1024;
+
+template <bool SPARSE>
+__global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ Maps maps, const AttnParams p)
+{
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    uint8_t* smem = smem_raw + (((raw + 1023) & ~1023u) - raw);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + A3_OFF_BAR);
+    uint64_t* q_full = bars + 0;
+    uint64_t* k_full = bars + 1;                   // [A3_KST]
+    uint64_t* k_empty = k_full + A3_KST;           // [A3_KST]
+    uint64_t* v_full = k_empty + A3_KST;           // [A3_VST]
+    uint64_t* v_empty = v_full + A3_VST;           // [A3_VST]
+    uint64_t* s_full = v_empty + A3_VST;           // [2] per S buffer
+    uint64_t* p_full = s_full + 2;
+    uint64_t* pv_done = p_full + 1;
+    uint64_t* xchg = pv_done + 1;
+    uint64_t* drain = xchg + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+    const int warp = warp_id();
+    const int tile = blockIdx.x, head = blockIdx.y;
+    const CubeGrid& g = p.grid;
+    int nkv;
+    int2 qu;
+    const int4* entries = nullptr;
+    bool implicit = false;
+    if constexpr (SPARSE) {
+        nkv = p.nblocks[head * p.q_tiles + tile];
+        implicit = nkv < 0;
+        if (implicit)
+            nkv = (g.units() + 1) / 2;
+        qu = p.q_units[tile];
+        entries = p.blocks + (size_t(head) * p.q_tiles + tile) * p.max_blocks;
+    } else {
+        nkv = (p.rows + 127) / 128;
+        qu = make_int2(2 * tile, 2 * tile + 1);
+    }
+    auto entry = [&](int j) -> int4 {
+        if constexpr (SPARSE)
+            return implicit ? implicit_entry(j, g) : entries[j];
+        else
+            return make_int4(2 * j, 2 * j + 1, 15, 0);
+    };
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        for (int i = 0; i < A3_KST; ++i) {
+            mbar_init(&k_full[i], 1);
+            mbar_init(&k_empty[i], 1);
+        }
+        for (int i = 0; i < A3_VST; ++i) {
+            mbar_init(&v_full[i], 1);
+            mbar_init(&v_empty[i], 1);
+        }
+        mbar_init(&s_full[0], 1);
+        mbar_init(&s_full[1], 1);
+        mbar_init(p_full, 8);
+        mbar_init(pv_done, 1);
+        mbar_init(xchg, 8);
+        mbar_init(drain, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    constexpr uint32_t T_O = 256;
+
+    if (nkv > 0 && warp == 0 && elect_one_lane()) {
+        // ------------------------------------------------------------------------------------------ TMA
+        mbar_arrive_expect_tx(q_full, TILE);
+        load_unit<SPARSE>(smem + A3_OFF_Q, 0, qu.x, head, &maps.q, &maps.cq, g, q_full);
+        load_unit<SPARSE>(smem + A3_OFF_Q, 1, qu.y < 0 ? qu.x : qu.y, head, &maps.q, &maps.cq, g, q_full);
+        // K runs ahead of V by up to the depth of its ring
+        int jk = 0, jv = 0;
+        bool ok = true;
+        while (ok && jv < nkv) {
+            const bool k_turn = jk < nkv && jk < jv + A3_KST;
+            if (k_turn) {
+                const int s = jk % A3_KST;
+                if (!(ok = mbar_wait(&k_empty[s], ((jk / A3_KST) & 1) ^ 1)))
+                    break;
+                const int4 e = entry(jk);
+                mbar_arrive_expect_tx(&k_full[s], TILE);
+                load_unit<SPARSE>(smem + A3_OFF_K + s * TILE, 0, e.x, head, &maps.k, &maps.ck, g, &k_full[s]);
+                load_unit<SPARSE>(smem + A3_OFF_K + s * TILE, 1, e.y < 0 ? e.x : e.y, head, &maps.k, &maps.ck, g, &k_full[s]);
+                ++jk;
+            } else {
+                const int s = jv % A3_VST;
+                if (!(ok = mbar_wait(&v_empty[s], ((jv / A3_VST) & 1) ^ 1)))
+                    break;
+                const int4 e = entry(jv);
+                mbar_arrive_expect_tx(&v_full[s], TILE);
+                load_unit<SPARSE>(smem + A3_OFF_V + s * TILE, 0, e.x, head, &maps.v, &maps.cv, g, &v_full[s]);
+                load_unit<SPARSE>(smem + A3_OFF_V + s * TILE, 1, e.y < 0 ? e.x : e.y, head, &maps.v, &maps.cv, g, &v_full[s]);
+                ++jv;
+            }
+        }
+    } else if (nkv > 0 && warp == 1 && elect_one_lane()) {
+        // ------------------------------------------------------------------------------------------ MMA
+        const uint32_t id_s = idesc_bf16(128, 128);
+        const uint32_t id_pv = idesc_bf16(128, 128, false, true);
+        const uint32_t sq = smem_u32(smem + A3_OFF_Q);
+        auto issue_s = [&](int j) {
+            const int s = j % A3_KST;
+            const uint32_t sk = smem_u32(smem + A3_OFF_K + s * TILE);
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+                const uint32_t off = (kk >> 2) * HALF + (kk & 3) * 32;
+                mma_bf16_ss(tmem + (j & 1) * 128, sdesc_sw128(sq + off, 16, 1024), sdesc_sw128(sk + off, 16, 1024), id_s, kk > 0);
+            }
+            mma_commit(&s_full[j & 1]);
+            mma_commit(&k_empty[s]);
+        };
+        bool ok = mbar_wait(q_full, 0);
+        for (int j = 0; j < 2 && j < nkv && ok; ++j) {
+            if ((ok = mbar_wait(&k_full[j % A3_KST], (j / A3_KST) & 1))) {
+                tc_fence_after();
+                issue_s(j);
+            }
+        }
+        for (int j = 0; j < nkv && ok; ++j) {
+            const int sv = j % A3_VST;
+            if (!(ok = mbar_wait(p_full, j & 1) && mbar_wait(&v_full[sv], (j / A3_VST) & 1)))
+                break;
+            tc_fence_after();
+            const uint32_t vb = smem_u32(smem + A3_OFF_V + sv * TILE);
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+                mma_bf16_ts(tmem + T_O, tmem + (j & 1) * 128 + kk * 8, sdesc_sw128(vb + kk * 2048, HALF, 1024), id_pv, (j | kk) != 0);
+            mma_commit(pv_done);
+            mma_commit(&v_empty[sv]);
+            if (j + 2 < nkv) {
+                if (!(ok = mbar_wait(&k_full[(j + 2) % A3_KST], ((j + 2) / A3_KST) & 1)))
+                    break;
+                tc_fence_after();
+                issue_s(j + 2);
+            }
+        }
+        mma_commit(drain);
+        mbar_wait(drain, 0);
+    } else if (nkv > 0 && warp >= 2) {
+        // -------------------------------------------------------------------------------------- softmax
+        const int hc = (warp - 2) >> 2; // key unit of the block this warp handles
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane_id();
+        const int qh = row >> 6;
+        const uint32_t lane_base = uint32_t(quarter * 32) << 16;
+        const uint32_t tO = tmem + lane_base + T_O + hc * 64;
+        float* red = reinterpret_cast<float*>(smem + A3_OFF_RED); // [3 slots][2 slices][128 rows]
+        const float sl2 = p.scale * 1.4426950408889634f;
+        float m = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < nkv; ++j) {
+            const uint32_t tS = tmem + lane_base + (j & 1) * 128;
+            if (!(ok = mbar_wait(&s_full[j & 1], (j >> 1) & 1)))
+                break;
+            tc_fence_after();
+            float s[64];
+            {
+                uint32_t r[2][32];
+                tmem_ld32(tS + hc * 64, r[0]);
+                tmem_ld32(tS + hc * 64 + 32, r[1]);
+                tmem_wait_ld();
+#pragma unroll
+                for (int c = 0; c < 2; ++c)
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        s[c * 32 + i] = __uint_as_float(r[c][i]);
+            }
+            // Keys this slice may not see: past the sequence (dense), or padding / unselected units (sparse).
+            uint64_t km = ~0ull;
+            if constexpr (SPARSE) {
+                const int4 e = entry(j);
+                const int u = hc ? e.y : e.x;
+                km = (u >= 0 && ((e.z >> (2 * qh + hc)) & 1)) ? unit_valid_mask(u, g) : 0ull;
+            } else {
+                const int left = p.rows - j * 128 - hc * 64;
+                if (left < 64)
+                    km = left <= 0 ? 0ull : (1ull << left) - 1;
+            }
+            if (km != ~0ull) {
+#pragma unroll
+                for (int c = 0; c < 64; ++c)
+                    if (!((km >> c) & 1))
+                        s[c] = -INFINITY;
+            }
+            float mp[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                mp[i] = fmaxf(s[2 * i], s[2 * i + 1]);
+#pragma unroll
+            for (int c = 16; c < 64; c += 16)
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    mp[i] = max3f(mp[i], s[c + 2 * i], s[c + 2 * i + 1]);
+            float mx = max3f(max3f(mp[0], mp[1], mp[2]), max3f(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7]));
+            {
+                // Both slices have loaded their scores once this exchange completes, so P may then overwrite them.
+                float* slot = red + (j & 1) * 256;
+                slot[hc * 128 + row] = mx;
+                __syncwarp();
+                if (elect_one_lane())
+                    mbar_arrive(xchg);
+                if (!(ok = mbar_wait(xchg, j & 1)))
+                    break;
+                mx = fmaxf(mx, slot[(hc ^ 1) * 128 + row]);
+            }
+            const float m_cand = mx * sl2;
+            const bool need = m_cand > m + kRescaleThreshold;
+            const float m_use = need ? m_cand : m;
+            const float alpha = need ? ex2_approx(m - m_use) : 1.f;
+            const float msub = m_use == -INFINITY ? 0.f : m_use;
+            const float2 scale2 = make_float2(sl2, sl2), neg2 = make_float2(-msub, -msub);
+            float2 sp[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+            uint32_t pk[32];
+#pragma unroll
+            for (int c = 0; c < 32; ++c) {
+                const float2 x = fma2(make_float2(s[2 * c], s[2 * c + 1]), scale2, neg2);
+                const float2 e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+                sp[c & 3] = add2(sp[c & 3], e);
+                pk[c] = pack_bf16x2(e.x, e.y);
+            }
+            const float2 s01 = add2(add2(sp[0], sp[1]), add2(sp[2], sp[3]));
+            const float rs = s01.x + s01.y;
+            if (j > 0 && __any_sync(0xffffffffu, need)) {
+                // O holds PV_0..PV_{j-2} for sure; wait for PV_{j-1} before scaling it
+                if (!(ok = mbar_wait(pv_done, (j - 1) & 1)))
+                    break;
+                tc_fence_after();
+#pragma unroll 1
+                for (int c = 0; c < 2; ++c) {
                     uint32_t o[32];
                     tmem_ld32(tO + c * 32, o);
                     tmem_wait_ld();
@@ -553,22 +640,38 @@ __global__ void __launch_bounds__(NT2, 1) attn2_kernel(const __grid_constant__ M
             }
             l = l * alpha + rs;
             m = m_use;
-            tmem_st32(tS, *reinterpret_cast<uint32_t(*)[32]>(pk));
-            tmem_st32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(pk + 32));
+            tmem_st32(tS + hc * 32, pk);
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
             if (elect_one_lane())
-                mbar_arrive(&p_full[t]);
+                mbar_arrive(p_full);
         }
-        if (ok && mbar_wait(&pv_done[t], (nkv - 1) & 1)) {
+        if (ok) {
+            float* slot = red + 2 * 256;
+            slot[hc * 128 + row] = l;
+            __syncwarp();
+            if (elect_one_lane())
+                mbar_arrive(xchg);
+            ok = mbar_wait(xchg, nkv & 1);
+            l = slot[row] + slot[128 + row];
+        }
+        if (ok && mbar_wait(pv_done, (nkv - 1) & 1)) {
             tc_fence_after();
-            const int out_row = pair * 256 + t * 128 + row;
+            int out_row;
+            if constexpr (SPARSE) {
+                const int u = qh ? qu.y : qu.x;
+                out_row = u < 0 ? -1 : unit_row(u, row & 63, g);
+            } else {
+                out_row = tile * 128 + row;
+                if (out_row >= p.rows)
+                    out_row = -1;
+            }
             const float inv = l > 0.f ? 1.f / l : 0.f;
-            __nv_bfloat16* dst =
-                out_row < p.rows ? reinterpret_cast<__nv_bfloat16*>(p.out) + size_t(out_row) * p.out_row_stride + head * 128 : nullptr;
+            __nv_bfloat16* dst = out_row < 0 ? nullptr
+                                             : reinterpret_cast<__nv_bfloat16*>(p.out) + size_t(out_row) * p.out_row_stride + head * 128 + hc * 64;
 #pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
+            for (int c = 0; c < 2; ++c) {
                 uint32_t o[32];
                 tmem_ld32(tO + c * 32, o);
                 tmem_wait_ld();
@@ -639,16 +742,17 @@ void attention(const AttnParams& p, cudaStream_t s)
     static bool attr[2] = {false, false};
     if (!attr[sparse]) {
         if (sparse)
-            H3_CUDA(cudaFuncSetAttribute(attn_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+            H3_CUDA(cudaFuncSetAttribute(attn3_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, A3_SMEM));
         else
-            H3_CUDA(cudaFuncSetAttribute(attn2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, A2_SMEM));
+            H3_CUDA(cudaFuncSetAttribute(attn2_kernel<A2_SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize, A2_SMEM));
         attr[sparse] = true;
     }
-    if (sparse) {
-        attn_kernel<true><<<dim3(p.q_tiles, p.heads), NT, SMEM_BYTES, s>>>(maps, p);
-    } else {
-        attn2_kernel<<<dim3((p.rows + 255) / 256, p.heads), NT2, A2_SMEM, s>>>(maps, p);
-    }
+    // Dense: two query tiles per CTA share every K/V tile (half the shared-memory traffic per FLOP). Sparse: query
+    // tiles have their own key lists, so one tile per CTA with double-buffered scores.
+    if (sparse)
+        attn3_kernel<true><<<dim3(p.q_tiles, p.heads), NT3, A3_SMEM, s>>>(maps, p);
+    else
+        attn2_kernel<A2_SPLIT><<<dim3((p.rows + 255) / 256, p.heads), NT2, A2_SMEM, s>>>(maps, p);
     H3_CUDA(cudaGetLastError());
 }
 

@@ -1,5 +1,5 @@
 // The C ABI (include/h3_c.h): status codes and a per-thread error message around the C++ runtime.
-#include "../../include/h3_c.h"
+#include "h3_c.h"
 
 #include "common.hpp"
 #include "embed.cuh"

@@ -9,7 +9,7 @@
 // keeps the last call's contents: calls whose work overlaps on the GPU (two streams, or two host threads) race on it.
 // Its device address is looked up once per device, on the first call made with that device current; make that first
 // call before any stream capture.
-#include "../../include/h3_c.h"
+#include "h3_c.h"
 
 #include "attention.cuh"
 #include "common.hpp"
