@@ -363,6 +363,9 @@ def main():
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if "NCCL_DEBUG_FILE" not in os.environ:
+        # NCCL's own messages (its version banner included) go to a file: the JSON line is rank 0's only stdout
+        os.environ["NCCL_DEBUG_FILE"] = os.path.join(tempfile.gettempdir(), f"h3_nccl.{os.getpid()}.log")
     if args.impl == "reference":
         run_reference(args, rank, world)
         return

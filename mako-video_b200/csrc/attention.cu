@@ -71,6 +71,20 @@ __device__ __forceinline__ uint64_t unit_valid_mask(int unit, const CubeGrid& g)
     return n >= 64 ? ~0ull : (n <= 0 ? 0ull : ((1ull << n) - 1));
 }
 
+// Where query row `row`'s output (head `head`, dims from `d0`) goes: this rank's buffer, or straight to the row's
+// owner when the sequence-parallel exchange is fused into the epilogue (the stores are performed when the kernel
+// completes; the barrier that follows it on the stream orders them before any reader). Null for padding rows.
+__device__ __forceinline__ __nv_bfloat16* out_ptr(const AttnParams& p, int row, int head, int d0)
+{
+    if (row < 0)
+        return nullptr;
+    if (!p.peer_out[0])
+        return reinterpret_cast<__nv_bfloat16*>(p.out) + size_t(row) * p.out_row_stride + head * 128 + d0;
+    const int owner = row / p.rows_per_rank, local = row - owner * p.rows_per_rank;
+    return reinterpret_cast<__nv_bfloat16*>(p.peer_out[owner]) +
+           (size_t(p.my_rank) * p.rows_per_rank + local) * (size_t(p.heads) * 128) + head * 128 + d0;
+}
+
 // The model row of row `r` (0..63) of a unit, or -1 when it is padding.
 __device__ __forceinline__ int unit_row(int unit, int r, const CubeGrid& g)
 {
@@ -346,9 +360,7 @@ __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid
             tc_fence_after();
             const int out_row = pair * 256 + t * 128 + row;
             const float inv = l > 0.f ? 1.f / l : 0.f;
-            __nv_bfloat16* dst = out_row < p.rows
-                                     ? reinterpret_cast<__nv_bfloat16*>(p.out) + size_t(out_row) * p.out_row_stride + head * 128 + hc * NC
-                                     : nullptr;
+            __nv_bfloat16* dst = out_ptr(p, out_row < p.rows ? out_row : -1, head, hc * NC);
 #pragma unroll 1
             for (int c = 0; c < NC / 32; ++c) {
                 uint32_t o[32];
@@ -668,8 +680,7 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
                     out_row = -1;
             }
             const float inv = l > 0.f ? 1.f / l : 0.f;
-            __nv_bfloat16* dst = out_row < 0 ? nullptr
-                                             : reinterpret_cast<__nv_bfloat16*>(p.out) + size_t(out_row) * p.out_row_stride + head * 128 + hc * 64;
+            __nv_bfloat16* dst = out_ptr(p, out_row, head, hc * 64);
 #pragma unroll 1
             for (int c = 0; c < 2; ++c) {
                 uint32_t o[32];

@@ -36,6 +36,11 @@ struct AttnParams {
     int rows = 0;           // dense mode: query and key rows (keys at or past `rows` are masked)
     void* out = nullptr;    // o: (row, head, dim) at out + row * out_row_stride + head * 128 + dim
     int64_t out_row_stride = 0;
+    // Sequence parallel with the exchange fused into the epilogue: row R's output goes straight to its owner
+    // R / rows_per_rank, into that rank's [P][rows_per_rank][heads x 128] buffer (block my_rank), mapped into this
+    // process (peer_out[0] null: write `out`).
+    void* peer_out[8] = {};
+    int rows_per_rank = 0, my_rank = 0;
     float scale = 0.08838834764831845f; // 1 / sqrt(128)
 
     // Sparse mode (blocks != null). Query tile t is the unit pair q_units[t]; for head h it visits

@@ -129,8 +129,11 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tacc
             }
             const int head = (col % p.inner) / 128;
             const int rank = head / p.heads_per_rank, hl = head % p.heads_per_rank;
-            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) +
-                                 ((size_t(rank) * p.rows_local + gm) * 3 + sec) * size_t(p.heads_per_rank) * 128 + hl * 128;
+            // Into the head group's owner: straight into its receive buffer (block my_rank of the sequence) when a
+            // peer pointer is given, else into this rank's send layout (block `rank`).
+            __nv_bfloat16* base = reinterpret_cast<__nv_bfloat16*>(p.peer_out[rank] ? p.peer_out[rank] : p.out);
+            const size_t rowpos = size_t(p.peer_out[rank] ? p.my_rank : rank) * p.rows_local + gm;
+            __nv_bfloat16* dst = base + (rowpos * 3 + sec) * size_t(p.heads_per_rank) * 128 + hl * 128;
 #pragma unroll
             for (int c = 0; c < 4; ++c)
                 store_bf16x32(dst + c * 32, v + c * 32);
@@ -330,6 +333,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             if (elect_one_lane())
                 mbar_arrive(&tempty[acc]);
         }
+        if (p.peer_out[0])
+            __threadfence_system(); // this thread's NVLink stores are performed before the kernel ends
     }
     tc_fence_before();
     __syncthreads();

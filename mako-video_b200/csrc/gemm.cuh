@@ -40,6 +40,10 @@ struct GemmParams {
     int inner = 0;          // heads * 128
     int heads_per_rank = 0; // heads each rank attends (all heads with one rank)
     int rows_local = 0;     // rows of this rank (the qkv layout's per-destination block)
+    // Sequence parallel with the exchange fused into the epilogue: rank r's receive buffer ([P x rows_local][3]
+    // [heads_per_rank][128], this rank's rows at block my_rank), mapped into this process (null: use `out`).
+    void* peer_out[8] = {};
+    int my_rank = 0;
     const float* a_scale = nullptr; // int8: per-row activation scale
     const float* b_scale = nullptr; // int8: per-output-row weight scale
 };

@@ -206,6 +206,21 @@ struct Model::Impl {
     DevBuf sp_mq, sp_mk, sp_scores, sp_sel, sp_nsel, sp_blocks, sp_nblocks, sp_qunits;
     ncclComm_t comm = nullptr;
     std::vector<cudaEvent_t> ev;
+    // Sequence parallel with the exchange fused into the kernels: every rank's qkv_recv and o_recv mapped here.
+    bool fused = true;
+    void* peer_qkv[8] = {};
+    void* peer_o[8] = {};
+    std::vector<void*> opened; // peers' buffers mapped by cudaIpcOpenMemHandle (closed on re-map and exit)
+    void* mapped_qkv = nullptr;
+    void* mapped_o = nullptr;
+    DevBuf barrier_word, ipc_stage;
+    void close_peers()
+    {
+        for (void* p : opened)
+            cudaIpcCloseMemHandle(p);
+        opened.clear();
+        mapped_qkv = mapped_o = nullptr;
+    }
 };
 
 #define H3_NCCL(x)                                                                                                       \
@@ -224,10 +239,14 @@ Model::Model(const Config& c, uint64_t seed, uint32_t int8_mask, const World& wo
         throw CudaError("world: heads must divide evenly over the ranks");
     H3_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
     if (world.size > 1) {
+        if (world.size > 8)
+            throw CudaError("world: at most 8 ranks (one NVSwitch box)");
         ncclUniqueId id;
         static_assert(sizeof(id) == 128, "ncclUniqueId size");
         std::memcpy(&id, world.nccl_id, 128);
         H3_NCCL(ncclCommInitRank(&d_->comm, world.size, id, world.rank));
+        const char* ex = std::getenv("H3_EXCHANGE");
+        d_->fused = !(ex && std::string(ex) == "nccl");
     }
     const int d = c.dim, L = c.blocks, inner = c.inner(), F = c.ffn, td = c.time_dim;
     cudaStream_t s = stream_;
@@ -310,6 +329,8 @@ Model::Model(const Config& c, uint64_t seed, uint32_t int8_mask, const World& wo
 
 Model::~Model()
 {
+    if (d_)
+        d_->close_peers();
     if (d_ && d_->comm)
         ncclCommDestroy(d_->comm);
     if (d_)
@@ -351,6 +372,46 @@ void Model::alloc_activations()
     }
     d_->rows_out.ensure(M * 128 * 4);
     d_->rows_all.ensure(Spad * 128 * 4);
+    if (P > 1 && d_->fused)
+        map_peers();
+}
+
+void Model::map_peers()
+{
+    Impl& d = *d_;
+    if (d.mapped_qkv == d.qkv_recv.p && d.mapped_o == d.o_recv.p)
+        return;
+    d.close_peers();
+    const int P = world_.size, me = world_.rank;
+    cudaIpcMemHandle_t mine[2];
+    H3_CUDA(cudaIpcGetMemHandle(&mine[0], d.qkv_recv.p));
+    H3_CUDA(cudaIpcGetMemHandle(&mine[1], d.o_recv.p));
+    static_assert(sizeof(mine) == 128, "two 64-byte IPC handles");
+    d.ipc_stage.ensure(size_t(P) * 128);
+    d.barrier_word.ensure(16);
+    uint8_t* stage = d.ipc_stage.as<uint8_t>();
+    H3_CUDA(cudaMemcpyAsync(stage + size_t(me) * 128, mine, 128, cudaMemcpyHostToDevice, stream_));
+    H3_NCCL(ncclAllGather(stage + size_t(me) * 128, stage, 128, ncclUint8, d.comm, stream_));
+    std::vector<cudaIpcMemHandle_t> all(2 * size_t(P));
+    H3_CUDA(cudaMemcpyAsync(all.data(), stage, size_t(P) * 128, cudaMemcpyDeviceToHost, stream_));
+    H3_CUDA(cudaStreamSynchronize(stream_));
+    for (int r = 0; r < P; ++r) {
+        if (r == me) {
+            d.peer_qkv[r] = d.qkv_recv.p;
+            d.peer_o[r] = d.o_recv.p;
+            continue;
+        }
+        void* q = nullptr;
+        void* o = nullptr;
+        H3_CUDA(cudaIpcOpenMemHandle(&q, all[2 * r], cudaIpcMemLazyEnablePeerAccess));
+        d.opened.push_back(q);
+        H3_CUDA(cudaIpcOpenMemHandle(&o, all[2 * r + 1], cudaIpcMemLazyEnablePeerAccess));
+        d.opened.push_back(o);
+        d.peer_qkv[r] = q;
+        d.peer_o[r] = o;
+    }
+    d.mapped_qkv = d.qkv_recv.p;
+    d.mapped_o = d.o_recv.p;
 }
 
 void Model::begin(const float* text, int T, const Layout& l)
@@ -583,6 +644,12 @@ void Model::step(const float* video, const float* audio, float t_video, float t_
     grid.nct = (grid.frames + 3) / 4, grid.ncy = (grid.ph + 3) / 4, grid.ncx = (grid.pw + 3) / 4;
     const uint8_t* midx = d_->mod_idx.as<uint8_t>();
     __nv_bfloat16* qkv = d_->qkv.as<__nv_bfloat16>();
+    // With several ranks the Ulysses exchanges are fused into the q/k/v GEMM's and the attention's epilogues
+    // (stores into the peers' receive buffers); a 4-byte all-reduce then serves as the barrier after each.
+    const bool fused = P > 1 && d_->fused;
+    auto barrier = [&]() {
+        H3_NCCL(ncclAllReduce(d_->barrier_word.p, d_->barrier_word.p, 1, ncclInt32, ncclSum, d_->comm, s));
+    };
     for (int bl = 0; bl < L; ++bl) {
         Impl::Block& B = d_->blocks[bl];
         const float* mod = d_->mods.as<float>() + size_t(bl) * U * 18 * d;
@@ -594,6 +661,12 @@ void Model::step(const float* video, const float* audio, float t_video, float t_
         gq.M = M, gq.N = 3 * inner, gq.K = d;
         gq.out = qkv, gq.bias = B.qkv_b.as<float>(), gq.rope = d_->rope.as<float>(), gq.qn_w = B.qn.as<float>(),
         gq.kn_w = B.kn.as<float>(), gq.eps = c_.eps, gq.inner = inner, gq.heads_per_rank = Hp, gq.rows_local = M;
+        if (fused) {
+            // the epilogue stores each head group's rows straight into its owner's receive buffer over NVLink
+            for (int r = 0; r < P; ++r)
+                gq.peer_out[r] = d_->peer_qkv[r];
+            gq.my_rank = world_.rank;
+        }
         if (int8_ & kInt8Qkv) {
             rp.out_kind = RowOut::s8, rp.out = d_->hq.p, rp.ldo = d, rp.out_scale = d_->hs.as<float>();
             rms_mod_rows(rp, s);
@@ -609,7 +682,11 @@ void Model::step(const float* video, const float* audio, float t_video, float t_
         launches_ += 2;
         mark("qkv");
         const __nv_bfloat16* qsrc = qkv;
-        if (P > 1) {
+        if (fused) {
+            barrier(); // every rank's rows have landed in every receive buffer
+            qsrc = d_->qkv_recv.as<__nv_bfloat16>();
+            mark("a2a");
+        } else if (P > 1) {
             const size_t chunk = size_t(M) * 3 * Hp * 128;
             H3_NCCL(ncclGroupStart());
             for (int r = 0; r < P; ++r) {
@@ -624,6 +701,12 @@ void Model::step(const float* video, const float* audio, float t_video, float t_
         ap.q = qsrc, ap.k = qsrc + Hp * 128, ap.v = qsrc + 2 * Hp * 128;
         ap.row_stride = 3 * Hp * 128, ap.heads = Hp, ap.rows = S_;
         ap.out = d_->o.p, ap.out_row_stride = Hp * 128;
+        if (fused) {
+            // the epilogue stores each row's output straight to the rank that owns the row
+            for (int r = 0; r < P; ++r)
+                ap.peer_out[r] = d_->peer_o[r];
+            ap.rows_per_rank = M, ap.my_rank = world_.rank;
+        }
         if (sparse) {
             // coarse pass (cube_pool, cube_scores, cube_topk, pass lists), then the sparse flash kernel
             const SparseBuffers& b = d_->sp;
@@ -644,7 +727,12 @@ void Model::step(const float* video, const float* audio, float t_video, float t_
         const void* oin = d_->o.p;
         GemmParams go;
         go.M = M, go.N = d, go.K = inner;
-        if (P > 1) {
+        if (fused) {
+            barrier(); // every rank's head outputs for this rank's rows have landed
+            oin = d_->o_recv.p;
+            go.a_chunks = P, go.lda = Hp * 128, go.a_rows_stride = M;
+            mark("a2a");
+        } else if (P > 1) {
             const size_t chunk = size_t(M) * Hp * 128;
             H3_NCCL(ncclGroupStart());
             for (int r = 0; r < P; ++r) {

@@ -107,6 +107,7 @@ private:
     std::vector<std::pair<std::string, float>> stage_ms_;
     bool begun_ = false;
     void alloc_activations();
+    void map_peers(); // the ranks' receive buffers, mapped into every rank (sequence-parallel, fused exchange)
     void emit_probe(const char* name, int layer, const float* dev, size_t n);
 };
 

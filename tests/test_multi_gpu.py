@@ -26,7 +26,8 @@ def _inputs():
     return H, lay, text, video, audio
 
 
-def _rank(rank, world, nccl_id, sparse, q):
+def _rank(rank, world, nccl_id, sparse, q, exchange="fused"):
+    os.environ["H3_EXCHANGE"] = exchange
     H, lay, text, video, audio = _inputs()
     torch.cuda.set_device(rank)
     m = H.Model(CFG, seed=1, rank=rank, world=world, nccl_id=nccl_id, device=rank, sparse_ratio=sparse, sparse_local=1)
@@ -37,15 +38,17 @@ def _rank(rank, world, nccl_id, sparse, q):
     q.put((rank, v, a, v2, a2))
 
 
+@pytest.mark.parametrize("exchange", ["fused", "nccl"])
 @pytest.mark.parametrize("sparse", [0.0, 0.5])
-def test_two_rank_step_matches_one_rank(cuda, sparse):
+def test_two_rank_step_matches_one_rank(cuda, sparse, exchange):
+    """exchange: fused = the epilogues store into the peers' buffers over NVLink; nccl = NCCL all-to-alls."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     ctx = mp.get_context("spawn")
     H, *_ = _inputs()
     nccl_id = H.nccl_unique_id()
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, 2, nccl_id, sparse, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, 2, nccl_id, sparse, q, exchange)) for r in range(2)]
     for p in procs:
         p.start()
     res = {}
