@@ -117,12 +117,13 @@ __device__ __forceinline__ int4 implicit_entry(int j, const CubeGrid& g)
 // P_t(j) and rescale O_t.
 constexpr int A2_SPLIT = 1;        // warps sharing a query row in the softmax (2 measured no faster)
 constexpr int NT2 = 64 + 256 * A2_SPLIT;
-constexpr int A2_OFF_Q = 0;        // Q0, Q1
-constexpr int A2_OFF_K = 2 * TILE; // 2 stages
-constexpr int A2_OFF_V = 4 * TILE; // 2 stages
-constexpr int A2_OFF_BAR = 6 * TILE;
-constexpr int A2_OFF_RED = 6 * TILE + 256; // row maxima and sums exchanged between a row's warps
-constexpr int A2_SMEM = 6 * TILE + 256 + 2 * 3 * 4 * 128 * 4 + 1024;
+constexpr int A2_KST = 3, A2_VST = 2; // K is freed once both S MMAs read it, V after both PV MMAs
+constexpr int A2_OFF_Q = 0;           // Q0, Q1
+constexpr int A2_OFF_K = 2 * TILE;
+constexpr int A2_OFF_V = A2_OFF_K + A2_KST * TILE;
+constexpr int A2_OFF_BAR = A2_OFF_V + A2_VST * TILE;
+constexpr int A2_OFF_RED = A2_OFF_BAR + 256; // row maxima and sums exchanged between a row's warps
+constexpr int A2_SMEM = A2_OFF_RED + (A2_SPLIT > 1 ? 2 * 3 * A2_SPLIT * 128 * 4 : 0) + 1024;
 
 template <int SPLIT>
 __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid_constant__ Maps maps, const AttnParams p)
@@ -132,15 +133,16 @@ __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid
     uint8_t* smem = smem_raw + (((raw + 1023) & ~1023u) - raw);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + A2_OFF_BAR);
     uint64_t* q_full = bars + 0;
-    uint64_t* k_full = bars + 1;   // [2]
-    uint64_t* v_full = bars + 3;   // [2]
-    uint64_t* kv_empty = bars + 5; // [2]
-    uint64_t* s_full = bars + 7;   // [2] per tile
-    uint64_t* p_full = bars + 9;   // [2] per tile
-    uint64_t* pv_done = bars + 11; // [2] per tile
-    uint64_t* drain = bars + 13;
-    uint64_t* xchg = bars + 14;    // [2] per tile: the row-maximum / row-sum exchange between a row's warps
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+    uint64_t* k_full = bars + 1;          // [A2_KST]
+    uint64_t* k_empty = k_full + A2_KST;  // [A2_KST]
+    uint64_t* v_full = k_empty + A2_KST;  // [A2_VST]
+    uint64_t* v_empty = v_full + A2_VST;  // [A2_VST]
+    uint64_t* s_full = v_empty + A2_VST;  // [2] per tile
+    uint64_t* p_full = s_full + 2;        // [2] per tile
+    uint64_t* pv_done = p_full + 2;       // [2] per tile
+    uint64_t* drain = pv_done + 2;
+    uint64_t* xchg = drain + 1;           // [2] per tile: the row-maximum / row-sum exchange between a row's warps
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xchg + 2);
 
     const int warp = warp_id();
     const int pair = blockIdx.x, head = blockIdx.y;
@@ -149,10 +151,15 @@ __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < A2_KST; ++i) {
             mbar_init(&k_full[i], 1);
+            mbar_init(&k_empty[i], 1);
+        }
+        for (int i = 0; i < A2_VST; ++i) {
             mbar_init(&v_full[i], 1);
-            mbar_init(&kv_empty[i], 1);
+            mbar_init(&v_empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
             mbar_init(&s_full[i], 1);
             mbar_init(&p_full[i], 4 * SPLIT);
             mbar_init(&pv_done[i], 1);
@@ -175,37 +182,53 @@ __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid
         mbar_arrive_expect_tx(q_full, 2 * TILE);
         for (int u = 0; u < 4; ++u)
             load_unit<false>(smem + A2_OFF_Q + (u >> 1) * TILE, u & 1, 4 * pair + u, head, &maps.q, &maps.cq, g, q_full);
-        for (int j = 0; j < nkv; ++j) {
-            const int s = j & 1;
-            if (!mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1))
-                break;
-            mbar_arrive_expect_tx(&k_full[s], TILE);
-            load_unit<false>(smem + A2_OFF_K + s * TILE, 0, 2 * j, head, &maps.k, &maps.ck, g, &k_full[s]);
-            load_unit<false>(smem + A2_OFF_K + s * TILE, 1, 2 * j + 1, head, &maps.k, &maps.ck, g, &k_full[s]);
-            mbar_arrive_expect_tx(&v_full[s], TILE);
-            load_unit<false>(smem + A2_OFF_V + s * TILE, 0, 2 * j, head, &maps.v, &maps.cv, g, &v_full[s]);
-            load_unit<false>(smem + A2_OFF_V + s * TILE, 1, 2 * j + 1, head, &maps.v, &maps.cv, g, &v_full[s]);
+        // K runs ahead of V by up to the depth of its ring
+        int jk = 0, jv = 0;
+        while (jv < nkv) {
+            if (jk < nkv && jk < jv + A2_KST) {
+                const int s = jk % A2_KST;
+                if (!mbar_wait(&k_empty[s], ((jk / A2_KST) & 1) ^ 1))
+                    break;
+                mbar_arrive_expect_tx(&k_full[s], TILE);
+                load_unit<false>(smem + A2_OFF_K + s * TILE, 0, 2 * jk, head, &maps.k, &maps.ck, g, &k_full[s]);
+                load_unit<false>(smem + A2_OFF_K + s * TILE, 1, 2 * jk + 1, head, &maps.k, &maps.ck, g, &k_full[s]);
+                ++jk;
+            } else {
+                const int s = jv % A2_VST;
+                if (!mbar_wait(&v_empty[s], ((jv / A2_VST) & 1) ^ 1))
+                    break;
+                mbar_arrive_expect_tx(&v_full[s], TILE);
+                load_unit<false>(smem + A2_OFF_V + s * TILE, 0, 2 * jv, head, &maps.v, &maps.cv, g, &v_full[s]);
+                load_unit<false>(smem + A2_OFF_V + s * TILE, 1, 2 * jv + 1, head, &maps.v, &maps.cv, g, &v_full[s]);
+                ++jv;
+            }
         }
     } else if (warp == 1 && elect_one_lane()) {
         // ------------------------------------------------------------------------------------------ MMA
         const uint32_t id_s = idesc_bf16(128, 128);
         const uint32_t id_pv = idesc_bf16(128, 128, false, true);
         auto issue_s = [&](int t, int j) {
+            const int ks = j % A2_KST;
             const uint32_t sq = smem_u32(smem + A2_OFF_Q + t * TILE);
-            const uint32_t sk = smem_u32(smem + A2_OFF_K + (j & 1) * TILE);
+            const uint32_t sk = smem_u32(smem + A2_OFF_K + ks * TILE);
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk) {
                 const uint32_t off = (kk >> 2) * HALF + (kk & 3) * 32;
                 mma_bf16_ss(tmem + t * 128, sdesc_sw128(sq + off, 16, 1024), sdesc_sw128(sk + off, 16, 1024), id_s, kk > 0);
             }
             mma_commit(&s_full[t]);
+            if (t == 1)
+                mma_commit(&k_empty[ks]); // both tiles' S MMAs have read K_j
         };
         auto issue_pv = [&](int t, int j) {
-            const uint32_t sv = smem_u32(smem + A2_OFF_V + (j & 1) * TILE);
+            const int vs = j % A2_VST;
+            const uint32_t sv = smem_u32(smem + A2_OFF_V + vs * TILE);
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk)
                 mma_bf16_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8, sdesc_sw128(sv + kk * 2048, HALF, 1024), id_pv, (j | kk) != 0);
             mma_commit(&pv_done[t]);
+            if (t == 1)
+                mma_commit(&v_empty[vs]); // both tiles' PV MMAs have read V_j
         };
         bool ok = mbar_wait(q_full, 0) && mbar_wait(&k_full[0], 0);
         if (ok) {
@@ -214,13 +237,13 @@ __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid
             issue_s(1, 0);
         }
         for (int j = 0; j < nkv && ok; ++j) {
-            if (!(ok = mbar_wait(&v_full[j & 1], (j >> 1) & 1) && mbar_wait(&p_full[0], j & 1)))
+            if (!(ok = mbar_wait(&v_full[j % A2_VST], (j / A2_VST) & 1) && mbar_wait(&p_full[0], j & 1)))
                 break;
             tc_fence_after();
             issue_pv(0, j);
             const bool more = j + 1 < nkv;
             if (more) {
-                if (!(ok = mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1)))
+                if (!(ok = mbar_wait(&k_full[(j + 1) % A2_KST], ((j + 1) / A2_KST) & 1)))
                     break;
                 tc_fence_after();
                 issue_s(0, j + 1);
@@ -229,7 +252,6 @@ __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid
                 break;
             tc_fence_after();
             issue_pv(1, j);
-            mma_commit(&kv_empty[j & 1]);
             if (more)
                 issue_s(1, j + 1);
         }
