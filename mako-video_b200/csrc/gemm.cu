@@ -28,13 +28,34 @@ constexpr int STAGES = 4;
 constexpr int GROUP_M = 16;
 constexpr int NUM_THREADS = 192;  // 6 warps
 
-template <int BN>
+template <int BN, Epi EPI>
 struct Smem {
     static constexpr int A_BYTES = BM * KBYTES;
     static constexpr int B_BYTES = BN * KBYTES;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int TOTAL = STAGES * STAGE_BYTES + 1024 /* alignment slack */ + 256 /* barriers */;
+    // the q/k/v epilogue stages one head tile (128 rows x 128 dims bf16, two 128-byte-swizzled halves) for TMA
+    static constexpr int STAGING = EPI == Epi::qkv ? BM * 256 : 0;
+    static constexpr int TOTAL = STAGES * STAGE_BYTES + STAGING + 1024 /* alignment slack */ + 256 /* barriers */;
 };
+
+// Destination tensor maps of the q/k/v epilogue, one per rank that owns heads: (dim, q/k/v x head slot, row) over
+// that rank's block of this rank's rows, in its receive buffer (fused exchange) or in this rank's send layout.
+struct OutMaps {
+    CUtensorMap m[8];
+};
+
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); } // the 4 epilogue warps
+
+__device__ __forceinline__ void tma_store_3d(const void* tmap, const void* smem_src, int32_t c0, int32_t c1, int32_t c2)
+{
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(tmap)),
+                 "r"(smem_u32(smem_src)), "r"(c0), "r"(c1), "r"(c2)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& tm, int& tn)
 {
@@ -80,7 +101,7 @@ __device__ __forceinline__ void load_acc(uint32_t taddr, int col0, float* v, flo
 }
 
 template <int BN, Epi EPI, bool IS_I8>
-__device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tacc, int m0, int n0)
+__device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tacc, int m0, int n0, uint8_t* stage, const OutMaps* om)
 {
     const int quarter = warp_id() & 3;
     const int row = quarter * 32 + lane_id();
@@ -91,14 +112,14 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tacc
     const float* bsc = IS_I8 ? p.b_scale + n0 : nullptr;
 
     if constexpr (EPI == Epi::qkv) {
-        // BN = 256 covers two heads; the q/k/v section never changes inside a tile (inner % 256 == 0).
+        // BN = 256 covers two heads; the q/k/v section never changes inside a tile (inner % 256 == 0). Every epilogue
+        // thread takes part in each head (the staging barriers), rows past M included (their stores are clipped).
         const int sec = n0 / p.inner;
+        const int grow = valid ? gm : p.M - 1; // rows past M read a valid row's rotary entry
 #pragma unroll 1
         for (int hh = 0; hh < BN / 128; ++hh) {
             float v[128];
             load_acc<IS_I8, 4>(taddr, hh * 128, v, a_scale, IS_I8 ? bsc + hh * 128 : nullptr);
-            if (!valid)
-                continue;
             const int col = n0 + hh * 128;
             if (p.bias) {
                 const float4* b4 = reinterpret_cast<const float4*>(p.bias + col);
@@ -118,7 +139,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tacc
 #pragma unroll
                 for (int i = 0; i < 128; ++i)
                     v[i] = v[i] * rinv * __ldg(w + i);
-                const float2* cs = reinterpret_cast<const float2*>(p.rope) + size_t(gm) * 48;
+                const float2* cs = reinterpret_cast<const float2*>(p.rope) + size_t(grow) * 48;
 #pragma unroll
                 for (int j = 0; j < 48; ++j) {
                     const float2 t = __ldg(cs + j);
@@ -129,14 +150,26 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tacc
             }
             const int head = (col % p.inner) / 128;
             const int rank = head / p.heads_per_rank, hl = head % p.heads_per_rank;
-            // Into the head group's owner: straight into its receive buffer (block my_rank of the sequence) when a
-            // peer pointer is given, else into this rank's send layout (block `rank`).
-            __nv_bfloat16* base = reinterpret_cast<__nv_bfloat16*>(p.peer_out[rank] ? p.peer_out[rank] : p.out);
-            const size_t rowpos = size_t(p.peer_out[rank] ? p.my_rank : rank) * p.rows_local + gm;
-            __nv_bfloat16* dst = base + (rowpos * 3 + sec) * size_t(p.heads_per_rank) * 128 + hl * 128;
+            // Stage the head tile in shared memory (once the previous head's store has read it) and let TMA store it
+            // into the head group's owner: its receive buffer over NVLink (fused exchange) or this rank's send layout.
+            if (threadIdx.x == 64)
+                bulk_wait_read0();
+            epi_bar();
 #pragma unroll
-            for (int c = 0; c < 4; ++c)
-                store_bf16x32(dst + c * 32, v + c * 32);
+            for (int c8 = 0; c8 < 16; ++c8) {
+                const int half = c8 >> 3, c = c8 & 7;
+                const uint4 w = make_uint4(pack_bf16x2(v[c8 * 8 + 0], v[c8 * 8 + 1]), pack_bf16x2(v[c8 * 8 + 2], v[c8 * 8 + 3]),
+                                           pack_bf16x2(v[c8 * 8 + 4], v[c8 * 8 + 5]), pack_bf16x2(v[c8 * 8 + 6], v[c8 * 8 + 7]));
+                *reinterpret_cast<uint4*>(stage + half * (BM * 128) + row * 128 + ((c ^ (row & 7)) << 4)) = w;
+            }
+            fence_proxy_async_smem();
+            epi_bar();
+            if (threadIdx.x == 64) {
+                const int slot = sec * p.heads_per_rank + hl;
+                tma_store_3d(&om->m[rank], stage, 0, slot, m0);
+                tma_store_3d(&om->m[rank], stage + BM * 128, 64, slot, m0);
+                bulk_commit();
+            }
         }
     } else if constexpr (EPI == Epi::swiglu) {
         // Gate columns [0,128) and value columns [128,256) of the tile pair up; 128 outputs per tile.
@@ -213,13 +246,15 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tacc
 
 template <int BN, Epi EPI, bool IS_I8>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmParams p)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmParams p,
+                const __grid_constant__ OutMaps om)
 {
-    using SM = Smem<BN>;
+    using SM = Smem<BN, EPI>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t* smem = smem_raw + (((raw + 1023) & ~1023u) - raw);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * SM::STAGE_BYTES);
+    uint8_t* stage = smem + STAGES * SM::STAGE_BYTES; // q/k/v epilogue staging (1024-aligned)
+    uint64_t* bars = reinterpret_cast<uint64_t*>(stage + SM::STAGING);
     uint64_t* full = bars;                 // [STAGES]
     uint64_t* empty = bars + STAGES;       // [STAGES]
     uint64_t* tfull = bars + 2 * STAGES;   // [2]
@@ -327,14 +362,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tc_fence_after();
             int tm, tn;
             tile_coords(tile, tiles_m, tiles_n, tm, tn);
-            epilogue_tile<BN, EPI, IS_I8>(p, tmem_base + acc * BN, tm * BM, tn * BN);
+            epilogue_tile<BN, EPI, IS_I8>(p, tmem_base + acc * BN, tm * BM, tn * BN, stage, &om);
             tc_fence_before();
             __syncwarp();
             if (elect_one_lane())
                 mbar_arrive(&tempty[acc]);
         }
-        if (p.peer_out[0])
-            __threadfence_system(); // this thread's NVLink stores are performed before the kernel ends
+        if (EPI == Epi::qkv && threadIdx.x == 64)
+            bulk_wait0(); // the head tiles' TMA stores are complete
     }
     tc_fence_before();
     __syncthreads();
@@ -363,14 +398,28 @@ void launch(const void* A, const void* B, const GemmParams& p, cudaStream_t s)
     const uint32_t bbox[2] = {uint32_t(kelems), uint32_t(BN)};
     const CUtensorMap tb = make_tmap(dt, 2, B, bdims, bstr, bbox);
     static bool attr_set = false;
-    const int smem = Smem<BN>::TOTAL;
+    const int smem = Smem<BN, EPI>::TOTAL;
     if (!attr_set) {
         H3_CUDA(cudaFuncSetAttribute(gemm_kernel<BN, EPI, IS_I8>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         attr_set = true;
     }
     const int tiles = ((p.M + BM - 1) / BM) * (p.N / BN);
     const int grid = std::min(tiles, num_sms());
-    gemm_kernel<BN, EPI, IS_I8><<<grid, NUM_THREADS, smem, s>>>(ta, tb, p);
+    OutMaps om{};
+    if constexpr (EPI == Epi::qkv) {
+        // rank r's block of this rank's rows: in r's receive buffer (fused exchange) or in this rank's send layout
+        const int P = p.inner / 128 / p.heads_per_rank;
+        const uint64_t slots = 3 * uint64_t(p.heads_per_rank);
+        const uint64_t odims[3] = {128, slots, uint64_t(p.rows_local)};
+        const uint64_t ostr[2] = {256, slots * 256};
+        const uint32_t obox[3] = {64, 1, 128};
+        for (int r = 0; r < P; ++r) {
+            const size_t block = size_t(p.peer_out[r] ? p.my_rank : r) * p.rows_local * slots * 128;
+            const __nv_bfloat16* base = static_cast<const __nv_bfloat16*>(p.peer_out[r] ? p.peer_out[r] : p.out) + block;
+            om.m[r] = make_tmap(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, odims, ostr, obox);
+        }
+    }
+    gemm_kernel<BN, EPI, IS_I8><<<grid, NUM_THREADS, smem, s>>>(ta, tb, p, om);
     H3_CUDA(cudaGetLastError());
 }
 
@@ -385,8 +434,13 @@ void check_shape(const GemmParams& p, Epi epi, int bn, bool i8)
         throw std::runtime_error("gemm: chunked A needs chunk widths that are multiples of the K tile");
     if ((p.K * (i8 ? 1 : 2)) % 16)
         throw std::runtime_error("gemm: K rows must be 16-byte multiples");
-    if (epi == Epi::qkv && (p.inner % 256 || !p.rope || !p.qn_w || !p.kn_w || p.heads_per_rank <= 0))
+    if (epi == Epi::qkv && (p.inner % 256 || !p.rope || !p.qn_w || !p.kn_w || p.heads_per_rank <= 0 ||
+                            (p.inner / 128) % p.heads_per_rank || p.inner / 128 / p.heads_per_rank > 8 || p.rows_local < p.M))
         throw std::runtime_error("gemm: qkv epilogue arguments");
+    if (epi == Epi::qkv)
+        for (int r = 0; r < p.inner / 128 / p.heads_per_rank; ++r)
+            if (!p.peer_out[r] && !p.out)
+                throw std::runtime_error("gemm: qkv epilogue needs an output for every head group");
     if (epi == Epi::gate_resid && (!p.x || !p.mod || !p.mod_idx))
         throw std::runtime_error("gemm: gate_resid epilogue arguments");
     if (epi == Epi::s32 && !i8)
