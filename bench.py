@@ -41,6 +41,15 @@ WORKLOADS = {
 }
 
 
+
+_json_out = None
+
+
+def emit(line):
+    out = _json_out if _json_out is not None else sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
 def load_traffic(kernel, workload):
     """DRAM bytes per launch of the dominant kernel from the committed ncu summary (null when not captured)."""
     p = os.path.join(REPO, "profiles", "traffic.json")
@@ -211,7 +220,7 @@ def run_reference(args, rank, world):
             "config": {"workload": wdesc, "rows": S, "dim": cfg["dim"], "heads": cfg["heads"], "blocks": cfg["blocks"]},
             "cpu_baseline": {"value": value, "unit": "s", "cores": threads, "kind": "port", "sample": desc},
             "e2e": {"value": value, "unit": "s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def run_ours(args, rank, world, local_rank):
@@ -346,7 +355,7 @@ def run_ours(args, rank, world, local_rank):
         v, desc, spent = cpu_sample(cfg, S)
         line["cpu_baseline"] = {"value": v, "unit": "s", "cores": os.cpu_count(), "kind": "port", "sample": desc,
                                 "sample_seconds": spent}
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def main():
@@ -363,9 +372,12 @@ def main():
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
-    if "NCCL_DEBUG_FILE" not in os.environ:
-        # NCCL's own messages (its version banner included) go to a file: the JSON line is rank 0's only stdout
-        os.environ["NCCL_DEBUG_FILE"] = os.path.join(tempfile.gettempdir(), f"h3_nccl.{os.getpid()}.log")
+    # The JSON line is the only thing on stdout: everything else written to file descriptor 1 (NCCL's version banner
+    # and other native messages included) goes to stderr.
+    global _json_out
+    _json_out = os.fdopen(os.dup(1), "w")
+    sys.stdout.flush()
+    os.dup2(2, 1)
     if args.impl == "reference":
         run_reference(args, rank, world)
         return

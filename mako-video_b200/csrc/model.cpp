@@ -746,9 +746,9 @@ void Model::step(const float* video, const float* audio, float t_video, float t_
         }
         go.x = x, go.ldx = d, go.bias = B.out_b.as<float>(), go.mod = mod, go.mod_idx = midx, go.gate_slot = 2, go.dim = d;
         if (int8_ & kInt8Out) {
-            if (P > 1)
-                throw CudaError("int8 out projection with sequence parallelism is not supported");
-            quant_rows_i8(oin, inner, M, inner, d_->hq.as<int8_t>(), d_->hs.as<float>(), s);
+            // quantised per row (across the chunks of every rank's heads), written as dense int8 rows
+            quant_rows_i8_chunked(oin, M, inner, go.a_chunks, M, d_->hq.as<int8_t>(), d_->hs.as<float>(), s);
+            go.a_chunks = 1, go.lda = 0, go.a_rows_stride = 0;
             go.a_scale = d_->hs.as<float>(), go.b_scale = B.out_s.as<float>();
             gemm_s8(d_->hq.p, B.out_q.p, go, Epi::gate_resid, s);
             launches_ += 2;

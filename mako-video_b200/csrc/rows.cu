@@ -175,15 +175,18 @@ __global__ void swiglu_kernel(const __nv_bfloat16* gv, int rows, int F, __nv_bfl
     }
 }
 
-// One CTA (256 threads) per row; two passes over the row (the second from L1/L2).
-__global__ void __launch_bounds__(256) quant_rows_kernel(const __nv_bfloat16* x, int64_t ldx, int K, int8_t* q, float* scale)
+// One CTA (256 threads) per row; two passes over the row (the second from L1/L2). The row may be split into column
+// chunks of Kc elements stored one after another (element k at x + (k / Kc) * chunk_stride + r * ldx + k % Kc), the
+// layout the out projection's input has after the sequence-parallel exchange.
+__global__ void __launch_bounds__(256) quant_rows_kernel(const __nv_bfloat16* x, int64_t ldx, int K, int Kc, int64_t chunk_stride,
+                                                         int8_t* q, float* scale)
 {
     __shared__ float red[8];
     const int r = blockIdx.x;
-    const __nv_bfloat16* xr = x + size_t(r) * ldx;
+    auto at = [&](int c) { return x + (c / Kc) * chunk_stride + size_t(r) * ldx + (c % Kc); };
     float amax = 0.f;
     for (int c = threadIdx.x * 8; c < K; c += 256 * 8) {
-        const uint4 v = *reinterpret_cast<const uint4*>(xr + c);
+        const uint4 v = *reinterpret_cast<const uint4*>(at(c));
         const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&v);
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
@@ -196,7 +199,7 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __nv_bfloat16* x,
     if (threadIdx.x == 0)
         scale[r] = amax / 127.0f;
     for (int c = threadIdx.x * 8; c < K; c += 256 * 8) {
-        const uint4 v = *reinterpret_cast<const uint4*>(xr + c);
+        const uint4 v = *reinterpret_cast<const uint4*>(at(c));
         const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&v);
         signed char o[8];
 #pragma unroll
@@ -368,7 +371,18 @@ void quant_rows_i8(const void* x, int64_t ldx, int rows, int K, int8_t* q, float
         throw CudaError("quant_rows_i8: K must be a multiple of 8");
     if (!rows)
         return;
-    quant_rows_kernel<<<rows, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), ldx, K, q, scale);
+    quant_rows_kernel<<<rows, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), ldx, K, K, 0, q, scale);
+    H3_CUDA(cudaGetLastError());
+}
+
+void quant_rows_i8_chunked(const void* x, int rows, int K, int chunks, int rows_stride, int8_t* q, float* scale, cudaStream_t s)
+{
+    const int Kc = K / chunks;
+    if (K % chunks || Kc % 8 || rows_stride < rows)
+        throw CudaError("quant_rows_i8_chunked: chunk widths must be multiples of 8");
+    if (!rows)
+        return;
+    quant_rows_kernel<<<rows, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), Kc, K, Kc, int64_t(rows_stride) * Kc, q, scale);
     H3_CUDA(cudaGetLastError());
 }
 

@@ -36,6 +36,9 @@ void swiglu_rows(const void* gv_bf16, int rows, int F, void* out_bf16, cudaStrea
 
 // Symmetric per-row int8: scale = max|x| / 127, q = rint(x * (127 / max|x|)) clamped to +-127 (0 for a zero row).
 void quant_rows_i8(const void* x_bf16, int64_t ldx, int rows, int K, int8_t* q, float* scale, cudaStream_t s);
+// The same for rows split into `chunks` column chunks stored one after another ([chunks][rows_stride][K / chunks]);
+// q is written as dense [rows][K].
+void quant_rows_i8_chunked(const void* x_bf16, int rows, int K, int chunks, int rows_stride, int8_t* q, float* scale, cudaStream_t s);
 
 // The standalone heads_partial: per-head RMS norm (weights qn/kn) and rotary of q and k inside a
 // [rows][3][heads][128] bf16 tensor, in place; v untouched.

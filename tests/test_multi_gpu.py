@@ -26,11 +26,12 @@ def _inputs():
     return H, lay, text, video, audio
 
 
-def _rank(rank, world, nccl_id, sparse, q, exchange="fused"):
+def _rank(rank, world, nccl_id, sparse, q, exchange="fused", int8_mask=0):
     os.environ["H3_EXCHANGE"] = exchange
     H, lay, text, video, audio = _inputs()
     torch.cuda.set_device(rank)
-    m = H.Model(CFG, seed=1, rank=rank, world=world, nccl_id=nccl_id, device=rank, sparse_ratio=sparse, sparse_local=1)
+    m = H.Model(CFG, seed=1, rank=rank, world=world, nccl_id=nccl_id, device=rank, sparse_ratio=sparse, sparse_local=1,
+                int8_mask=int8_mask)
     m.begin(text, lay)
     v, a = m.step(video, audio, 0.7, 0.4)
     v2, a2 = m.step(video, audio, 0.3, 0.2)
@@ -38,17 +39,14 @@ def _rank(rank, world, nccl_id, sparse, q, exchange="fused"):
     q.put((rank, v, a, v2, a2))
 
 
-@pytest.mark.parametrize("exchange", ["fused", "nccl"])
-@pytest.mark.parametrize("sparse", [0.0, 0.5])
-def test_two_rank_step_matches_one_rank(cuda, sparse, exchange):
-    """exchange: fused = the epilogues store into the peers' buffers over NVLink; nccl = NCCL all-to-alls."""
+def _compare_two_ranks_with_one(sparse, exchange, int8_mask=0):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     ctx = mp.get_context("spawn")
     H, *_ = _inputs()
     nccl_id = H.nccl_unique_id()
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, 2, nccl_id, sparse, q, exchange)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, 2, nccl_id, sparse, q, exchange, int8_mask)) for r in range(2)]
     for p in procs:
         p.start()
     res = {}
@@ -58,7 +56,7 @@ def test_two_rank_step_matches_one_rank(cuda, sparse, exchange):
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    one = ctx.Process(target=_rank, args=(0, 1, None, sparse, q))
+    one = ctx.Process(target=_rank, args=(0, 1, None, sparse, q, exchange, int8_mask))
     one.start()
     ref = q.get(timeout=300)[1:]
     one.join(timeout=120)
@@ -66,3 +64,18 @@ def test_two_rank_step_matches_one_rank(cuda, sparse, exchange):
         for got, want in zip(res[rank], ref):
             rel = np.linalg.norm(got - want) / max(np.linalg.norm(want), 1e-30)
             assert rel < 1e-5, (rank, rel)
+
+
+@pytest.mark.parametrize("exchange", ["fused", "nccl"])
+@pytest.mark.parametrize("sparse", [0.0, 0.5])
+def test_two_rank_step_matches_one_rank(cuda, sparse, exchange):
+    """exchange: fused = the epilogues store into the peers' buffers over NVLink; nccl = NCCL all-to-alls."""
+    _compare_two_ranks_with_one(sparse, exchange)
+
+
+@pytest.mark.parametrize("exchange", ["fused", "nccl"])
+def test_two_rank_int8_step_matches_one_rank(cuda, exchange):
+    """W8A8 on every projection: the out projection's input arrives in per-rank column chunks and is quantised per
+    row across them, so the int8 rows (and the step) equal the single-rank ones."""
+    H, *_ = _inputs()
+    _compare_two_ranks_with_one(0.0, exchange, int8_mask=H.INT8_QKV | H.INT8_OUT | H.INT8_FC1 | H.INT8_FC2)
