@@ -172,10 +172,17 @@ int h3k_attention(const void* q, const void* k, const void* v, int64_t row_strid
                   int64_t out_row_stride, void* stream);
 
 /* The sparse attention's cube grid: dense_rows rows (text, keyframe, audio) then frames x ph x pw generated video
- * rows (a row is a 2x2 patch), cut into 4x4x4 cubes with the grid padded to multiples of 4. */
+ * rows (a row is a 2x2 patch), cut into 4x4x4 cubes (cubes at the far edges cut short). The h3k_sparse_* calls take
+ * q, k, v and write out in the packed row order: the dense rows, then the generated video rows cube by cube (cubes
+ * in (frame group, row group, column group) order, each cube's rows in (frame, row, column) order), which is the
+ * order the step keeps its rows in. (The reference's sparse kernels gather a cube's rows through a row map instead,
+ * h3.hpp Cubes per its arch.md:121-124; the packed order makes every cube one run of rows.) */
 typedef struct h3k_cube_grid {
     int32_t dense_rows, frames, ph, pw;
 } h3k_cube_grid;
+/* The packed order of the generated video rows: src[i] = (f * ph + y) * pw + x of packed video row i (the row
+ * dense_rows + i), for i < frames * ph * pw. No counterpart in the reference. */
+int h3k_video_order(const h3k_cube_grid* g, int32_t* src);
 /* Sizes for a grid: cubes, kcap (selected cubes per query cube at most), q_tiles, max_blocks. */
 int h3k_sparse_sizes(const h3k_cube_grid* g, float ratio, int32_t local, int32_t* cubes, int32_t* kcap, int32_t* q_tiles,
                      int32_t* max_blocks);

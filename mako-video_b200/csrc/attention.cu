@@ -6,9 +6,9 @@
 //                 tiles so one tile's MMAs overlap the other tile's softmax.
 //   attn3_kernel  sparse (and usable dense): one query tile per CTA with two S buffers, so S_{j+1} is computed while
 //                 the softmax works on S_j; query tiles carry their own key lists.
-// Every tile is four 64x64 TMA boxes (two 64-row units x two 64-dim halves), so the same loads serve the dense
-// layout (units of 64 consecutive rows) and the sparse one (a unit is a 4x4x4 latent cube read straight from the
-// model-ordered rows by a 5-D tensor map, the grid's padding zero-filled, or 64 dense rows).
+// Every tile is four 64x64 TMA boxes (two 64-row units x two 64-dim halves) of consecutive rows: in the packed row
+// order each 4x4x4 latent cube is one run of rows, so a sparse unit is the same plain box as a dense one (the rows
+// past a cut-short cube's count belong to the next unit and are masked).
 #include "attention.cuh"
 #include "common.hpp"
 #include "ptx.cuh"
@@ -24,51 +24,16 @@ constexpr int TILE = 32768; // 128 rows x 128 dims
 constexpr float kRescaleThreshold = 8.0f; // log2 units
 
 struct Maps {
-    CUtensorMap q, k, v;    // dense rows: (dim, head, row), box 64 x 1 x 64
-    CUtensorMap cq, ck, cv; // cubes: (dim, head, x, y, frame), box 64 x 1 x 4 x 4 x 4
+    CUtensorMap q, k, v; // (dim, head, row), box 64 x 1 x 64
 };
 
-// Issue the TMA loads of one 64-row unit into rows [64 * half, 64 * half + 64) of a 128-row tile (both dim halves).
-template <bool SPARSE>
-__device__ __forceinline__ void load_unit(uint8_t* tile, int half, int unit, int head, const CUtensorMap* dense, const CUtensorMap* cube,
-                                          const CubeGrid& g, uint64_t* bar)
+// Issue the TMA loads of the 64 rows from `row` into rows [64 * half, 64 * half + 64) of a 128-row tile (both dim
+// halves). Rows past the tensor read as zeros.
+__device__ __forceinline__ void load_rows(uint8_t* tile, int half, int row, int head, const CUtensorMap* map, uint64_t* bar)
 {
 #pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-        uint8_t* dst = tile + hh * HALF + half * 8192;
-        if (!SPARSE) {
-            tma_load_3d(dst, dense, bar, hh * 64, head, unit * 64);
-        } else if (unit < g.cubes()) {
-            const int cx = unit % g.ncx, cy = (unit / g.ncx) % g.ncy, ct = unit / (g.ncx * g.ncy);
-            tma_load_5d(dst, cube, bar, hh * 64, head, 4 * cx, 4 * cy, 4 * ct);
-        } else {
-            tma_load_3d(dst, dense, bar, hh * 64, head, (unit - g.cubes()) * 64);
-        }
-    }
-}
-
-// Valid key rows of a unit as a 64-bit mask (bit kr: row kr of the unit is a token).
-__device__ __forceinline__ uint64_t unit_valid_mask(int unit, const CubeGrid& g)
-{
-    if (unit < 0)
-        return 0;
-    if (unit < g.cubes()) {
-        const int cx = unit % g.ncx, cy = (unit / g.ncx) % g.ncy, ct = unit / (g.ncx * g.ncy);
-        const int nx = min(4, g.pw - 4 * cx), ny = min(4, g.ph - 4 * cy), nf = min(4, g.frames - 4 * ct);
-        if (nx == 4 && ny == 4 && nf == 4)
-            return ~0ull;
-        const uint64_t xm = (1ull << nx) - 1;                         // within one 4-row run
-        uint64_t ym = 0;
-        for (int y = 0; y < ny; ++y)
-            ym |= xm << (4 * y);                                      // within one 16-row frame slice
-        uint64_t m = 0;
-        for (int f = 0; f < nf; ++f)
-            m |= ym << (16 * f);
-        return m;
-    }
-    const int first = (unit - g.cubes()) * 64;
-    const int n = min(64, g.dense_rows - first);
-    return n >= 64 ? ~0ull : (n <= 0 ? 0ull : ((1ull << n) - 1));
+    for (int hh = 0; hh < 2; ++hh)
+        tma_load_3d(tile + hh * HALF + half * 8192, map, bar, hh * 64, head, row);
 }
 
 // Where query row `row`'s output (head `head`, dims from `d0`) goes: this rank's buffer, or straight to the row's
@@ -85,23 +50,21 @@ __device__ __forceinline__ __nv_bfloat16* out_ptr(const AttnParams& p, int row, 
            (size_t(p.my_rank) * p.rows_per_rank + local) * (size_t(p.heads) * 128) + head * 128 + d0;
 }
 
-// The model row of row `r` (0..63) of a unit, or -1 when it is padding.
-__device__ __forceinline__ int unit_row(int unit, int r, const CubeGrid& g)
+// Key block j of a tile that sees every row: rows [128 j, 128 j + 128) as two 64-row units.
+__device__ __forceinline__ int4 every_row_block(int j, int rows)
 {
-    if (unit < g.cubes()) {
-        const int cx = unit % g.ncx, cy = (unit / g.ncx) % g.ncy, ct = unit / (g.ncx * g.ncy);
-        const int x = 4 * cx + (r & 3), y = 4 * cy + ((r >> 2) & 3), f = 4 * ct + (r >> 4);
-        if (x >= g.pw || y >= g.ph || f >= g.frames)
-            return -1;
-        return g.dense_rows + (f * g.ph + y) * g.pw + x;
-    }
-    const int row = (unit - g.cubes()) * 64 + r;
-    return row < g.dense_rows ? row : -1;
+    const int na = min(max(rows - 128 * j, 0), 64), nb = min(max(rows - 128 * j - 64, 0), 64);
+    return make_int4(128 * j, nb > 0 ? 128 * j + 64 : -1, 15, na | (nb << 8));
 }
 
-__device__ __forceinline__ int4 implicit_entry(int j, const CubeGrid& g)
+// Visible keys of half kh of block entry e for query half qh, as a 64-bit mask over the unit's loaded rows.
+__device__ __forceinline__ uint64_t block_key_mask(const int4& e, int qh, int kh)
 {
-    return make_int4(2 * j, 2 * j + 1 < g.units() ? 2 * j + 1 : -1, 15, 0);
+    const int first = kh ? e.y : e.x;
+    const int n = (e.w >> (8 * kh)) & 0xff;
+    if (first < 0 || n <= 0 || !((e.z >> (2 * qh + kh)) & 1))
+        return 0ull;
+    return n >= 64 ? ~0ull : (1ull << n) - 1;
 }
 
 // ------------------------------------------------------------------------------------------------------------
@@ -147,7 +110,6 @@ __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid
     const int warp = warp_id();
     const int pair = blockIdx.x, head = blockIdx.y;
     const int nkv = (p.rows + 127) / 128;
-    const CubeGrid& g = p.grid;
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
@@ -181,7 +143,7 @@ __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid
         // ------------------------------------------------------------------------------------------ TMA
         mbar_arrive_expect_tx(q_full, 2 * TILE);
         for (int u = 0; u < 4; ++u)
-            load_unit<false>(smem + A2_OFF_Q + (u >> 1) * TILE, u & 1, 4 * pair + u, head, &maps.q, &maps.cq, g, q_full);
+            load_rows(smem + A2_OFF_Q + (u >> 1) * TILE, u & 1, (4 * pair + u) * 64, head, &maps.q, q_full);
         // K runs ahead of V by up to the depth of its ring
         int jk = 0, jv = 0;
         while (jv < nkv) {
@@ -190,16 +152,16 @@ __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid
                 if (!mbar_wait(&k_empty[s], ((jk / A2_KST) & 1) ^ 1))
                     break;
                 mbar_arrive_expect_tx(&k_full[s], TILE);
-                load_unit<false>(smem + A2_OFF_K + s * TILE, 0, 2 * jk, head, &maps.k, &maps.ck, g, &k_full[s]);
-                load_unit<false>(smem + A2_OFF_K + s * TILE, 1, 2 * jk + 1, head, &maps.k, &maps.ck, g, &k_full[s]);
+                load_rows(smem + A2_OFF_K + s * TILE, 0, 128 * jk, head, &maps.k, &k_full[s]);
+                load_rows(smem + A2_OFF_K + s * TILE, 1, 128 * jk + 64, head, &maps.k, &k_full[s]);
                 ++jk;
             } else {
                 const int s = jv % A2_VST;
                 if (!mbar_wait(&v_empty[s], ((jv / A2_VST) & 1) ^ 1))
                     break;
                 mbar_arrive_expect_tx(&v_full[s], TILE);
-                load_unit<false>(smem + A2_OFF_V + s * TILE, 0, 2 * jv, head, &maps.v, &maps.cv, g, &v_full[s]);
-                load_unit<false>(smem + A2_OFF_V + s * TILE, 1, 2 * jv + 1, head, &maps.v, &maps.cv, g, &v_full[s]);
+                load_rows(smem + A2_OFF_V + s * TILE, 0, 128 * jv, head, &maps.v, &v_full[s]);
+                load_rows(smem + A2_OFF_V + s * TILE, 1, 128 * jv + 64, head, &maps.v, &v_full[s]);
                 ++jv;
             }
         }
@@ -448,28 +410,23 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
 
     const int warp = warp_id();
     const int tile = blockIdx.x, head = blockIdx.y;
-    const CubeGrid& g = p.grid;
     int nkv;
-    int2 qu;
+    int4 qr; // (first row of query half 0, of half 1 or -1, rows of half 0, rows of half 1)
     const int4* entries = nullptr;
-    bool implicit = false;
+    bool every = true; // the tile sees every row
     if constexpr (SPARSE) {
         nkv = p.nblocks[head * p.q_tiles + tile];
-        implicit = nkv < 0;
-        if (implicit)
-            nkv = (g.units() + 1) / 2;
-        qu = p.q_units[tile];
+        every = nkv < 0;
+        if (every)
+            nkv = (p.rows + 127) / 128;
+        qr = p.q_rows[tile];
         entries = p.blocks + (size_t(head) * p.q_tiles + tile) * p.max_blocks;
     } else {
         nkv = (p.rows + 127) / 128;
-        qu = make_int2(2 * tile, 2 * tile + 1);
+        const int4 e = every_row_block(tile, p.rows);
+        qr = make_int4(e.x, e.y, e.w & 0xff, e.w >> 8);
     }
-    auto entry = [&](int j) -> int4 {
-        if constexpr (SPARSE)
-            return implicit ? implicit_entry(j, g) : entries[j];
-        else
-            return make_int4(2 * j, 2 * j + 1, 15, 0);
-    };
+    auto entry = [&](int j) -> int4 { return every ? every_row_block(j, p.rows) : entries[j]; };
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
@@ -502,10 +459,11 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
     if (nkv > 0 && warp == 0 && elect_one_lane()) {
         // ------------------------------------------------------------------------------------------ TMA
         mbar_arrive_expect_tx(q_full, TILE);
-        load_unit<SPARSE>(smem + A3_OFF_Q, 0, qu.x, head, &maps.q, &maps.cq, g, q_full);
-        load_unit<SPARSE>(smem + A3_OFF_Q, 1, qu.y < 0 ? qu.x : qu.y, head, &maps.q, &maps.cq, g, q_full);
-        // K runs ahead of V by up to the depth of its ring
+        load_rows(smem + A3_OFF_Q, 0, qr.x, head, &maps.q, q_full);
+        load_rows(smem + A3_OFF_Q, 1, qr.y < 0 ? qr.x : qr.y, head, &maps.q, q_full);
+        // K runs ahead of V by up to the depth of its ring; each list entry is fetched while the ring slot is awaited
         int jk = 0, jv = 0;
+        int4 ek = entry(0), ev = ek;
         bool ok = true;
         while (ok && jv < nkv) {
             const bool k_turn = jk < nkv && jk < jv + A3_KST;
@@ -513,20 +471,20 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
                 const int s = jk % A3_KST;
                 if (!(ok = mbar_wait(&k_empty[s], ((jk / A3_KST) & 1) ^ 1)))
                     break;
-                const int4 e = entry(jk);
                 mbar_arrive_expect_tx(&k_full[s], TILE);
-                load_unit<SPARSE>(smem + A3_OFF_K + s * TILE, 0, e.x, head, &maps.k, &maps.ck, g, &k_full[s]);
-                load_unit<SPARSE>(smem + A3_OFF_K + s * TILE, 1, e.y < 0 ? e.x : e.y, head, &maps.k, &maps.ck, g, &k_full[s]);
-                ++jk;
+                load_rows(smem + A3_OFF_K + s * TILE, 0, ek.x, head, &maps.k, &k_full[s]);
+                load_rows(smem + A3_OFF_K + s * TILE, 1, ek.y < 0 ? ek.x : ek.y, head, &maps.k, &k_full[s]);
+                if (++jk < nkv)
+                    ek = entry(jk);
             } else {
                 const int s = jv % A3_VST;
                 if (!(ok = mbar_wait(&v_empty[s], ((jv / A3_VST) & 1) ^ 1)))
                     break;
-                const int4 e = entry(jv);
                 mbar_arrive_expect_tx(&v_full[s], TILE);
-                load_unit<SPARSE>(smem + A3_OFF_V + s * TILE, 0, e.x, head, &maps.v, &maps.cv, g, &v_full[s]);
-                load_unit<SPARSE>(smem + A3_OFF_V + s * TILE, 1, e.y < 0 ? e.x : e.y, head, &maps.v, &maps.cv, g, &v_full[s]);
-                ++jv;
+                load_rows(smem + A3_OFF_V + s * TILE, 0, ev.x, head, &maps.v, &v_full[s]);
+                load_rows(smem + A3_OFF_V + s * TILE, 1, ev.y < 0 ? ev.x : ev.y, head, &maps.v, &v_full[s]);
+                if (++jv < nkv)
+                    ev = entry(jv);
             }
         }
     } else if (nkv > 0 && warp == 1 && elect_one_lane()) {
@@ -584,50 +542,49 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
         const float sl2 = p.scale * 1.4426950408889634f;
         float m = -INFINITY, l = 0.f;
         bool ok = true;
+        int4 e_next = entry(0);
         for (int j = 0; j < nkv; ++j) {
             const uint32_t tS = tmem + lane_base + (j & 1) * 128;
+            // Keys this slice may see (not past the unit's rows, unit selected for this query half). km is the same for
+            // the whole warp (its rows share the query half qh), so a slice with no visible key skips its scores.
+            const int4 e = e_next;
+            if (j + 1 < nkv)
+                e_next = entry(j + 1);
+            const uint64_t km = block_key_mask(e, qh, hc);
             if (!(ok = mbar_wait(&s_full[j & 1], (j >> 1) & 1)))
                 break;
             tc_fence_after();
             float s[64];
-            {
-                uint32_t r[2][32];
-                tmem_ld32(tS + hc * 64, r[0]);
-                tmem_ld32(tS + hc * 64 + 32, r[1]);
-                tmem_wait_ld();
+            float mx = -INFINITY;
+            if (km != 0ull) {
+                {
+                    uint32_t r[2][32];
+                    tmem_ld32(tS + hc * 64, r[0]);
+                    tmem_ld32(tS + hc * 64 + 32, r[1]);
+                    tmem_wait_ld();
 #pragma unroll
-                for (int c = 0; c < 2; ++c)
+                    for (int c = 0; c < 2; ++c)
 #pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        s[c * 32 + i] = __uint_as_float(r[c][i]);
-            }
-            // Keys this slice may not see: past the sequence (dense), or padding / unselected units (sparse).
-            uint64_t km = ~0ull;
-            if constexpr (SPARSE) {
-                const int4 e = entry(j);
-                const int u = hc ? e.y : e.x;
-                km = (u >= 0 && ((e.z >> (2 * qh + hc)) & 1)) ? unit_valid_mask(u, g) : 0ull;
-            } else {
-                const int left = p.rows - j * 128 - hc * 64;
-                if (left < 64)
-                    km = left <= 0 ? 0ull : (1ull << left) - 1;
-            }
-            if (km != ~0ull) {
+                        for (int i = 0; i < 32; ++i)
+                            s[c * 32 + i] = __uint_as_float(r[c][i]);
+                }
+                if (km != ~0ull) {
 #pragma unroll
-                for (int c = 0; c < 64; ++c)
-                    if (!((km >> c) & 1))
-                        s[c] = -INFINITY;
-            }
-            float mp[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-                mp[i] = fmaxf(s[2 * i], s[2 * i + 1]);
-#pragma unroll
-            for (int c = 16; c < 64; c += 16)
+                    for (int c = 0; c < 64; ++c)
+                        if (!((km >> c) & 1))
+                            s[c] = -INFINITY;
+                }
+                float mp[8];
 #pragma unroll
                 for (int i = 0; i < 8; ++i)
-                    mp[i] = max3f(mp[i], s[c + 2 * i], s[c + 2 * i + 1]);
-            float mx = max3f(max3f(mp[0], mp[1], mp[2]), max3f(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7]));
+                    mp[i] = fmaxf(s[2 * i], s[2 * i + 1]);
+#pragma unroll
+                for (int c = 16; c < 64; c += 16)
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        mp[i] = max3f(mp[i], s[c + 2 * i], s[c + 2 * i + 1]);
+                mx = max3f(max3f(mp[0], mp[1], mp[2]), max3f(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7]));
+            }
             {
                 // Both slices have loaded their scores once this exchange completes, so P may then overwrite them.
                 float* slot = red + (j & 1) * 256;
@@ -645,17 +602,24 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
             const float alpha = need ? ex2_approx(m - m_use) : 1.f;
             const float msub = m_use == -INFINITY ? 0.f : m_use;
             const float2 scale2 = make_float2(sl2, sl2), neg2 = make_float2(-msub, -msub);
-            float2 sp[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
             uint32_t pk[32];
+            float rs = 0.f;
+            if (km != 0ull) {
+                float2 sp[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
-            for (int c = 0; c < 32; ++c) {
-                const float2 x = fma2(make_float2(s[2 * c], s[2 * c + 1]), scale2, neg2);
-                const float2 e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
-                sp[c & 3] = add2(sp[c & 3], e);
-                pk[c] = pack_bf16x2(e.x, e.y);
+                for (int c = 0; c < 32; ++c) {
+                    const float2 x = fma2(make_float2(s[2 * c], s[2 * c + 1]), scale2, neg2);
+                    const float2 e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+                    sp[c & 3] = add2(sp[c & 3], e);
+                    pk[c] = pack_bf16x2(e.x, e.y);
+                }
+                const float2 s01 = add2(add2(sp[0], sp[1]), add2(sp[2], sp[3]));
+                rs = s01.x + s01.y;
+            } else {
+#pragma unroll
+                for (int c = 0; c < 32; ++c)
+                    pk[c] = 0u;
             }
-            const float2 s01 = add2(add2(sp[0], sp[1]), add2(sp[2], sp[3]));
-            const float rs = s01.x + s01.y;
             if (j > 0 && __any_sync(0xffffffffu, need)) {
                 // O holds PV_0..PV_{j-2} for sure; wait for PV_{j-1} before scaling it
                 if (!(ok = mbar_wait(pv_done, (j - 1) & 1)))
@@ -692,15 +656,8 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
         }
         if (ok && mbar_wait(pv_done, (nkv - 1) & 1)) {
             tc_fence_after();
-            int out_row;
-            if constexpr (SPARSE) {
-                const int u = qh ? qu.y : qu.x;
-                out_row = u < 0 ? -1 : unit_row(u, row & 63, g);
-            } else {
-                out_row = tile * 128 + row;
-                if (out_row >= p.rows)
-                    out_row = -1;
-            }
+            const int first = qh ? qr.y : qr.x, nq = qh ? qr.w : qr.z;
+            const int out_row = first >= 0 && (row & 63) < nq ? first + (row & 63) : -1;
             const float inv = l > 0.f ? 1.f / l : 0.f;
             __nv_bfloat16* dst = out_ptr(p, out_row, head, hc * 64);
 #pragma unroll 1
@@ -728,22 +685,12 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
     }
 }
 
-CUtensorMap dense_map(const void* base, int heads, int rows, int64_t row_stride)
+CUtensorMap rows_map(const void* base, int heads, int rows, int64_t row_stride)
 {
     const uint64_t dims[3] = {128, uint64_t(heads), uint64_t(rows > 0 ? rows : 1)};
     const uint64_t str[2] = {256, uint64_t(row_stride) * 2};
     const uint32_t box[3] = {64, 1, 64};
     return make_tmap(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, str, box);
-}
-
-CUtensorMap cube_map(const void* base, int heads, const CubeGrid& g, int64_t row_stride)
-{
-    const void* video = static_cast<const uint8_t*>(base) + size_t(g.dense_rows) * row_stride * 2;
-    const uint64_t rs = uint64_t(row_stride) * 2;
-    const uint64_t dims[5] = {128, uint64_t(heads), uint64_t(g.pw), uint64_t(g.ph), uint64_t(g.frames)};
-    const uint64_t str[4] = {256, rs, rs * g.pw, rs * g.pw * g.ph};
-    const uint32_t box[5] = {64, 1, 4, 4, 4};
-    return make_tmap(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, video, dims, str, box);
 }
 
 } // namespace
@@ -753,25 +700,14 @@ void attention(const AttnParams& p, cudaStream_t s)
     if (p.heads <= 0 || !p.q || !p.k || !p.v || !p.out || (p.row_stride * 2) % 16 || (p.out_row_stride * 2) % 16)
         throw CudaError("attention: bad arguments");
     const bool sparse = p.blocks != nullptr;
+    if (sparse && (p.grid.cubes() <= 0 || !p.nblocks || !p.q_rows || p.q_tiles <= 0 || p.rows != p.grid.rows()))
+        throw CudaError("attention: bad sparse arguments");
+    if (p.rows <= 0)
+        return;
     Maps maps;
-    if (!sparse) {
-        if (p.rows <= 0)
-            return;
-        maps.q = dense_map(p.q, p.heads, p.rows, p.row_stride);
-        maps.k = dense_map(p.k, p.heads, p.rows, p.row_stride);
-        maps.v = dense_map(p.v, p.heads, p.rows, p.row_stride);
-        maps.cq = maps.q, maps.ck = maps.k, maps.cv = maps.v;
-    } else {
-        const CubeGrid& g = p.grid;
-        if (g.cubes() <= 0 || !p.nblocks || !p.q_units || p.q_tiles <= 0)
-            throw CudaError("attention: bad sparse arguments");
-        maps.q = dense_map(p.q, p.heads, g.dense_rows, p.row_stride);
-        maps.k = dense_map(p.k, p.heads, g.dense_rows, p.row_stride);
-        maps.v = dense_map(p.v, p.heads, g.dense_rows, p.row_stride);
-        maps.cq = cube_map(p.q, p.heads, g, p.row_stride);
-        maps.ck = cube_map(p.k, p.heads, g, p.row_stride);
-        maps.cv = cube_map(p.v, p.heads, g, p.row_stride);
-    }
+    maps.q = rows_map(p.q, p.heads, p.rows, p.row_stride);
+    maps.k = rows_map(p.k, p.heads, p.rows, p.row_stride);
+    maps.v = rows_map(p.v, p.heads, p.rows, p.row_stride);
     static bool attr[2] = {false, false};
     if (!attr[sparse]) {
         if (sparse)

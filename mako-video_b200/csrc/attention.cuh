@@ -13,10 +13,15 @@
 
 namespace h3 {
 
-// The sparse attention's units: 64-row tiles, either a 4x4x4 cube of the generated video rows (latent frame, patch
-// row, patch column; the grid padded to multiples of 4 with rows that are no token) or 64 consecutive dense rows
-// (text, conditioning and audio rows, which precede the generated video rows). Units 0 .. cubes-1 are the cubes in
+// The sparse attention's units, 64-row key/query tiles: either a 4x4x4 cube of the generated video rows (latent
+// frame, patch row, patch column; cubes at the grid's far edges are cut short) or 64 consecutive dense rows (text,
+// conditioning and audio rows, which precede the generated video rows). Units 0 .. cubes-1 are the cubes in
 // (frame group, row group, column group) order; units cubes .. cubes+dense_units-1 the dense chunks.
+//
+// Packed row order: the generated video rows are stored cube by cube, in unit order, each cube's rows in (frame, row,
+// column) order with no padding, so that every cube is one run of consecutive rows. A cube of nf x ny x nx rows
+// (each at most 4) starting at latent position (4 ct, 4 cy, 4 cx) begins at
+//     dense_rows + 4 ct ph pw + nf (4 cy pw + ny 4 cx).
 struct CubeGrid {
     int dense_rows = 0; // D: rows before the generated video rows
     int frames = 0, ph = 0, pw = 0; // generated video rows as [frames][ph][pw]
@@ -24,6 +29,31 @@ struct CubeGrid {
     H3_HD int cubes() const { return nct * ncy * ncx; }
     H3_HD int dense_units() const { return (dense_rows + 63) / 64; }
     H3_HD int units() const { return cubes() + dense_units(); }
+    H3_HD int video_rows() const { return frames * ph * pw; }
+    H3_HD int rows() const { return dense_rows + video_rows(); }
+    // First packed row and row count of unit u.
+    H3_HD void unit_span(int u, int& first, int& n) const
+    {
+        if (u < cubes()) {
+            const int cx = u % ncx, cy = (u / ncx) % ncy, ct = u / (ncx * ncy);
+            const int nx = pw - 4 * cx < 4 ? pw - 4 * cx : 4, ny = ph - 4 * cy < 4 ? ph - 4 * cy : 4;
+            const int nf = frames - 4 * ct < 4 ? frames - 4 * ct : 4;
+            first = dense_rows + 4 * ct * ph * pw + nf * (4 * cy * pw + ny * 4 * cx);
+            n = nf * ny * nx;
+        } else {
+            first = (u - cubes()) * 64;
+            n = dense_rows - first < 64 ? dense_rows - first : 64;
+        }
+    }
+    // Packed row of generated video row (f, y, x).
+    H3_HD int video_pos(int f, int y, int x) const
+    {
+        const int ct = f >> 2, cy = y >> 2, cx = x >> 2;
+        int first, n;
+        unit_span((ct * ncy + cy) * ncx + cx, first, n);
+        const int nx = pw - 4 * cx < 4 ? pw - 4 * cx : 4, ny = ph - 4 * cy < 4 ? ph - 4 * cy : 4;
+        return first + ((f & 3) * ny + (y & 3)) * nx + (x & 3);
+    }
 };
 
 struct AttnParams {
@@ -33,7 +63,7 @@ struct AttnParams {
     const void* v = nullptr;
     int64_t row_stride = 0; // elements between consecutive rows of q, k and v
     int heads = 0;          // heads addressed by the q/k/v tensors
-    int rows = 0;           // dense mode: query and key rows (keys at or past `rows` are masked)
+    int rows = 0;           // query and key rows (sparse mode: grid.rows())
     void* out = nullptr;    // o: (row, head, dim) at out + row * out_row_stride + head * 128 + dim
     int64_t out_row_stride = 0;
     // Sequence parallel with the exchange fused into the epilogue: row R's output goes straight to its owner
@@ -43,12 +73,14 @@ struct AttnParams {
     int rows_per_rank = 0, my_rank = 0;
     float scale = 0.08838834764831845f; // 1 / sqrt(128)
 
-    // Sparse mode (blocks != null). Query tile t is the unit pair q_units[t]; for head h it visits
-    // nblocks[h * q_tiles + t] key blocks blocks[(h * q_tiles + t) * max_blocks + j] = (unit a, unit b, keep, 0): keys
-    // of unit a then unit b (b = -1: none), `keep` bit (2 * qh + kh) set when query half qh may see key unit kh.
+    // Sparse mode (blocks != null; rows in the packed order above). Query tile t is two units, q_rows[t] = (first
+    // row a, first row b or -1, rows of a, rows of b). For head h it visits nblocks[h * q_tiles + t] key blocks
+    // blocks[(h * q_tiles + t) * max_blocks + j] = (first row a, first row b or -1, keep, rows of a | rows of b << 8):
+    // 64 keys from each first row, of which the unit's row count are its tokens; `keep` bit (2 * qh + kh) is set when
+    // query half qh may see key unit kh. nblocks -1: the tile sees every row (128-row blocks over all rows).
     const int4* blocks = nullptr;
     const int32_t* nblocks = nullptr;
-    const int2* q_units = nullptr;
+    const int4* q_rows = nullptr;
     int q_tiles = 0;
     int max_blocks = 0;
     CubeGrid grid;

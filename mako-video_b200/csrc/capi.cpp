@@ -11,6 +11,7 @@
 #include <nccl.h>
 
 #include <cstring>
+#include <initializer_list>
 #include <string>
 
 struct h3_model {
@@ -63,6 +64,16 @@ int guarded(F&& f)
         g_error = e.what();
         return H3_ERR_CUDA;
     }
+}
+
+// The h3k_* kernel entry points take device-accessible memory only (device, managed, or mapped pinned host memory):
+// a plain host pointer passed by mistake is refused here rather than faulting inside a kernel. Null is let through
+// (each call checks its own required arguments).
+void device_ptrs(const char* fn, std::initializer_list<const void*> ptrs)
+{
+    for (const void* p : ptrs)
+        if (!h3::device_accessible(p))
+            throw ArgError(std::string(fn) + ": a pointer argument is host memory the GPU cannot access");
 }
 
 h3::Layout to_layout(const h3_layout* l)
@@ -334,6 +345,7 @@ int h3k_gemm(const void* A, const void* B, const h3k_gemm_args* a, int32_t epilo
     return guarded([&] {
         if (!A || !B || !a)
             throw ArgError("h3k_gemm: null argument");
+        device_ptrs("h3k_gemm", {A, B, a->out, a->bias, a->x, a->mod, a->mod_idx, a->rope, a->qn_w, a->kn_w, a->a_scale, a->b_scale});
         if (epilogue < 0 || epilogue > 5)
             throw ArgError("h3k_gemm: unknown epilogue");
         h3::GemmParams p;
@@ -358,6 +370,7 @@ int h3k_rms_mod(const float* x, int64_t ldx, int32_t rows, int32_t d, const floa
     return guarded([&] {
         if (out_kind < 0 || out_kind > 2)
             throw ArgError("h3k_rms_mod: out_kind 0 bf16, 1 f32, 2 int8");
+        device_ptrs("h3k_rms_mod", {x, w, mod, mod_idx, out, out_scale});
         h3::RmsModParams p;
         p.x = x, p.ldx = ldx, p.rows = rows, p.d = d, p.w = w, p.mod = mod, p.mod_idx = mod_idx, p.mod_slots = mod_slots;
         p.shift_slot = shift_slot, p.scale_slot = scale_slot, p.eps = eps, p.out_kind = h3::RowOut(out_kind), p.out = out, p.ldo = ldo;
@@ -369,34 +382,50 @@ int h3k_rms_mod(const float* x, int64_t ldx, int32_t rows, int32_t d, const floa
 int h3k_gate_add(float* x, int64_t ldx, const void* y, int64_t ldy, int32_t rows, int32_t d, const float* mod, const uint8_t* mod_idx,
                  int32_t gate_slot, void* stream)
 {
-    return guarded([&] { h3::gate_add_rows(x, ldx, y, ldy, rows, d, mod, mod_idx, gate_slot, st(stream)); });
+    return guarded([&] {
+        device_ptrs("h3k_gate_add", {x, y, mod, mod_idx});
+        h3::gate_add_rows(x, ldx, y, ldy, rows, d, mod, mod_idx, gate_slot, st(stream));
+    });
 }
 
 int h3k_swiglu(const void* gv, int32_t rows, int32_t F, void* out, void* stream)
 {
-    return guarded([&] { h3::swiglu_rows(gv, rows, F, out, st(stream)); });
+    return guarded([&] {
+        device_ptrs("h3k_swiglu", {gv, out});
+        h3::swiglu_rows(gv, rows, F, out, st(stream));
+    });
 }
 
 int h3k_quant_rows_i8(const void* x, int64_t ldx, int32_t rows, int32_t K, int8_t* q, float* scale, void* stream)
 {
-    return guarded([&] { h3::quant_rows_i8(x, ldx, rows, K, q, scale, st(stream)); });
+    return guarded([&] {
+        device_ptrs("h3k_quant_rows_i8", {x, q, scale});
+        h3::quant_rows_i8(x, ldx, rows, K, q, scale, st(stream));
+    });
 }
 
 int h3k_quant_weight(const void* w, int32_t rows, int32_t K, int8_t* q, float* scale, void* stream)
 {
-    return guarded([&] { h3::quant_weight_rows(w, rows, K, q, scale, st(stream)); });
+    return guarded([&] {
+        device_ptrs("h3k_quant_weight", {w, q, scale});
+        h3::quant_weight_rows(w, rows, K, q, scale, st(stream));
+    });
 }
 
 int h3k_heads_partial(void* qkv, int32_t rows, int32_t heads, const float* qn_w, const float* kn_w, const float* rope, float eps,
                       void* stream)
 {
-    return guarded([&] { h3::heads_partial(qkv, rows, heads, qn_w, kn_w, rope, eps, st(stream)); });
+    return guarded([&] {
+        device_ptrs("h3k_heads_partial", {qkv, qn_w, kn_w, rope});
+        h3::heads_partial(qkv, rows, heads, qn_w, kn_w, rope, eps, st(stream));
+    });
 }
 
 int h3k_attention(const void* q, const void* k, const void* v, int64_t row_stride, int32_t heads, int32_t rows, void* out,
                   int64_t out_row_stride, void* stream)
 {
     return guarded([&] {
+        device_ptrs("h3k_attention", {q, k, v, out});
         h3::AttnParams p;
         p.q = q, p.k = k, p.v = v, p.row_stride = row_stride, p.heads = heads, p.rows = rows, p.out = out;
         p.out_row_stride = out_row_stride;
@@ -427,6 +456,9 @@ int h3k_sparse_select(const void* q, const void* k, int64_t row_stride, int32_t 
 {
     return guarded([&] {
         const h3::CubeGrid c = to_grid(g);
+        if (!q || !k || !sel || !nsel)
+            throw ArgError("h3k_sparse_select: null argument");
+        device_ptrs("h3k_sparse_select", {q, k, mq, mk, scores, sel, nsel});
         int kc, qt, mb;
         h3::sparse_sizes(c, ratio, local, kc, qt, mb);
         Scratch sc;
@@ -444,11 +476,27 @@ int h3k_sparse_select(const void* q, const void* k, int64_t row_stride, int32_t 
     });
 }
 
+int h3k_video_order(const h3k_cube_grid* g, int32_t* src)
+{
+    return guarded([&] {
+        const h3::CubeGrid c = to_grid(g);
+        if (!src)
+            throw ArgError("h3k_video_order: null output");
+        for (int f = 0, n = 0; f < c.frames; ++f)
+            for (int y = 0; y < c.ph; ++y)
+                for (int x = 0; x < c.pw; ++x, ++n)
+                    src[c.video_pos(f, y, x) - c.dense_rows] = n;
+    });
+}
+
 int h3k_cube_topk(const float* scores, int32_t heads, const h3k_cube_grid* g, float ratio, int32_t local, int32_t* sel, int32_t* nsel,
                   void* stream)
 {
     return guarded([&] {
         const h3::CubeGrid c = to_grid(g);
+        if (!scores || !sel || !nsel)
+            throw ArgError("h3k_cube_topk: null argument");
+        device_ptrs("h3k_cube_topk", {scores, sel, nsel});
         int kc, qt, mb;
         h3::sparse_sizes(c, ratio, local, kc, qt, mb);
         h3::cube_topk(scores, heads, c, h3::sparse_k(ratio, c.cubes()), local, sel, nsel, kc, st(stream));
@@ -460,6 +508,9 @@ int h3k_sparse_attention(const void* q, const void* k, const void* v, int64_t ro
 {
     return guarded([&] {
         const h3::CubeGrid c = to_grid(g);
+        if (!q || !k || !v || !out)
+            throw ArgError("h3k_sparse_attention: null argument");
+        device_ptrs("h3k_sparse_attention", {q, k, v, out});
         h3::SparseBuffers b;
         h3::sparse_sizes(c, ratio, local, b.kcap, b.q_tiles, b.max_blocks);
         Scratch sc;
@@ -471,7 +522,7 @@ int h3k_sparse_attention(const void* q, const void* k, const void* v, int64_t ro
         b.nsel = static_cast<int32_t*>(sc.get(size_t(heads) * nc * 4));
         b.blocks = static_cast<int4*>(sc.get(size_t(heads) * b.q_tiles * b.max_blocks * 16));
         b.nblocks = static_cast<int32_t*>(sc.get(size_t(heads) * b.q_tiles * 4));
-        b.q_units = static_cast<int2*>(sc.get(size_t(b.q_tiles) * 8));
+        b.q_rows = static_cast<int4*>(sc.get(size_t(b.q_tiles) * 16));
         h3::AttnParams p;
         p.q = q, p.k = k, p.v = v, p.row_stride = row_stride, p.heads = heads, p.rows = c.dense_rows + c.frames * c.ph * c.pw;
         p.out = out, p.out_row_stride = out_row_stride;
@@ -482,24 +533,36 @@ int h3k_sparse_attention(const void* q, const void* k, const void* v, int64_t ro
 
 int h3k_fill_synthetic(void* dst, int32_t is_bf16, uint64_t n, uint64_t seed, uint32_t tensor_id, float mean, float stdev, void* stream)
 {
-    return guarded([&] { h3::fill_synthetic(dst, is_bf16, n, seed, tensor_id, mean, stdev, st(stream)); });
+    return guarded([&] {
+        device_ptrs("h3k_fill_synthetic", {dst});
+        h3::fill_synthetic(dst, is_bf16, n, seed, tensor_id, mean, stdev, st(stream));
+    });
 }
 
 int h3k_gemv_f32(const float* W, const float* b, const float* x, int32_t U, int32_t N, int32_t K, int32_t act, float* out, float* out2,
                  void* stream)
 {
-    return guarded([&] { h3::gemv_f32(W, b, x, U, N, K, h3::Act(act), out, out2, st(stream)); });
+    return guarded([&] {
+        device_ptrs("h3k_gemv_f32", {W, b, x, out, out2});
+        h3::gemv_f32(W, b, x, U, N, K, h3::Act(act), out, out2, st(stream));
+    });
 }
 
 int h3k_adaln(const void* W, const float* b, const float* x, int32_t U, int32_t groups, int32_t G, int32_t K, float* out, void* stream)
 {
-    return guarded([&] { h3::adaln_gemv(W, b, x, U, groups, G, K, out, st(stream)); });
+    return guarded([&] {
+        device_ptrs("h3k_adaln", {W, b, x, out});
+        h3::adaln_gemv(W, b, x, U, groups, G, K, out, st(stream));
+    });
 }
 
 int h3k_heads(const float* x, int64_t ldx, int32_t rows, const float* W, const float* b, int32_t N, int32_t K, float* out, int64_t ldo,
               void* stream)
 {
-    return guarded([&] { h3::heads_f32(x, ldx, rows, W, b, N, K, out, ldo, st(stream)); });
+    return guarded([&] {
+        device_ptrs("h3k_heads", {x, W, b, out});
+        h3::heads_f32(x, ldx, rows, W, b, N, K, out, ldo, st(stream));
+    });
 }
 
 int h3k_check(void* stream)

@@ -65,6 +65,18 @@ uint32_t take_device_error(cudaStream_t s)
     return v;
 }
 
+bool device_accessible(const void* p)
+{
+    if (!p)
+        return true;
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type != cudaMemoryTypeUnregistered && a.devicePointer != nullptr;
+}
+
 int num_sms()
 {
     int dev = 0, n = 0;

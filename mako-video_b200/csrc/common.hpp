@@ -30,4 +30,8 @@ uint32_t take_device_error(cudaStream_t s);
 
 int num_sms();
 
+// True when a kernel may dereference p: device or managed memory, or pinned host memory mapped into the device's
+// address space (null counts as accessible; callers check their own required arguments).
+bool device_accessible(const void* p);
+
 } // namespace h3

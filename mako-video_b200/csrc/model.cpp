@@ -197,13 +197,18 @@ struct Model::Impl {
     DevBuf rope;       // [S_local][48][2]
     DevBuf mod_idx;    // [S_local] u8: level * 3 + tag
     DevBuf lvl_idx;    // [S_local] u8: level
+    // The step keeps the generated video rows in the packed (cube-major) order; these map between it and the
+    // layout's (frame, row, column) order: video_src[i] = layout index of packed video row i, video_dst the inverse.
+    CubeGrid grid;
+    std::vector<int32_t> h_video_src;
+    DevBuf video_src, video_dst, out_video_rows;
     std::vector<uint8_t> h_tags, h_roles, h_lvl_kind; // per global row; lvl_kind: 0 video/text level, 1 audio, 2 cond
     // per step
     DevBuf emb, th, temb, tsilu, mods, fmods;
     DevBuf x, h, hq, hs, qkv, qkv_recv, o, o_recv, act;
     DevBuf in_video, in_audio, pk_video, pk_audio, rows_out, rows_all;
     SparseBuffers sp;
-    DevBuf sp_mq, sp_mk, sp_scores, sp_sel, sp_nsel, sp_blocks, sp_nblocks, sp_qunits;
+    DevBuf sp_mq, sp_mk, sp_scores, sp_sel, sp_nsel, sp_blocks, sp_nblocks, sp_qrows;
     ncclComm_t comm = nullptr;
     std::vector<cudaEvent_t> ev;
     // Sequence parallel with the exchange fused into the kernels: every rank's qkv_recv and o_recv mapped here.
@@ -446,8 +451,41 @@ void Model::begin(const float* text, int T, const Layout& l)
         gemm_bf16(tpk.p, d_->cond_w.p, g, Epi::f32, s);
         H3_CUDA(cudaStreamSynchronize(s));
     }
-    // row tables for this rank's rows
-    const Rows r = layout_rows(l);
+    // the packed row order: generated video rows cube by cube
+    CubeGrid& g = d_->grid;
+    g = CubeGrid();
+    g.dense_rows = l.dense_rows();
+    g.frames = l.frames, g.ph = l.h / 2, g.pw = l.w / 2;
+    g.nct = (g.frames + 3) / 4, g.ncy = (g.ph + 3) / 4, g.ncx = (g.pw + 3) / 4;
+    const int Vg = g.video_rows();
+    std::vector<int32_t>& src = d_->h_video_src;
+    src.assign(Vg, 0);
+    std::vector<int32_t> dst(Vg);
+    for (int f = 0, n = 0; f < g.frames; ++f)
+        for (int y = 0; y < g.ph; ++y)
+            for (int x = 0; x < g.pw; ++x, ++n) {
+                const int i = g.video_pos(f, y, x) - g.dense_rows;
+                src[i] = n, dst[n] = i;
+            }
+    d_->video_src.ensure(size_t(std::max(Vg, 1)) * 4);
+    d_->video_dst.ensure(size_t(std::max(Vg, 1)) * 4);
+    d_->out_video_rows.ensure(size_t(std::max(Vg, 1)) * c_.video_patch * 4);
+    if (Vg) {
+        H3_CUDA(cudaMemcpyAsync(d_->video_src.p, src.data(), size_t(Vg) * 4, cudaMemcpyHostToDevice, s));
+        H3_CUDA(cudaMemcpyAsync(d_->video_dst.p, dst.data(), size_t(Vg) * 4, cudaMemcpyHostToDevice, s));
+    }
+    // row tables for this rank's rows, in the packed order
+    Rows r = layout_rows(l);
+    {
+        const Rows nat = r;
+        const size_t D = size_t(g.dense_rows);
+        for (int i = 0; i < Vg; ++i) {
+            const size_t to = D + i, from = D + src[i];
+            r.tags[to] = nat.tags[from], r.roles[to] = nat.roles[from];
+            for (int a = 0; a < 3; ++a)
+                r.pos[3 * to + a] = nat.pos[3 * from + a];
+        }
+    }
     d_->h_tags = r.tags;
     d_->h_roles = r.roles;
     d_->h_lvl_kind.assign(S_, 0);
@@ -463,10 +501,6 @@ void Model::begin(const float* text, int T, const Layout& l)
     d_->lvl_idx.ensure(S_local_);
     // sparse buffers
     if (sparse_ratio_ > 0.f) {
-        CubeGrid g;
-        g.dense_rows = l.dense_rows();
-        g.frames = l.frames, g.ph = l.h / 2, g.pw = l.w / 2;
-        g.nct = (g.frames + 3) / 4, g.ncy = (g.ph + 3) / 4, g.ncx = (g.pw + 3) / 4;
         if (g.cubes() > 0) {
             const int Hp = c_.heads / P;
             SparseBuffers& b = d_->sp;
@@ -479,23 +513,29 @@ void Model::begin(const float* text, int T, const Layout& l)
             d_->sp_nsel.ensure(size_t(Hp) * nc * 4);
             d_->sp_blocks.ensure(size_t(Hp) * b.q_tiles * b.max_blocks * 16);
             d_->sp_nblocks.ensure(size_t(Hp) * b.q_tiles * 4);
-            d_->sp_qunits.ensure(size_t(b.q_tiles) * 8);
+            d_->sp_qrows.ensure(size_t(b.q_tiles) * 16);
             b.mq = d_->sp_mq.as<float>(), b.mk = d_->sp_mk.as<float>(), b.scores = d_->sp_scores.as<float>();
             b.sel = d_->sp_sel.as<int32_t>(), b.nsel = d_->sp_nsel.as<int32_t>();
-            b.blocks = d_->sp_blocks.as<int4>(), b.nblocks = d_->sp_nblocks.as<int32_t>(), b.q_units = d_->sp_qunits.as<int2>();
+            b.blocks = d_->sp_blocks.as<int4>(), b.nblocks = d_->sp_nblocks.as<int32_t>(), b.q_rows = d_->sp_qrows.as<int4>();
         }
     }
     H3_CUDA(cudaStreamSynchronize(s));
     begun_ = true;
 }
 
-void Model::emit_probe(const char* name, int layer, const float* dev, size_t n)
+void Model::emit_probe(const char* name, int layer, const float* dev, size_t n, bool rows)
 {
     if (!probe_)
         return;
     std::vector<float> h(n);
     H3_CUDA(cudaMemcpyAsync(h.data(), dev, n * 4, cudaMemcpyDeviceToHost, stream_));
     H3_CUDA(cudaStreamSynchronize(stream_));
+    if (rows && S_ > 0 && !d_->h_video_src.empty()) {
+        const size_t w = n / size_t(S_), D = size_t(d_->grid.dense_rows);
+        std::vector<float> packed(h.begin() + D * w, h.end());
+        for (size_t i = 0; i < d_->h_video_src.size(); ++i)
+            std::memcpy(&h[(D + d_->h_video_src[i]) * w], &packed[i * w], w * 4);
+    }
     probe_(name, layer, h.data(), n);
 }
 
@@ -611,8 +651,15 @@ void Model::step(const float* video, const float* audio, float t_video, float t_
                                 cudaMemcpyDeviceToDevice, s));
     d_->pk_video.ensure(size_t(std::max(V, 1)) * c_.video_patch * 2);
     d_->pk_audio.ensure(size_t(std::max(A, 1)) * 64 * 2);
-    if (V) {
-        pack_bf16_rows(dv, V, c_.video_patch, d_->pk_video.p, c_.video_patch, s);
+    if (C) {
+        pack_bf16_rows(dv, C, c_.video_patch, d_->pk_video.p, c_.video_patch, s);
+        ++launches_;
+    }
+    if (V - C) {
+        // generated video rows gathered into the packed order
+        pack_bf16_rows(dv + size_t(C) * c_.video_patch, V - C, c_.video_patch,
+                       static_cast<__nv_bfloat16*>(d_->pk_video.p) + size_t(C) * c_.video_patch, c_.video_patch, s,
+                       d_->video_src.as<int32_t>());
         ++launches_;
     }
     if (A) {
@@ -635,13 +682,11 @@ void Model::step(const float* video, const float* audio, float t_video, float t_
     proj(d_->pk_video.p, c_.video_patch, C, D, V - C, d_->vp_w, d_->vp_b, c_.video_patch);       // generated video
     mark("input");
     if (P == 1)
-        emit_probe("x0", -1, x, size_t(S_) * d);
+        emit_probe("x0", -1, x, size_t(S_) * d, true);
 
     // ---- blocks
     const bool sparse = sparse_ratio_ > 0.f && d_->sp.blocks != nullptr;
-    CubeGrid grid;
-    grid.dense_rows = D, grid.frames = l.frames, grid.ph = l.h / 2, grid.pw = l.w / 2;
-    grid.nct = (grid.frames + 3) / 4, grid.ncy = (grid.ph + 3) / 4, grid.ncx = (grid.pw + 3) / 4;
+    const CubeGrid& grid = d_->grid;
     const uint8_t* midx = d_->mod_idx.as<uint8_t>();
     __nv_bfloat16* qkv = d_->qkv.as<__nv_bfloat16>();
     // With several ranks the Ulysses exchanges are fused into the q/k/v GEMM's and the attention's epilogues
@@ -713,9 +758,9 @@ void Model::step(const float* video, const float* audio, float t_video, float t_
             cube_pool(ap.q, ap.k, ap.row_stride, Hp, grid, b.mq, b.mk, s);
             cube_scores(b.mq, b.mk, Hp, grid.cubes(), b.scores, s);
             cube_topk(b.scores, Hp, grid, sparse_k(sparse_ratio_, grid.cubes()), sparse_local_, b.sel, b.nsel, b.kcap, s);
-            build_passes(b.sel, b.nsel, b.kcap, Hp, grid, b.blocks, b.nblocks, b.q_units, b.q_tiles, b.max_blocks, s);
+            build_passes(b.sel, b.nsel, b.kcap, Hp, grid, b.blocks, b.nblocks, b.q_rows, b.q_tiles, b.max_blocks, s);
             mark("select");
-            ap.blocks = b.blocks, ap.nblocks = b.nblocks, ap.q_units = b.q_units, ap.q_tiles = b.q_tiles;
+            ap.blocks = b.blocks, ap.nblocks = b.nblocks, ap.q_rows = b.q_rows, ap.q_tiles = b.q_tiles;
             ap.max_blocks = b.max_blocks, ap.grid = grid;
             attention(ap, s);
             launches_ += 5;
@@ -790,7 +835,7 @@ void Model::step(const float* video, const float* audio, float t_video, float t_
         }
         mark("fc2");
         if (probe_ && P == 1)
-            emit_probe("block", bl, x, size_t(S_) * d);
+            emit_probe("block", bl, x, size_t(S_) * d, true);
     }
 
     // ---- final norm (per level shift and scale, no weight) and the heads
@@ -801,7 +846,7 @@ void Model::step(const float* video, const float* audio, float t_video, float t_
     rms_mod_rows(fp, s);
     ++launches_;
     if (P == 1)
-        emit_probe("norm_out", -1, xn, size_t(S_) * d);
+        emit_probe("norm_out", -1, xn, size_t(S_) * d, true);
     float* ro = d_->rows_out.as<float>();
     // rows_out: 128 floats a row (a video row's 96 values or an audio row's 32)
     auto head = [&](int first, int n, const DevBuf& w, const DevBuf& b, int N) {
@@ -824,9 +869,15 @@ void Model::step(const float* video, const float* audio, float t_video, float t_
     const cudaMemcpyKind kind = device_io ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost;
     if (C)
         H3_CUDA(cudaMemcpy2DAsync(out_video, c_.video_patch * 4, all + size_t(T) * 128, 128 * 4, c_.video_patch * 4, C, kind, s));
-    if (V - C)
-        H3_CUDA(cudaMemcpy2DAsync(out_video + size_t(C) * c_.video_patch, c_.video_patch * 4, all + size_t(D) * 128, 128 * 4,
-                                  c_.video_patch * 4, V - C, kind, s));
+    if (V - C) {
+        // back to the layout's row order
+        float* vo = device_io ? out_video + size_t(C) * c_.video_patch : d_->out_video_rows.as<float>();
+        gather_rows_f32(all + size_t(D) * 128, 128, d_->video_dst.as<int32_t>(), V - C, c_.video_patch, vo, c_.video_patch, s);
+        ++launches_;
+        if (!device_io)
+            H3_CUDA(cudaMemcpyAsync(out_video + size_t(C) * c_.video_patch, vo, size_t(V - C) * c_.video_patch * 4,
+                                    cudaMemcpyDeviceToHost, s));
+    }
     if (A)
         H3_CUDA(cudaMemcpy2DAsync(out_audio, c_.audio_channels * 4, all + size_t(T + C) * 128, 128 * 4, c_.audio_channels * 4, A, kind, s));
     if (timing_) {

@@ -108,7 +108,9 @@ private:
     bool begun_ = false;
     void alloc_activations();
     void map_peers(); // the ranks' receive buffers, mapped into every rank (sequence-parallel, fused exchange)
-    void emit_probe(const char* name, int layer, const float* dev, size_t n);
+    // Copies a device tensor to the host and hands it to the probe; with `rows` set it is [S][n / S] in the packed row
+    // order and is handed over in the layout's row order.
+    void emit_probe(const char* name, int layer, const float* dev, size_t n, bool rows = false);
 };
 
 } // namespace h3

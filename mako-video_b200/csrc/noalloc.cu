@@ -64,6 +64,9 @@ extern "C" int h3k_sparse_attention_noalloc(const void* q, const void* k, const 
             throw std::invalid_argument("h3k_sparse_attention_noalloc: null argument or no heads");
         if (g->frames <= 0 || g->ph <= 0 || g->pw <= 0 || g->dense_rows < 0)
             throw std::invalid_argument("h3k_sparse_attention_noalloc: bad cube grid");
+        for (const void* ptr : {q, k, v, static_cast<const void*>(out)})
+            if (!h3::device_accessible(ptr))
+                throw std::invalid_argument("h3k_sparse_attention_noalloc: a pointer argument is host memory the GPU cannot access");
         h3::CubeGrid c;
         c.dense_rows = g->dense_rows, c.frames = g->frames, c.ph = g->ph, c.pw = g->pw;
         c.nct = (c.frames + 3) / 4, c.ncy = (c.ph + 3) / 4, c.ncx = (c.pw + 3) / 4;
@@ -71,7 +74,7 @@ extern "C" int h3k_sparse_attention_noalloc(const void* q, const void* k, const 
         h3::sparse_sizes(c, ratio, local, b.kcap, b.q_tiles, b.max_blocks);
         const size_t nc = size_t(c.cubes()), H = size_t(heads);
         const size_t sizes[8] = {H * nc * 128 * 4, H * nc * 128 * 4, H * nc * nc * 4, H * nc * b.kcap * 4, H * nc * 4,
-                                 H * b.q_tiles * b.max_blocks * 16, H * b.q_tiles * 4, size_t(b.q_tiles) * 8};
+                                 H * b.q_tiles * b.max_blocks * 16, H * b.q_tiles * 4, size_t(b.q_tiles) * 16};
         size_t need = 0;
         for (size_t s : sizes)
             need += round256(s);
@@ -93,7 +96,7 @@ extern "C" int h3k_sparse_attention_noalloc(const void* q, const void* k, const 
         b.nsel = reinterpret_cast<int32_t*>(take(sizes[4]));
         b.blocks = reinterpret_cast<int4*>(take(sizes[5]));
         b.nblocks = reinterpret_cast<int32_t*>(take(sizes[6]));
-        b.q_units = reinterpret_cast<int2*>(take(sizes[7]));
+        b.q_rows = reinterpret_cast<int4*>(take(sizes[7]));
         const cudaStream_t s = static_cast<cudaStream_t>(stream);
         // Every buffer is written before it is read within one call; clearing the part in use anyway keeps a call
         // from ever seeing the previous call's selections.

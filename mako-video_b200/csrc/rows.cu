@@ -257,12 +257,22 @@ __global__ void heads_partial_kernel(__nv_bfloat16* qkv, int rows, int heads, co
     }
 }
 
-__global__ void pack_bf16_kernel(const float* in, int rows, int cols, __nv_bfloat16* out, int ld_out)
+__global__ void pack_bf16_kernel(const float* in, int rows, int cols, __nv_bfloat16* out, int ld_out, const int32_t* src_rows)
 {
     const size_t total = size_t(rows) * ld_out;
     for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
         const int r = int(i / ld_out), c = int(i % ld_out);
-        out[i] = __float2bfloat16_rn(c < cols ? in[size_t(r) * cols + c] : 0.f);
+        const size_t sr = src_rows ? size_t(src_rows[r]) : size_t(r);
+        out[i] = __float2bfloat16_rn(c < cols ? in[sr * cols + c] : 0.f);
+    }
+}
+
+__global__ void gather_rows_kernel(const float* src, int64_t lds, const int32_t* idx, int rows, int cols, float* dst, int64_t ldd)
+{
+    const size_t total = size_t(rows) * cols;
+    for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < total; i += size_t(gridDim.x) * blockDim.x) {
+        const int r = int(i / cols), c = int(i % cols);
+        dst[size_t(r) * ldd + c] = src[size_t(idx[r]) * lds + c];
     }
 }
 
@@ -396,11 +406,20 @@ void heads_partial(void* qkv, int rows, int heads, const float* qn_w, const floa
     H3_CUDA(cudaGetLastError());
 }
 
-void pack_bf16_rows(const float* in, int rows, int cols, void* out, int ld_out, cudaStream_t s)
+void pack_bf16_rows(const float* in, int rows, int cols, void* out, int ld_out, cudaStream_t s, const int32_t* src_rows)
 {
     if (!rows)
         return;
-    pack_bf16_kernel<<<grid_for(size_t(rows) * ld_out, 256), 256, 0, s>>>(in, rows, cols, static_cast<__nv_bfloat16*>(out), ld_out);
+    pack_bf16_kernel<<<grid_for(size_t(rows) * ld_out, 256), 256, 0, s>>>(in, rows, cols, static_cast<__nv_bfloat16*>(out), ld_out,
+                                                                           src_rows);
+    H3_CUDA(cudaGetLastError());
+}
+
+void gather_rows_f32(const float* src, int64_t lds, const int32_t* idx, int rows, int cols, float* dst, int64_t ldd, cudaStream_t s)
+{
+    if (!rows)
+        return;
+    gather_rows_kernel<<<grid_for(size_t(rows) * cols, 256), 256, 0, s>>>(src, lds, idx, rows, cols, dst, ldd);
     H3_CUDA(cudaGetLastError());
 }
 

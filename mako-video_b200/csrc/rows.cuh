@@ -45,8 +45,12 @@ void quant_rows_i8_chunked(const void* x_bf16, int rows, int K, int chunks, int 
 void heads_partial(void* qkv_bf16, int rows, int heads, const float* qn_w, const float* kn_w, const float* rope, float eps,
                    cudaStream_t s);
 
-// fp32 rows -> bf16 rows of width ld_out (zero padding past `cols`).
-void pack_bf16_rows(const float* in, int rows, int cols, void* out_bf16, int ld_out, cudaStream_t s);
+// fp32 rows -> bf16 rows of width ld_out (zero padding past `cols`); output row r reads input row src_rows[r] when
+// src_rows is given.
+void pack_bf16_rows(const float* in, int rows, int cols, void* out_bf16, int ld_out, cudaStream_t s, const int32_t* src_rows = nullptr);
+
+// dst[r][c] = src[idx[r]][c] for c < cols (fp32).
+void gather_rows_f32(const float* src, int64_t lds, const int32_t* idx, int rows, int cols, float* dst, int64_t ldd, cudaStream_t s);
 
 // Synthetic parameters: value i of tensor `tensor_id` = mean + std * IH4(seed, tensor_id, i), IH4 the centred sum of
 // four 16-bit uniforms from a splitmix64 hash (an Irwin-Hall approximation of a unit normal), computed with exact

@@ -26,20 +26,17 @@ void sparse_sizes(const CubeGrid& g, float ratio, int local, int& kcap, int& q_t
 
 namespace {
 
+// One CTA per (cube, head), one thread per dim: the cube's rows are consecutive in the packed order.
 __global__ void cube_pool_kernel(const __nv_bfloat16* q, const __nv_bfloat16* k, int64_t rs, CubeGrid g, float* mq, float* mk)
 {
     const int c = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
-    const int cx = c % g.ncx, cy = (c / g.ncx) % g.ncy, ct = c / (g.ncx * g.ncy);
+    int first, n;
+    g.unit_span(c, first, n);
     float sq = 0.f, sk = 0.f;
-    int n = 0;
-    for (int kr = 0; kr < 64; ++kr) {
-        const int x = 4 * cx + (kr & 3), y = 4 * cy + ((kr >> 2) & 3), f = 4 * ct + (kr >> 4);
-        if (x >= g.pw || y >= g.ph || f >= g.frames)
-            continue;
-        const size_t row = size_t(g.dense_rows) + (size_t(f) * g.ph + y) * g.pw + x;
+    for (int r = 0; r < n; ++r) {
+        const size_t row = size_t(first + r);
         sq = __fadd_rn(sq, __bfloat162float(q[row * rs + h * 128 + d]));
         sk = __fadd_rn(sk, __bfloat162float(k[row * rs + h * 128 + d]));
-        ++n;
     }
     const size_t o = (size_t(h) * g.cubes() + c) * 128 + d;
     mq[o] = __fdiv_rn(sq, float(n));
@@ -183,19 +180,31 @@ __global__ void __launch_bounds__(TK_NT) cube_topk_kernel(const float* scores, C
 }
 
 // One thread per (head, video query tile): merge the two cubes' selections, append the dense units, pair them.
+// (first row, rows) of unit u, or (-1, 0) for none.
+__device__ __forceinline__ int2 span_of(int u, const CubeGrid& g)
+{
+    if (u < 0)
+        return make_int2(-1, 0);
+    int first, n;
+    g.unit_span(u, first, n);
+    return make_int2(first, n);
+}
+
 __global__ void build_passes_kernel(const int32_t* sel, const int32_t* nsel, int kcap, int heads, CubeGrid g, int4* blocks,
-                                    int32_t* nblocks, int2* q_units, int q_tiles, int max_blocks)
+                                    int32_t* nblocks, int4* q_rows, int q_tiles, int max_blocks)
 {
     const int nc = g.cubes(), nd = g.dense_units();
     const int vt = (nc + 1) / 2;
     const int idx = blockIdx.x * blockDim.x + threadIdx.x;
     if (idx < q_tiles) {
-        if (idx < vt)
-            q_units[idx] = make_int2(2 * idx, 2 * idx + 1 < nc ? 2 * idx + 1 : -1);
-        else {
+        int2 a, b;
+        if (idx < vt) {
+            a = span_of(2 * idx, g), b = span_of(2 * idx + 1 < nc ? 2 * idx + 1 : -1, g);
+        } else {
             const int t = idx - vt;
-            q_units[idx] = make_int2(nc + 2 * t, 2 * t + 1 < nd ? nc + 2 * t + 1 : -1);
+            a = span_of(nc + 2 * t, g), b = span_of(2 * t + 1 < nd ? nc + 2 * t + 1 : -1, g);
         }
+        q_rows[idx] = make_int4(a.x, b.x, a.y, b.y);
     }
     if (idx >= heads * q_tiles)
         return;
@@ -218,8 +227,9 @@ __global__ void build_passes_kernel(const int32_t* sel, const int32_t* nsel, int
         } else {
             // keep bit (2 * qh + kh): unit a is kh 0, unit b is kh 1
             const int keep = (pend_bits & 1) | ((bits & 1) << 1) | ((pend_bits & 2) << 1) | ((bits & 2) << 2);
+            const int2 sa = span_of(pend_u, g), sb = span_of(u, g);
             if (nout < max_blocks)
-                out[nout] = make_int4(pend_u, u, keep, 0);
+                out[nout] = make_int4(sa.x, sb.x, keep, sa.y | (sb.y << 8));
             ++nout;
             pend_u = -1;
         }
@@ -238,8 +248,9 @@ __global__ void build_passes_kernel(const int32_t* sel, const int32_t* nsel, int
         emit(nc + u, 3);
     if (pend_u >= 0) {
         const int keep = (pend_bits & 1) | ((pend_bits & 2) << 1);
+        const int2 sa = span_of(pend_u, g);
         if (nout < max_blocks)
-            out[nout] = make_int4(pend_u, -1, keep, 0);
+            out[nout] = make_int4(sa.x, -1, keep, sa.y);
         ++nout;
     }
     nblocks[idx] = min(nout, max_blocks);
@@ -276,10 +287,10 @@ void cube_topk(const float* scores, int heads, const CubeGrid& g, int k, int loc
 }
 
 void build_passes(const int32_t* sel, const int32_t* nsel, int kcap, int heads, const CubeGrid& g, int4* blocks, int32_t* nblocks,
-                  int2* q_units, int q_tiles, int max_blocks, cudaStream_t s)
+                  int4* q_rows, int q_tiles, int max_blocks, cudaStream_t s)
 {
     const int n = std::max(heads * q_tiles, q_tiles);
-    build_passes_kernel<<<(n + 127) / 128, 128, 0, s>>>(sel, nsel, kcap, heads, g, blocks, nblocks, q_units, q_tiles, max_blocks);
+    build_passes_kernel<<<(n + 127) / 128, 128, 0, s>>>(sel, nsel, kcap, heads, g, blocks, nblocks, q_rows, q_tiles, max_blocks);
     H3_CUDA(cudaGetLastError());
 }
 
@@ -288,11 +299,12 @@ void sparse_attention(const AttnParams& a, const CubeGrid& g, float ratio, int l
     cube_pool(a.q, a.k, a.row_stride, a.heads, g, b.mq, b.mk, s);
     cube_scores(b.mq, b.mk, a.heads, g.cubes(), b.scores, s);
     cube_topk(b.scores, a.heads, g, sparse_k(ratio, g.cubes()), local, b.sel, b.nsel, b.kcap, s);
-    build_passes(b.sel, b.nsel, b.kcap, a.heads, g, b.blocks, b.nblocks, b.q_units, b.q_tiles, b.max_blocks, s);
+    build_passes(b.sel, b.nsel, b.kcap, a.heads, g, b.blocks, b.nblocks, b.q_rows, b.q_tiles, b.max_blocks, s);
     AttnParams p = a;
+    p.rows = g.rows();
     p.blocks = b.blocks;
     p.nblocks = b.nblocks;
-    p.q_units = b.q_units;
+    p.q_rows = b.q_rows;
     p.q_tiles = b.q_tiles;
     p.max_blocks = b.max_blocks;
     p.grid = g;

@@ -108,6 +108,7 @@ SIGNATURES = {
     "h3k_sparse_sizes": (ctypes.c_int, [ctypes.POINTER(h3k_cube_grid), _F, _I32, _P, _P, _P, _P]),
     "h3k_sparse_select": (ctypes.c_int, [_P, _P, _I64, _I32, ctypes.POINTER(h3k_cube_grid), _F, _I32, _P, _P, _P, _P, _P, _P]),
     "h3k_cube_topk": (ctypes.c_int, [_P, _I32, ctypes.POINTER(h3k_cube_grid), _F, _I32, _P, _P, _P]),
+    "h3k_video_order": (ctypes.c_int, [ctypes.POINTER(h3k_cube_grid), _P]),
     "h3k_sparse_attention": (ctypes.c_int, [_P, _P, _P, _I64, _I32, ctypes.POINTER(h3k_cube_grid), _F, _I32, _P, _I64, _P]),
     "h3k_sparse_attention_noalloc": (ctypes.c_int, [_P, _P, _P, _I64, _I32, ctypes.POINTER(h3k_cube_grid), _F, _I32, _P, _I64, _P]),
     "h3k_fill_synthetic": (ctypes.c_int, [_P, _I32, _U64, _U64, _U32, _F, _F, _P]),
@@ -202,6 +203,15 @@ def rope_table(layout):
     out = np.zeros((S, 48, 2), np.float32)
     check(lib().h3_rope_table(ctypes.byref(layout.c), out.ctypes.data))
     return out
+
+
+def packed_order(dense_rows, frames, ph, pw):
+    """Row permutation of the packed order the h3k_sparse_* calls and the step use: packed row i holds layout row
+    order[i] (the dense rows keep their places; the generated video rows go cube by cube)."""
+    g = h3k_cube_grid(dense_rows, frames, ph, pw)
+    src = np.zeros(frames * ph * pw, np.int32)
+    check(lib().h3k_video_order(ctypes.byref(g), src.ctypes.data))
+    return np.concatenate([np.arange(dense_rows, dtype=np.int64), dense_rows + src.astype(np.int64)])
 
 
 def nccl_unique_id():

@@ -198,6 +198,23 @@ def test_sparse_sizes_for_768p():
     assert exact.sparse_k(0.1, 528) == 53
 
 
+@pytest.mark.parametrize("dims", [(768, 32, 24, 42), (5, 6, 7, 10), (0, 3, 2, 5), (64, 4, 4, 4)])
+def test_packed_order_puts_each_cube_in_one_run(dims):
+    """h3k_video_order: a permutation that lists the generated video rows cube by cube (cubes in (frame group, row
+    group, column group) order, rows inside a cube in (frame, row, column) order), dense rows first and unmoved."""
+    D, F, ph, pw = dims
+    order = h3b200.packed_order(D, F, ph, pw)
+    want = list(range(D))
+    for ct in range(0, F, 4):
+        for cy in range(0, ph, 4):
+            for cx in range(0, pw, 4):
+                for f in range(ct, min(ct + 4, F)):
+                    for y in range(cy, min(cy + 4, ph)):
+                        for x in range(cx, min(cx + 4, pw)):
+                            want.append(D + (f * ph + y) * pw + x)
+    assert order.tolist() == want
+
+
 def test_create_refuses_checkpoint_paths_without_touching_the_gpu():
     L = h3b200.lib()
     cfg = h3b200.make_config("c1")

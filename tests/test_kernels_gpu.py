@@ -293,12 +293,19 @@ def sparse_case(cuda, dense_rows=70, frames=5, ph=6, pw=7, Hh=2, seed=0):
     return qkv.bfloat16(), H.h3k_cube_grid(dense_rows, frames, ph, pw)
 
 
+def packed(grid):
+    """(order, inverse): the sparse calls take rows in the packed order, packed row i = layout row order[i]."""
+    order = torch.from_numpy(H.packed_order(grid.dense_rows, grid.frames, grid.ph, grid.pw))
+    return order, torch.argsort(order)
+
+
 @pytest.mark.parametrize("ratio,local", [(0.1, 1), (0.3, 3), (0.5, 0), (1.0, 0)])
 def test_sparse_selection_bit_exact(cuda, ratio, local):
     """cube_pool, cube_scores and cube_topk against the exact CPU restatement: identical means, scores, indices."""
     qkv, grid = sparse_case(cuda)
     Hh = qkv.shape[2]
-    t = qkv.to(cuda)
+    order, _ = packed(grid)
+    t = qkv[order].contiguous().to(cuda)
     nc, kcap = ctypes.c_int32(), ctypes.c_int32()
     H.check(H.lib().h3k_sparse_sizes(ctypes.byref(grid), ratio, local, ctypes.byref(nc), ctypes.byref(kcap), None, None))
     nc, kcap = nc.value, kcap.value
@@ -350,11 +357,13 @@ def allowed_mask(S, D, frames, ph, pw, sel, nsel):
 def test_sparse_attention(cuda, ratio, local):
     qkv, grid = sparse_case(cuda, seed=1)
     S, _, Hh, _ = qkv.shape
-    t = qkv.to(cuda)
-    out = torch.zeros(S, Hh, 128, device=cuda, dtype=torch.bfloat16)
+    order, inverse = packed(grid)
+    t = qkv[order].contiguous().to(cuda)
+    out_packed = torch.zeros(S, Hh, 128, device=cuda, dtype=torch.bfloat16)
     H.check(H.lib().h3k_sparse_attention(ptr(t[:, 0]), ptr(t[:, 1]), ptr(t[:, 2]), 3 * Hh * 128, Hh, ctypes.byref(grid), ratio, local,
-                                         ptr(out), Hh * 128, stream()))
+                                         ptr(out_packed), Hh * 128, stream()))
     sync()
+    out = out_packed.cpu()[inverse]
     bits = qkv.contiguous().view(torch.int16).numpy().view(np.uint16).reshape(-1)
     mq, mk = exact.cube_pool(bits, bits[Hh * 128:], 3 * Hh * 128, Hh, grid.dense_rows, grid.frames, grid.ph, grid.pw)
     sel, nsel = exact.cube_topk(exact.cube_scores(mq, mk), grid.frames, grid.ph, grid.pw, ratio, local)
@@ -363,10 +372,10 @@ def test_sparse_attention(cuda, ratio, local):
     r = rel(out.float(), want)
     assert r < 1e-2, r
     if ratio == 1.0:
-        dense = torch.zeros_like(out)
+        dense = torch.zeros_like(out_packed)
         H.check(H.lib().h3k_attention(ptr(t[:, 0]), ptr(t[:, 1]), ptr(t[:, 2]), 3 * Hh * 128, Hh, S, ptr(dense), Hh * 128, stream()))
         sync()
-        assert rel(out.float(), dense.float()) < 1e-2  # every cube selected = dense (tests/CMakeLists.txt:9-12)
+        assert rel(out_packed.float(), dense.float()) < 1e-2  # every cube selected = dense (tests/CMakeLists.txt:9-12)
 
 
 # ---------------------------------------------------------------------------------- time embedding and AdaLN
@@ -409,3 +418,19 @@ def test_time_mlp_adaln_and_heads(cuda):
     H.check(H.lib().h3k_heads(ptr(c(x)), 256, 200, ptr(c(w["hv_w"])), ptr(c(w["hv_b"])), 96, 256, ptr(out), 128, stream()))
     sync()
     assert rel(out[:, :96], x @ w["hv_w"].T + w["hv_b"]) < 1e-5
+
+
+def test_host_pointers_are_refused_before_any_launch(cuda):
+    """A plain host buffer handed to a kernel entry point is an argument error, not a kernel fault."""
+    Hh, S = 2, 128
+    t = torch.zeros(S, 3, Hh, 128, device=cuda, dtype=torch.bfloat16)
+    host_out = np.zeros((S, Hh, 128), np.uint16)
+    rc = H.lib().h3k_attention(ptr(t[:, 0]), ptr(t[:, 1]), ptr(t[:, 2]), 3 * Hh * 128, Hh, S, ctypes.c_void_p(host_out.ctypes.data),
+                               Hh * 128, stream())
+    assert rc == H.H3_ERR_ARG
+    assert b"host memory" in H.lib().h3_last_error()
+    grid = H.h3k_cube_grid(64, 4, 4, 4)
+    rc = H.lib().h3k_sparse_attention(ctypes.c_void_p(host_out.ctypes.data), ptr(t[:, 1]), ptr(t[:, 2]), 3 * Hh * 128, Hh,
+                                      ctypes.byref(grid), 0.5, 1, ptr(t[:, 0]), Hh * 128, stream())
+    assert rc == H.H3_ERR_ARG
+    sync()  # the context is intact
