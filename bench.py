@@ -340,7 +340,7 @@ def run_ours(args, rank, world, local_rank):
                    "l2": "no flush: each step streams ~54 GB of weights, far past the 126 MB L2"},
         "roofline": {"bound": "tensor", "kernel": "attention (flash_attn, tcgen05)", "achieved": achieved, "peak": peak,
                      "unit": "TFLOP/s", "frac": (achieved / peak) if achieved else None,
-                     "traffic": load_traffic("attn_kernel", args.workload) if world == 1 else None,
+                     "traffic": load_traffic("attention", args.workload) if world == 1 else None,
                      "peak_kind": f"{peak_kind} bf16 sustained",
                      "launch_flops": attn_launch, "launch_ms": attn_ms / max(attn_n, 1) if attn_n else None,
                      "gemm_tflops": gemm_tflops, "gemm_frac": gemm_tflops / peak if gemm_tflops else None},
