@@ -36,8 +36,20 @@ typedef struct h3_config {
     float eps;               /* RMS norm epsilon */
 } h3_config;
 
-/* The packed sequence [text | keyframe rows | audio | generated video] (H3::Layout, src/video/engine.cpp:666-676;
- * tests/h3_ref_test.cpp:194). References (ref2va) are not supported: a layout with them is refused. */
+/* A reference block of a ref2va layout (H3::Layout::Reference, src/video/engine.cpp:604-616;
+ * tests/h3_ref_test.cpp:475-479): a picture (frames 1, h x w latents), a video (frames latent frames of h x w, audio
+ * soundtrack latents or 0) or a soundtrack (audio latents). Its visual rows are held at t = 0.999, its audio rows at
+ * t = 1 (docs/architecture.md:38-42, 203-215). */
+enum { H3_REF_IMAGE = 0, H3_REF_VIDEO = 1, H3_REF_AUDIO = 2 };
+typedef struct h3_layout_ref {
+    int32_t kind;
+    uint32_t frames, h, w, audio;
+} h3_layout_ref;
+
+/* The packed sequence [text | keyframe rows or reference blocks | audio | generated video] (H3::Layout,
+ * src/video/engine.cpp:666-676; tests/h3_ref_test.cpp:194, 476-481). The video input/output rows are the conditioning
+ * rows (keyframes, or the references' pictures and videos in reading order) then the generated rows; the audio rows
+ * are the references' soundtracks (reading order) then the generated audio. */
 typedef struct h3_layout {
     uint32_t text;        /* text rows T */
     uint32_t frames;      /* generated latent frames */
@@ -46,6 +58,8 @@ typedef struct h3_layout {
     uint32_t cond_frames; /* keyframe latent frames (rows held at t = 0.999) */
     const uint8_t* cond_last; /* [cond_frames]: keyframe anchored at the last generated frame (NULL: all first) */
     const uint8_t* text_tags; /* [text]: modality tag per text row, 1 text or 0 video (NULL: all text) */
+    const h3_layout_ref* refs; /* [n_refs] reference blocks in reading order (NULL when n_refs is 0) */
+    uint32_t n_refs;
 } h3_layout;
 
 typedef struct h3_world {

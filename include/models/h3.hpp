@@ -29,19 +29,46 @@ public:
     enum Int8 : uint32_t { qkv = 1, out = 2, fc1 = 4, fc2 = 8 };
 
     struct Layout {
+        // A reference block (ref2va): a picture (frames 1), a video (frames, h, w and its soundtrack's audio latents)
+        // or a soundtrack (audio latents) (src/video/engine.cpp:604-616; tests/h3_ref_test.cpp:475-479).
+        struct Reference {
+            enum class Kind : int32_t { image = H3_REF_IMAGE, video = H3_REF_VIDEO, audio = H3_REF_AUDIO };
+            Kind kind = Kind::image;
+            uint32_t frames = 0, h = 0, w = 0, audio = 0;
+        };
         uint32_t text = 0, frames = 0, h = 0, w = 0, audio = 0, cond_frames = 0;
         std::vector<uint8_t> cond_last; // per keyframe: anchored at the last generated frame
+        std::vector<Reference> refs;    // reference blocks in reading order
         std::vector<uint8_t> text_tags; // per text row: 1 text, 0 video (a vision block's rows)
         uint32_t patch_rows() const { return (h / 2) * (w / 2); }
-        uint32_t cond_rows() const { return cond_frames * patch_rows(); }
-        uint32_t video_rows() const { return (cond_frames + frames) * patch_rows(); }
-        uint32_t audio_rows() const { return 2 * audio; }
-        uint32_t cond_audio_rows() const { return 0; } // references are not supported
-        uint32_t rows() const { return text + video_rows() + audio_rows(); }
-        h3_layout c() const
+        uint32_t cond_rows() const
         {
+            uint32_t n = cond_frames * patch_rows();
+            for (const Reference& r : refs)
+                if (r.kind != Reference::Kind::audio)
+                    n += (r.kind == Reference::Kind::image ? 1 : r.frames) * (r.h / 2) * (r.w / 2);
+            return n;
+        }
+        uint32_t cond_audio_rows() const
+        {
+            uint32_t n = 0;
+            for (const Reference& r : refs)
+                if (r.kind != Reference::Kind::image)
+                    n += 2 * r.audio;
+            return n;
+        }
+        uint32_t video_rows() const { return cond_rows() + frames * patch_rows(); }
+        uint32_t audio_rows() const { return cond_audio_rows() + 2 * audio; }
+        uint32_t rows() const { return text + video_rows() + audio_rows(); }
+        // The C view; `refs_c` holds the reference blocks it points at.
+        h3_layout c(std::vector<h3_layout_ref>& refs_c) const
+        {
+            refs_c.clear();
+            for (const Reference& r : refs)
+                refs_c.push_back(h3_layout_ref{int32_t(r.kind), r.frames, r.h, r.w, r.audio});
             return h3_layout{text, frames, h, w, audio, cond_frames, cond_last.empty() ? nullptr : cond_last.data(),
-                             text_tags.empty() ? nullptr : text_tags.data()};
+                             text_tags.empty() ? nullptr : text_tags.data(), refs_c.empty() ? nullptr : refs_c.data(),
+                             uint32_t(refs_c.size())};
         }
     };
 
@@ -84,7 +111,8 @@ public:
     // begin(text [T][5120], layout) (src/video/engine.cpp:700).
     void begin(std::span<const float> text, const Layout& l)
     {
-        const h3_layout c = l.c();
+        std::vector<h3_layout_ref> refs;
+        const h3_layout c = l.c(refs);
         check(h3_begin(m_, text.data(), uint32_t(text.size() / kText), &c));
         layout_ = l;
     }
@@ -110,7 +138,8 @@ public:
     // H3::rows(layout) (tests/h3_ref_test.cpp:484-502).
     static Rows rows(const Layout& l)
     {
-        const h3_layout c = l.c();
+        std::vector<h3_layout_ref> refs;
+        const h3_layout c = l.c(refs);
         const uint64_t S = h3_layout_rows(&c);
         Rows r;
         r.pos.resize(S * 3);

@@ -87,6 +87,24 @@ h3::Layout to_layout(const h3_layout* l)
         o.cond_last.assign(l->cond_last, l->cond_last + l->cond_frames);
     if (l->text_tags)
         o.text_tags.assign(l->text_tags, l->text_tags + l->text);
+    if (l->n_refs && !l->refs)
+        throw ArgError("layout: n_refs without refs");
+    for (uint32_t i = 0; i < l->n_refs; ++i) {
+        const h3_layout_ref& r = l->refs[i];
+        if (r.kind < H3_REF_IMAGE || r.kind > H3_REF_AUDIO)
+            throw ArgError("layout: reference kind 0 picture, 1 video, 2 soundtrack");
+        h3::LayoutRef x;
+        x.kind = r.kind, x.frames = int(r.frames), x.h = int(r.h), x.w = int(r.w), x.audio = int(r.audio);
+        if (x.kind == h3::LayoutRef::kImage)
+            x.frames = 1, x.audio = 0;
+        if (x.kind == h3::LayoutRef::kAudio)
+            x.frames = x.h = x.w = 0;
+        if (x.kind != h3::LayoutRef::kAudio && (x.h <= 0 || x.w <= 0 || x.h % 2 || x.w % 2 || x.frames <= 0))
+            throw ArgError("layout: a reference picture or video needs frames and even latent sides");
+        o.refs.push_back(x);
+    }
+    if (o.cond_frames > 0 && !o.refs.empty())
+        throw ArgError("layout: keyframes or reference blocks, not both");
     if (o.h % 2 || o.w % 2)
         throw ArgError("layout: the latent height and width must be even");
     return o;

@@ -31,6 +31,12 @@ double video_time(int f)
 
 } // namespace
 
+// Positions follow docs/architecture.md:35-45 (text, keyframes, audio, video) and :203-215 (reference blocks): the
+// media rows share one time clock that starts at the text's length; a picture sits at one slot and advances the
+// clock by one, a soundtrack one slot a latent, a video's soundtrack and frames start together and advance the clock
+// by the longer of the two spans (its frames spaced as the generated video's); the generated audio and video rows
+// start where the clock ends. The spatial axes are each block's own latent grid centred on the unit square; audio
+// rows sit at the two ends of the width axis of the grid they belong to (a video's own, else the generated one's).
 Rows layout_rows(const Layout& l)
 {
     Rows r;
@@ -38,38 +44,78 @@ Rows layout_rows(const Layout& l)
     r.pos.assign(size_t(S) * 3, 0.0);
     r.tags.assign(S, 0);
     r.roles.assign(S, 0);
-    const int ph = l.h / 2, pw = l.w / 2;
-    const double norm = std::sqrt(double(ph) * pw);
-    auto hpos = [&](int y) { return (y + 0.5 - ph / 2.0) / norm * 32.0; };
-    auto wpos = [&](int x) { return (x + 0.5 - pw / 2.0) / norm * 32.0; };
+    struct Grid {
+        int ph, pw;
+        double norm;
+        double hpos(int y) const { return (y + 0.5 - ph / 2.0) / norm * 32.0; }
+        double wpos(int x) const { return (x + 0.5 - pw / 2.0) / norm * 32.0; }
+    };
+    auto grid_of = [](int h, int w) { return Grid{h / 2, w / 2, std::sqrt(double(h / 2) * (w / 2))}; };
+    const Grid gen = grid_of(l.h, l.w);
     int row = 0;
-    for (int i = 0; i < l.text; ++i, ++row) {
-        r.pos[3 * row] = i;
-        r.tags[row] = l.text_tags.empty() ? 1 : l.text_tags[i];
-        r.roles[row] = 0;
-    }
-    const double t0 = l.text;
+    auto put = [&](double t, double y, double x, uint8_t tag, uint8_t role) {
+        r.pos[3 * row] = t, r.pos[3 * row + 1] = y, r.pos[3 * row + 2] = x;
+        r.tags[row] = tag, r.roles[row] = role;
+        ++row;
+    };
+    auto frame_rows = [&](const Grid& g, double t, uint8_t role) {
+        for (int y = 0; y < g.ph; ++y)
+            for (int x = 0; x < g.pw; ++x)
+                put(t, g.hpos(y), g.wpos(x), 0, role);
+    };
+    auto audio_rows = [&](const Grid& g, double t, int n, uint8_t role) {
+        for (int c = 0; c < 2; ++c)
+            for (int a = 0; a < n; ++a)
+                put(t + a, 0.0, g.wpos(c == 0 ? 0 : g.pw - 1), 2, role);
+    };
+    for (int i = 0; i < l.text; ++i)
+        put(i, 0.0, 0.0, l.text_tags.empty() ? 1 : l.text_tags[i], 0);
+    double clock = l.text;
     for (int k = 0; k < l.cond_frames; ++k) {
         const bool last = k < int(l.cond_last.size()) && l.cond_last[k];
-        const double t = t0 + video_time(last ? std::max(l.frames - 1, 0) : 0);
-        for (int y = 0; y < ph; ++y)
-            for (int x = 0; x < pw; ++x, ++row) {
-                r.pos[3 * row] = t, r.pos[3 * row + 1] = hpos(y), r.pos[3 * row + 2] = wpos(x);
-                r.tags[row] = 0, r.roles[row] = 1;
-            }
+        frame_rows(gen, clock + video_time(last ? std::max(l.frames - 1, 0) : 0), 1);
     }
-    for (int c = 0; c < 2; ++c)
-        for (int a = 0; a < l.audio; ++a, ++row) {
-            r.pos[3 * row] = t0 + a, r.pos[3 * row + 1] = 0.0, r.pos[3 * row + 2] = wpos(c == 0 ? 0 : pw - 1);
-            r.tags[row] = 2, r.roles[row] = 3;
+    for (const LayoutRef& ref : l.refs) {
+        if (ref.kind == LayoutRef::kImage) {
+            frame_rows(grid_of(ref.h, ref.w), clock, 1);
+            clock += 1.0;
+        } else if (ref.kind == LayoutRef::kAudio) {
+            audio_rows(gen, clock, ref.audio, 2);
+            clock += ref.audio;
+        } else {
+            const Grid g = grid_of(ref.h, ref.w);
+            audio_rows(g, clock, ref.audio, 2);
+            for (int f = 0; f < ref.frames; ++f)
+                frame_rows(g, clock + video_time(f), 1);
+            clock += std::max(double(ref.audio), video_time(ref.frames));
         }
+    }
+    audio_rows(gen, clock, l.audio, 3);
     for (int f = 0; f < l.frames; ++f)
-        for (int y = 0; y < ph; ++y)
-            for (int x = 0; x < pw; ++x, ++row) {
-                r.pos[3 * row] = t0 + video_time(f), r.pos[3 * row + 1] = hpos(y), r.pos[3 * row + 2] = wpos(x);
-                r.tags[row] = 0, r.roles[row] = 4;
-            }
+        frame_rows(gen, clock + video_time(f), 4);
     return r;
+}
+
+std::vector<Segment> layout_segments(const Layout& l)
+{
+    const Rows r = layout_rows(l);
+    std::vector<Segment> out;
+    int in_video = 0, in_audio = 0;
+    const int S = int(r.roles.size());
+    for (int i = 0; i < S;) {
+        int j = i;
+        while (j < S && r.roles[j] == r.roles[i])
+            ++j;
+        const int role = r.roles[i];
+        Segment sg{i, j - i, role, -1};
+        if (role == 1 || role == 4)
+            sg.input_row = in_video, in_video += j - i;
+        else if (role == 2 || role == 3)
+            sg.input_row = in_audio, in_audio += j - i;
+        out.push_back(sg);
+        i = j;
+    }
+    return out;
 }
 
 void rope_inv_freq(float out[16])
@@ -202,7 +248,9 @@ struct Model::Impl {
     CubeGrid grid;
     std::vector<int32_t> h_video_src;
     DevBuf video_src, video_dst, out_video_rows;
-    std::vector<uint8_t> h_tags, h_roles, h_lvl_kind; // per global row; lvl_kind: 0 video/text level, 1 audio, 2 cond
+    // per global row; lvl_kind: 0 video/text level, 1 audio, 2 conditioning video (0.999), 3 reference audio (1)
+    std::vector<uint8_t> h_tags, h_roles, h_lvl_kind;
+    std::vector<Segment> segs;
     // per step
     DevBuf emb, th, temb, tsilu, mods, fmods;
     DevBuf x, h, hq, hs, qkv, qkv_recv, o, o_recv, act;
@@ -427,6 +475,12 @@ void Model::begin(const float* text, int T, const Layout& l)
         throw CudaError("begin: the latent grid must have even sides");
     if (!l.text_tags.empty() && int(l.text_tags.size()) != T)
         throw CudaError("begin: one text tag per text row");
+    if (l.cond_frames > 0 && !l.refs.empty())
+        throw CudaError("begin: a layout holds keyframes or reference blocks, not both");
+    for (const LayoutRef& ref : l.refs)
+        if (ref.kind < LayoutRef::kImage || ref.kind > LayoutRef::kAudio || ref.frames < 0 || ref.audio < 0 || ref.h % 2 || ref.w % 2 ||
+            (ref.kind == LayoutRef::kImage && ref.frames != 1) || (ref.kind != LayoutRef::kAudio && (ref.h <= 0 || ref.w <= 0)))
+            throw CudaError("begin: bad reference block (a picture is one latent frame; pictures and videos need even sides)");
     layout_ = l;
     S_ = l.rows();
     if (S_ <= 0)
@@ -490,7 +544,8 @@ void Model::begin(const float* text, int T, const Layout& l)
     d_->h_roles = r.roles;
     d_->h_lvl_kind.assign(S_, 0);
     for (int i = 0; i < S_; ++i)
-        d_->h_lvl_kind[i] = r.roles[i] == 3 ? 1 : (r.roles[i] == 1 ? 2 : 0);
+        d_->h_lvl_kind[i] = r.roles[i] == 3 ? 1 : (r.roles[i] == 1 ? 2 : (r.roles[i] == 2 ? 3 : 0));
+    d_->segs = layout_segments(l);
     const std::vector<float> rope = rope_table(r);
     std::vector<float> local(size_t(S_local_) * 96, 0.f);
     for (int i = 0; i < S_local_ && row0_ + i < S_; ++i)
@@ -547,12 +602,13 @@ void Model::step(const float* video, const float* audio, float t_video, float t_
     const Layout& l = layout_;
     const int d = c_.dim, inner = c_.inner(), F = c_.ffn, td = c_.time_dim, L = c_.blocks;
     const int P = world_.size, Hp = c_.heads / P;
-    const int T = l.text, C = l.cond_rows(), A = l.audio_rows(), V = l.video_rows(), D = l.dense_rows();
+    const int T = l.text, C = l.cond_rows(), CA = l.cond_audio_rows(), A = l.audio_rows(), V = l.video_rows(), D = l.dense_rows();
     const int M = S_local_;
     launches_ = 0;
     stage_ms_.clear();
 
-    // ---- noise levels: the video / text level, the audio level, the conditioning level (max(t_video, 0.999))
+    // ---- noise levels: the video / text level, the audio level, the conditioning video level (max(t_video, 0.999)),
+    // the reference audio level (1, clean)
     const float t_cond = std::max(t_video, 0.999f);
     std::vector<float> levels;
     auto level_of = [&](float t) {
@@ -563,15 +619,16 @@ void Model::step(const float* video, const float* audio, float t_video, float t_
         return int(levels.size() - 1);
     };
     const int lv_video = level_of(t_video);
-    const int lv_audio = A > 0 ? level_of(t_audio) : lv_video;
+    const int lv_audio = A - CA > 0 ? level_of(t_audio) : lv_video;
     const int lv_cond = C > 0 ? level_of(t_cond) : lv_video;
+    const int lv_ref_audio = CA > 0 ? level_of(1.0f) : lv_video;
     const int U = int(levels.size());
     {
         std::vector<uint8_t> midx(M, 0), lidx(M, 0);
         for (int i = 0; i < M && row0_ + i < S_; ++i) {
             const int g = row0_ + i;
             const int kind = d_->h_lvl_kind[g];
-            const int lv = kind == 1 ? lv_audio : (kind == 2 ? lv_cond : lv_video);
+            const int lv = kind == 1 ? lv_audio : (kind == 2 ? lv_cond : (kind == 3 ? lv_ref_audio : lv_video));
             lidx[i] = uint8_t(lv);
             midx[i] = uint8_t(lv * 3 + d_->h_tags[g]);
         }
@@ -677,9 +734,12 @@ void Model::step(const float* video, const float* audio, float t_video, float t_
         gemm_bf16(A0, w.p, g, Epi::f32, s);
         ++launches_;
     };
-    proj(d_->pk_video.p, c_.video_patch, 0, T, C, d_->vp_w, d_->vp_b, c_.video_patch);           // keyframe rows
-    proj(d_->pk_audio.p, 64, 0, T + C, A, d_->ap_w, d_->ap_b, 64);                               // audio rows
-    proj(d_->pk_video.p, c_.video_patch, C, D, V - C, d_->vp_w, d_->vp_b, c_.video_patch);       // generated video
+    for (const Segment& sg : d_->segs) {
+        if (sg.role == 1 || sg.role == 4) // conditioning and generated video rows (the generated ones packed)
+            proj(d_->pk_video.p, c_.video_patch, sg.input_row, sg.row0, sg.rows, d_->vp_w, d_->vp_b, c_.video_patch);
+        else if (sg.role == 2 || sg.role == 3) // reference and generated audio rows
+            proj(d_->pk_audio.p, 64, sg.input_row, sg.row0, sg.rows, d_->ap_w, d_->ap_b, 64);
+    }
     mark("input");
     if (P == 1)
         emit_probe("x0", -1, x, size_t(S_) * d, true);
@@ -856,19 +916,29 @@ void Model::step(const float* video, const float* audio, float t_video, float t_
         heads_f32(xn + size_t(a - r0) * d, d, bnd - a, w.as<float>(), b.as<float>(), N, d, ro + size_t(a - r0) * 128, 128, s);
         ++launches_;
     };
-    head(T, C, d_->hv_w, d_->hv_b, c_.video_patch);
-    head(T + C, A, d_->ha_w, d_->ha_b, c_.audio_channels);
-    head(D, V - C, d_->hv_w, d_->hv_b, c_.video_patch);
+    for (const Segment& sg : d_->segs) {
+        if (sg.role == 1 || sg.role == 4)
+            head(sg.row0, sg.rows, d_->hv_w, d_->hv_b, c_.video_patch);
+        else if (sg.role == 2 || sg.role == 3)
+            head(sg.row0, sg.rows, d_->ha_w, d_->ha_b, c_.audio_channels);
+    }
     const float* all = ro;
     if (P > 1) {
         H3_NCCL(ncclAllGather(ro, d_->rows_all.p, size_t(M) * 128, ncclFloat32, d_->comm, s));
         all = d_->rows_all.as<float>();
     }
     mark("final");
-    // ---- outputs: video rows (keyframe rows first, then generated) and audio rows
+    // ---- outputs: video rows (conditioning rows first, then generated) and audio rows (reference rows first), in
+    // the inputs' row order
     const cudaMemcpyKind kind = device_io ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost;
-    if (C)
-        H3_CUDA(cudaMemcpy2DAsync(out_video, c_.video_patch * 4, all + size_t(T) * 128, 128 * 4, c_.video_patch * 4, C, kind, s));
+    for (const Segment& sg : d_->segs) {
+        if (sg.role == 1)
+            H3_CUDA(cudaMemcpy2DAsync(out_video + size_t(sg.input_row) * c_.video_patch, c_.video_patch * 4, all + size_t(sg.row0) * 128,
+                                      128 * 4, c_.video_patch * 4, sg.rows, kind, s));
+        else if (sg.role == 2 || sg.role == 3)
+            H3_CUDA(cudaMemcpy2DAsync(out_audio + size_t(sg.input_row) * c_.audio_channels, c_.audio_channels * 4,
+                                      all + size_t(sg.row0) * 128, 128 * 4, c_.audio_channels * 4, sg.rows, kind, s));
+    }
     if (V - C) {
         // back to the layout's row order
         float* vo = device_io ? out_video + size_t(C) * c_.video_patch : d_->out_video_rows.as<float>();
@@ -878,8 +948,6 @@ void Model::step(const float* video, const float* audio, float t_video, float t_
             H3_CUDA(cudaMemcpyAsync(out_video + size_t(C) * c_.video_patch, vo, size_t(V - C) * c_.video_patch * 4,
                                     cudaMemcpyDeviceToHost, s));
     }
-    if (A)
-        H3_CUDA(cudaMemcpy2DAsync(out_audio, c_.audio_channels * 4, all + size_t(T + C) * 128, 128 * 4, c_.audio_channels * 4, A, kind, s));
     if (timing_) {
         H3_CUDA(cudaStreamSynchronize(s));
         for (size_t i = 1; i < ev_used; ++i)

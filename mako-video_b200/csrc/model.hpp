@@ -23,6 +23,18 @@ struct Config {
 
 // The packed sequence [text | conditioning video | audio | generated video] of one request
 // (mirrors the reference's H3::Layout; references are not supported).
+// A reference block of a ref2va layout (H3::Layout::Reference, src/video/engine.cpp:604-616): a picture (one latent
+// frame of h x w latents), a video (`frames` latent frames of h x w, with `audio` soundtrack latents or none) or a
+// soundtrack alone (`audio` latents).
+struct LayoutRef {
+    enum Kind : int { kImage = 0, kVideo = 1, kAudio = 2 };
+    int kind = kImage;
+    int frames = 0, h = 0, w = 0, audio = 0;
+    int visual_rows() const { return kind == kAudio ? 0 : (kind == kImage ? 1 : frames) * (h / 2) * (w / 2); }
+    int audio_rows() const { return kind == kImage ? 0 : 2 * audio; }
+};
+
+// The packed sequence [text | keyframe rows or reference blocks | audio | generated video].
 struct Layout {
     int text = 0;              // text rows T
     int frames = 0, h = 0, w = 0; // generated video: latent frames and latent height / width (2x2 patches a row)
@@ -30,12 +42,28 @@ struct Layout {
     int cond_frames = 0;       // keyframe latent frames (each h/2 * w/2 rows at t = 0.999), ahead of the audio rows
     std::vector<uint8_t> cond_last; // per keyframe: anchored at the last generated frame (else the first)
     std::vector<uint8_t> text_tags; // per text row: modality tag (1 text, 0 video); empty: all text
+    std::vector<LayoutRef> refs;    // reference blocks in reading order (ref2va)
     int patch_rows() const { return (h / 2) * (w / 2); }
-    int video_rows() const { return (cond_frames + frames) * patch_rows(); } // conditioning + generated
-    int cond_rows() const { return cond_frames * patch_rows(); }
-    int audio_rows() const { return 2 * audio; }
+    // conditioning video rows: keyframes and the references' pictures and videos (the first rows of the video input)
+    int cond_rows() const
+    {
+        int n = cond_frames * patch_rows();
+        for (const LayoutRef& r : refs)
+            n += r.visual_rows();
+        return n;
+    }
+    // conditioning audio rows: the references' soundtracks (the first rows of the audio input)
+    int cond_audio_rows() const
+    {
+        int n = 0;
+        for (const LayoutRef& r : refs)
+            n += r.audio_rows();
+        return n;
+    }
+    int video_rows() const { return cond_rows() + frames * patch_rows(); } // conditioning + generated
+    int audio_rows() const { return cond_audio_rows() + 2 * audio; }
     int rows() const { return text + video_rows() + audio_rows(); }
-    int dense_rows() const { return text + cond_rows() + audio_rows(); }
+    int dense_rows() const { return rows() - frames * patch_rows(); } // every row before the generated video
 };
 
 // Per-row metadata of a layout (the reference's H3::rows): rotary positions (t, h, w) in double, modality tag
@@ -45,6 +73,13 @@ struct Rows {
     std::vector<uint8_t> tags, roles;
 };
 Rows layout_rows(const Layout& l);
+
+// Runs of rows with one role, in sequence order, and where each run's rows come from in the step's inputs: video
+// roles (1, 4) from the video rows, audio roles (2, 3) from the audio rows, in order (input_row -1 for text).
+struct Segment {
+    int row0 = 0, rows = 0, role = 0, input_row = -1;
+};
+std::vector<Segment> layout_segments(const Layout& l);
 
 // The rotary frequencies: 16 per axis, base 10000 (1 / 10000^(2i/32) in float).
 void rope_inv_freq(float out[16]);

@@ -50,10 +50,18 @@ class h3_config(ctypes.Structure):
                 ("audio_channels", ctypes.c_uint32), ("eps", ctypes.c_float)]
 
 
+class h3_layout_ref(ctypes.Structure):
+    _fields_ = [("kind", ctypes.c_int32), ("frames", ctypes.c_uint32), ("h", ctypes.c_uint32), ("w", ctypes.c_uint32),
+                ("audio", ctypes.c_uint32)]
+
+
+REF_KINDS = {"image": 0, "video": 1, "audio": 2}
+
+
 class h3_layout(ctypes.Structure):
     _fields_ = [("text", ctypes.c_uint32), ("frames", ctypes.c_uint32), ("h", ctypes.c_uint32), ("w", ctypes.c_uint32),
                 ("audio", ctypes.c_uint32), ("cond_frames", ctypes.c_uint32), ("cond_last", ctypes.c_void_p),
-                ("text_tags", ctypes.c_void_p)]
+                ("text_tags", ctypes.c_void_p), ("refs", ctypes.POINTER(h3_layout_ref)), ("n_refs", ctypes.c_uint32)]
 
 
 class h3_world(ctypes.Structure):
@@ -148,15 +156,22 @@ def make_config(name_or_dict, eps=1e-6):
 
 
 class Layout:
-    """An h3_layout plus the arrays it points at (kept alive with it)."""
+    """An h3_layout plus the arrays it points at (kept alive with it). refs: reference blocks in reading order, each
+    a dict(kind="image"|"video"|"audio", frames=, h=, w=, audio=)."""
 
-    def __init__(self, text, frames, h, w, audio=0, cond_frames=0, cond_last=None, text_tags=None):
-        self.d = dict(text=text, frames=frames, h=h, w=w, audio=audio, cond_frames=cond_frames)
+    def __init__(self, text, frames, h, w, audio=0, cond_frames=0, cond_last=None, text_tags=None, refs=None):
+        self.refs = [dict(kind=r["kind"], frames=1 if r["kind"] == "image" else r.get("frames", 0),
+                          h=r.get("h", 0) if r["kind"] != "audio" else 0, w=r.get("w", 0) if r["kind"] != "audio" else 0,
+                          audio=r.get("audio", 0) if r["kind"] != "image" else 0) for r in (refs or [])]
+        self.d = dict(text=text, frames=frames, h=h, w=w, audio=audio, cond_frames=cond_frames, refs=self.refs)
         self._cl = None if cond_last is None else np.ascontiguousarray(cond_last, dtype=np.uint8)
         self._tt = None if text_tags is None else np.ascontiguousarray(text_tags, dtype=np.uint8)
+        self._refs = (h3_layout_ref * max(len(self.refs), 1))(
+            *[h3_layout_ref(REF_KINDS[r["kind"]], r["frames"], r["h"], r["w"], r["audio"]) for r in self.refs])
         self.c = h3_layout(text, frames, h, w, audio, cond_frames,
                            None if self._cl is None else self._cl.ctypes.data,
-                           None if self._tt is None else self._tt.ctypes.data)
+                           None if self._tt is None else self._tt.ctypes.data,
+                           self._refs if self.refs else None, len(self.refs))
 
     @property
     def patch_rows(self):
@@ -164,15 +179,23 @@ class Layout:
 
     @property
     def cond_rows(self):
-        return self.d["cond_frames"] * self.patch_rows
+        n = self.d["cond_frames"] * self.patch_rows
+        for r in self.refs:
+            if r["kind"] != "audio":
+                n += r["frames"] * (r["h"] // 2) * (r["w"] // 2)
+        return n
+
+    @property
+    def cond_audio_rows(self):
+        return sum(2 * r["audio"] for r in self.refs if r["kind"] != "image")
 
     @property
     def video_rows(self):
-        return (self.d["cond_frames"] + self.d["frames"]) * self.patch_rows
+        return self.cond_rows + self.d["frames"] * self.patch_rows
 
     @property
     def audio_rows(self):
-        return 2 * self.d["audio"]
+        return self.cond_audio_rows + 2 * self.d["audio"]
 
     @property
     def rows(self):
@@ -180,7 +203,7 @@ class Layout:
 
     @property
     def dense_rows(self):
-        return self.d["text"] + self.cond_rows + self.audio_rows
+        return self.rows - self.d["frames"] * self.patch_rows
 
     @classmethod
     def named(cls, name):

@@ -126,30 +126,57 @@ def video_time(f):
 
 
 def layout_rows(L):
-    """H3::rows restated (architecture.md:35-45): positions [S][3] f64, tags, roles, for the order
-    [text | keyframe rows | audio (left then right) | generated video]."""
+    """H3::rows restated: positions [S][3] f64, tags, roles for [text | keyframe rows or reference blocks | audio (left
+    then right) | generated video] (architecture.md:35-45 for the target's rows; :203-215 for the reference blocks:
+    one clock from the text's length, a picture one slot, a soundtrack one slot a latent at the ends of its block's
+    width axis, a video's soundtrack and frames from one origin with the clock advanced by the longer span; the
+    generated rows from where the clock ends). Roles: 0 text, 1 conditioning video, 2 reference audio, 3 audio,
+    4 video. Reference blocks: L["refs"] = [dict(kind="image"|"video"|"audio", frames, h, w, audio)]."""
     T, Fr, h, w, A, CF = L["text"], L["frames"], L["h"], L["w"], L.get("audio", 0), L.get("cond_frames", 0)
-    ph, pw = h // 2, w // 2
-    norm = math.sqrt(ph * pw)
-    hp = lambda y: (y + 0.5 - ph / 2.0) / norm * 32.0
-    wp = lambda x: (x + 0.5 - pw / 2.0) / norm * 32.0
+
+    def axes(hh, ww):
+        ph_, pw_ = hh // 2, ww // 2
+        nrm = math.sqrt(ph_ * pw_)
+        return (ph_, pw_, lambda y: (y + 0.5 - ph_ / 2.0) / nrm * 32.0, lambda x: (x + 0.5 - pw_ / 2.0) / nrm * 32.0)
+
+    ph, pw, hp, wp = axes(h, w)
     pos, tags, roles = [], [], []
     tt = L.get("text_tags")
     for i in range(T):
         pos.append((float(i), 0.0, 0.0)); tags.append(1 if tt is None else int(tt[i])); roles.append(0)
+
+    def frame(t, grid, role):
+        gph, gpw, ghp, gwp = grid
+        for y in range(gph):
+            for x in range(gpw):
+                pos.append((t, ghp(y), gwp(x))); tags.append(0); roles.append(role)
+
+    def sound(t0, n, grid, role):
+        gwp, gpw = grid[3], grid[1]
+        for c in range(2):
+            for a in range(n):
+                pos.append((float(t0 + a), 0.0, gwp(0 if c == 0 else gpw - 1))); tags.append(2); roles.append(role)
+
+    clock = float(T)
     cl = L.get("cond_last") or []
     for k in range(CF):
-        t = T + video_time(max(Fr - 1, 0) if (k < len(cl) and cl[k]) else 0)
-        for y in range(ph):
-            for x in range(pw):
-                pos.append((t, hp(y), wp(x))); tags.append(0); roles.append(1)
-    for c in range(2):
-        for a in range(A):
-            pos.append((float(T + a), 0.0, wp(0 if c == 0 else pw - 1))); tags.append(2); roles.append(3)
+        frame(clock + video_time(max(Fr - 1, 0) if (k < len(cl) and cl[k]) else 0), (ph, pw, hp, wp), 1)
+    for r in L.get("refs") or []:
+        if r["kind"] == "image":
+            frame(clock, axes(r["h"], r["w"]), 1)
+            clock += 1.0
+        elif r["kind"] == "audio":
+            sound(clock, r["audio"], (ph, pw, hp, wp), 2)
+            clock += r["audio"]
+        else:
+            g = axes(r["h"], r["w"])
+            sound(clock, r.get("audio", 0), g, 2)
+            for f in range(r["frames"]):
+                frame(clock + video_time(f), g, 1)
+            clock += max(float(r.get("audio", 0)), video_time(r["frames"]))
+    sound(clock, A, (ph, pw, hp, wp), 3)
     for f in range(Fr):
-        for y in range(ph):
-            for x in range(pw):
-                pos.append((T + video_time(f), hp(y), wp(x))); tags.append(0); roles.append(4)
+        frame(clock + video_time(f), (ph, pw, hp, wp), 4)
     return np.array(pos, np.float64).reshape(-1, 3), np.array(tags, np.uint8), np.array(roles, np.uint8)
 
 
@@ -238,21 +265,24 @@ def bf(t):
 
 def step(cfg, w, L, text, video, audio, t_video, t_audio, allowed_fn=None, int8=0, probes=None, eps=1e-6,
          round_activations=False):
-    """One forward: velocities for every video row [V][96] (keyframe rows first) and audio row [A][32].
+    """One forward: velocities for every video row [V][96] (conditioning rows first) and audio row [A][32] (reference
+    soundtrack rows first), in the inputs' row order.
     allowed_fn(block, q, k) -> [H][S][S] bool restricts attention (sparse); int8 a mask (1 qkv, 2 out, 4 fc1, 8 fc2)
     switching those projections to the int8 dequant path; probes(name, layer, array) sees temb, mod0, x0, block l and
     norm_out. round_activations rounds every GEMM and attention input to bf16 as the GPU path does."""
     d, H, F = cfg["dim"], cfg["heads"], cfg["ffn"]
-    T, A = L["text"], 2 * L.get("audio", 0)
-    ph, pw = L["h"] // 2, L["w"] // 2
-    C = L.get("cond_frames", 0) * ph * pw
-    V = C + L["frames"] * ph * pw
-    S = T + V + A
-    D = T + C + A
+    T = L["text"]
     pos, tags, roles = layout_rows(L)
+    S = len(roles)
+    video_rows = np.nonzero((roles == 1) | (roles == 4))[0]  # the video input's rows in sequence order
+    audio_rows = np.nonzero((roles == 2) | (roles == 3))[0]  # the audio input's rows in sequence order
+    V, A = len(video_rows), len(audio_rows)
+    C = int((roles == 1).sum())
+    CA = int((roles == 2).sum())
     cs = torch.from_numpy(rope_table(pos))
     R = (lambda t: bf(t)) if round_activations else (lambda t: t)
-    # levels: video/text, audio, keyframe rows (max(t_video, 0.999)), in order of first appearance
+    # levels: video/text, audio, conditioning video (max(t_video, 0.999)), reference audio (1), in order of first
+    # appearance (architecture.md:38-42)
     levels = []
 
     def lv(t):
@@ -262,9 +292,10 @@ def step(cfg, w, L, text, video, audio, t_video, t_audio, allowed_fn=None, int8=
 
     t_cond = max(np.float32(t_video), np.float32(0.999))
     lv_v = lv(np.float32(t_video))
-    lv_a = lv(np.float32(t_audio)) if A else lv_v
+    lv_a = lv(np.float32(t_audio)) if A - CA else lv_v
     lv_c = lv(t_cond) if C else lv_v
-    lvl = np.array([lv_a if r == 3 else (lv_c if r == 1 else lv_v) for r in roles], np.int64)
+    lv_r = lv(np.float32(1.0)) if CA else lv_v
+    lvl = np.array([lv_a if r == 3 else (lv_c if r == 1 else (lv_r if r == 2 else lv_v)) for r in roles], np.int64)
     midx = torch.from_numpy(lvl * 3 + tags.astype(np.int64))
     U = len(levels)
     temb, s = time_embedding(levels, w)
@@ -276,11 +307,11 @@ def step(cfg, w, L, text, video, audio, t_video, t_audio, allowed_fn=None, int8=
         x[:T] = bf(torch.from_numpy(np.asarray(text, np.float32))) @ w["cond_w"].T + w["cond_b"]
     vin = torch.from_numpy(np.asarray(video, np.float32).reshape(V, 96))
     ain = torch.from_numpy(np.asarray(audio, np.float32).reshape(A, 32))
-    if C:
-        x[T:T + C] = R(vin[:C]) @ w["vp_w"].T + w["vp_b"]
+    vi, ai = torch.from_numpy(video_rows), torch.from_numpy(audio_rows)
+    if V:
+        x[vi] = R(vin) @ w["vp_w"].T + w["vp_b"]
     if A:
-        x[T + C:D] = R(ain) @ w["ap_w"].T + w["ap_b"]
-    x[D:] = R(vin[C:]) @ w["vp_w"].T + w["vp_b"]
+        x[ai] = R(ain) @ w["ap_w"].T + w["ap_b"]
     if probes:
         probes("x0", -1, x.numpy().copy())
 
@@ -313,8 +344,8 @@ def step(cfg, w, L, text, video, audio, t_video, t_audio, allowed_fn=None, int8=
     xn = rms(x, eps) * (1 + fm[:, 1]) + fm[:, 0]
     if probes:
         probes("norm_out", -1, xn.numpy().copy())
-    out_v = torch.cat([xn[T:T + C], xn[D:]]) @ w["hv_w"].T + w["hv_b"]
-    out_a = xn[T + C:D] @ w["ha_w"].T + w["ha_b"]
+    out_v = xn[vi] @ w["hv_w"].T + w["hv_b"]
+    out_a = xn[ai] @ w["ha_w"].T + w["ha_b"]
     return out_v.numpy(), out_a.numpy()
 
 

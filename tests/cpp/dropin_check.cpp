@@ -25,6 +25,17 @@ int main()
     const H3::Rows r = H3::rows(l);
     check(r.tags.size() == l.rows() && r.pos.size() == 3 * l.rows(), "rows: one entry per row");
     check(r.tags[0] == H3::kTextTag && r.tags[4] == H3::kAudioTag && r.tags.back() == H3::kVideoTag, "rows: tags by segment");
+    // A ref2va layout written the way tests/h3_ref_test.cpp:475-480 writes it.
+    using LR = H3::Layout::Reference;
+    H3::Layout ref{.text = 7, .frames = 6, .h = 8, .w = 12, .audio = 9};
+    ref.refs = {LR{.kind = LR::Kind::image, .frames = 1, .h = 6, .w = 10}, LR{.kind = LR::Kind::audio, .audio = 5},
+                LR{.kind = LR::Kind::video, .frames = 3, .h = 4, .w = 6, .audio = 11}};
+    check(ref.cond_rows() == 15 + 18 && ref.cond_audio_rows() == 32 && ref.rows() == 7 + 33 + 6 * 24 + 32 + 18,
+          "ref2va layout: row counts");
+    const H3::Rows rr = H3::rows(ref);
+    check(rr.tags.size() == ref.rows() && rr.roles[7] == 1 && rr.roles[7 + 15] == 2 && rr.pos[3 * 7] == 7.0 &&
+              rr.pos[3 * (7 + 15)] == 8.0,
+          "ref2va layout: rows (picture at the text's length, the soundtrack after it)");
     bool threw = false;
     try {
         mako::mtl::Context ctx;

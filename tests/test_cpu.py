@@ -171,6 +171,42 @@ def test_layout_with_keyframes_and_tags():
     assert list(r[:5]) == [0] * 5 and (r[5:5 + 2 * 24] == 1).all()
 
 
+REF_LAYOUT = dict(text=7, frames=6, h=8, w=12, audio=9, refs=[
+    dict(kind="image", frames=1, h=6, w=10), dict(kind="audio", audio=5),
+    dict(kind="video", frames=3, h=4, w=6, audio=11), dict(kind="video", frames=7, h=4, w=4, audio=2)])
+
+
+def test_layout_with_reference_blocks():
+    """Reference blocks (ref2va): row counts as the reference's Layout reports them, and H3::rows against the
+    oracle's own restatement of architecture.md:203-215 (one clock for every block, the generated rows after)."""
+    lay = h3b200.Layout(**REF_LAYOUT)
+    pos, t, r = h3b200.rows(lay)
+    p2, t2, r2 = O.layout_rows(REF_LAYOUT)
+    np.testing.assert_array_equal(pos, p2)
+    np.testing.assert_array_equal(t, t2)
+    np.testing.assert_array_equal(r, r2)
+    # counts: pictures and videos are conditioning video rows, soundtracks conditioning audio rows
+    assert lay.cond_rows == 3 * 5 + 3 * 2 * 3 + 7 * 2 * 2 == (r == 1).sum()
+    assert lay.cond_audio_rows == 2 * (5 + 11 + 2) == (r == 2).sum()
+    assert pos.shape[0] == lay.rows == int(h3b200.lib().h3_layout_rows(ctypes.byref(lay.c)))
+    # the clock: picture at 7, soundtrack at 8..12, the first video's rows from 13 (soundtrack 11 latents, frames
+    # spanning 5/3 x 9 = 15), the second video from 28 (soundtrack 2, frames 5/3 x 22), the generated rows after
+    assert (pos[r == 1][:15, 0] == 7).all()
+    assert pos[7 + 15, 0] == 8 and pos[7 + 15 + 4, 0] == 12
+    first_video_audio = pos[(r == 2)][10:, 0]
+    assert first_video_audio[0] == 13
+    gen_audio = pos[r == 3][:, 0]
+    assert gen_audio[0] == 28 + 5.0 / 3.0 * 22
+    assert (t[r == 2] == 2).all() and (t[r == 1] == 0).all()
+
+
+def test_layout_refuses_keyframes_with_reference_blocks():
+    lay = h3b200.Layout(text=2, frames=2, h=4, w=4, cond_frames=1, refs=[dict(kind="audio", audio=3)])
+    n = np.zeros((64, 3))
+    rc = h3b200.lib().h3_rows(ctypes.byref(lay.c), n.ctypes.data, None, None)
+    assert rc == h3b200.H3_ERR_ARG
+
+
 def test_rope_table_matches_oracle():
     lay = h3b200.Layout.named("c1")
     got = h3b200.rope_table(lay)

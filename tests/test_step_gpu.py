@@ -72,6 +72,35 @@ def test_step_with_audio_keyframes_and_three_levels(cuda):
         assert rel < VEL_REL and cos > VEL_COS, (rel, cos)
 
 
+REF_LAYOUT = dict(text=24, frames=6, h=12, w=14, audio=16, refs=[
+    dict(kind="image", frames=1, h=10, w=8), dict(kind="audio", audio=9),
+    dict(kind="video", frames=3, h=6, w=8, audio=13)])
+
+
+@pytest.mark.parametrize("sparse", [0.0, 0.5])
+def test_step_with_reference_blocks_and_four_levels(cuda, sparse):
+    """ref2va: a picture, a soundtrack and a video with its soundtrack ahead of the generated rows; four noise levels
+    (video/text, audio, reference pictures and videos at 0.999, reference soundtracks at 1) in one forward. The
+    sparse case keeps every reference row among the dense rows every video query sees."""
+    if sparse:
+        lay, text, video, audio = inputs(REF_LAYOUT, MINI)
+        m = H.Model(MINI, seed=0, sparse_ratio=1.0, sparse_local=1)
+        m.begin(text, lay)
+        sv, sa = m.step(video, audio, 0.7, 0.4)
+        m.close()
+        _, _, (gv, ga), _, _ = run_both(MINI, REF_LAYOUT, 0.7, 0.4)
+        for g, o, wdt in ((sv, gv, 96), (sa, ga, 32)):
+            rel, cos = O.diff(g, o, wdt)
+            assert rel < 1e-2 and cos > 0.9999, (rel, cos)  # every cube selected = dense
+        return
+    got, want, (gv, ga), (ov, oa), _ = run_both(MINI, REF_LAYOUT, 0.7, 0.4)
+    assert want["temb"].shape[0] == 4
+    check_probes(got, want, MINI["dim"], MINI["blocks"])
+    for g, o, wdt in ((gv, ov, 96), (ga, oa, 32)):
+        rel, cos = O.diff(g, o, wdt)
+        assert rel < VEL_REL and cos > VEL_COS, (rel, cos)
+
+
 def test_step_sparse_every_cube_equals_dense(cuda):
     """--sparse 1.0 --sparse-local 0: every cube selected, so the sparse path must give the dense model's velocities
     (the reference's h3_dit_sparse_all, tests/CMakeLists.txt:9-12)."""
