@@ -107,6 +107,25 @@ int h3_step_device(h3_model* m, const float* video, uint64_t video_rows, const f
 /* Waits for the model's stream and reports a device-side failure of the queued work as H3_ERR_DEVICE. */
 int h3_synchronize(h3_model* m);
 
+/* Engine::sigmas(steps, shift) (src/video/engine.cpp:71-88): the schedule from 1 to 0, torch.linspace's float
+ * spacing, shifted by s x / (1 + (s - 1) x), consecutive repeats dropped. Writes up to `steps` points to out and
+ * their count to *points. Host only. */
+int h3_sigmas(uint32_t steps, float shift, float* out, uint32_t* points);
+
+/* Progress of h3_denoise: called on the host after step `step` (1-based) of `steps` has finished on the GPU; a
+ * nonzero return stops the loop after that step (the reference's cooperative cancellation,
+ * src/video/engine.cpp:717-718, tools/video_server.cpp:499-501). */
+typedef int (*h3_progress_fn)(void* user, uint32_t step, uint32_t steps);
+
+/* Engine::denoise's step loop (src/video/engine.cpp:701-719) on the GPU: for i < points - 1, the forward at
+ * t_video = 1 - sigma_video[i], t_audio = 1 - sigma_audio[i], then the Euler move of the generated rows to
+ * sigma[i + 1] (x0 = x + (1 - t) v; x = r x + (1 - r) x0, r = sigma[i + 1] / sigma[i]); the conditioning rows stay.
+ * video [V][96] and audio [A][32] are host memory holding the start sample (conditioning rows, then noise) and get
+ * the final sample. The sample stays on the device between steps: no host copies per step. progress may be NULL.
+ * *steps_run (may be NULL) gets the steps taken. */
+int h3_denoise(h3_model* m, float* video, uint64_t video_rows, float* audio, uint64_t audio_rows, const float* sigma_video,
+               const float* sigma_audio, uint32_t points, h3_progress_fn progress, void* user, uint32_t* steps_run);
+
 /* The model's CUDA stream (a cudaStream_t). */
 void* h3_stream(h3_model* m);
 

@@ -128,6 +128,35 @@ public:
         return v;
     }
 
+    // Engine::denoise's step loop on the GPU (src/video/engine.cpp:701-719): the sample (conditioning rows, then
+    // noise) in, the final sample out; sigmas from Engine::sigmas for video and audio. No counterpart member in the
+    // reference's H3, whose caller runs this loop on the host around step(). `progress(step, steps)` returning
+    // false stops the loop after that step. Returns the steps run.
+    uint32_t denoise(std::span<float> video, std::span<float> audio, std::span<const float> sigma_video, std::span<const float> sigma_audio,
+                     std::function<bool(uint32_t, uint32_t)> progress = {})
+    {
+        if (sigma_video.size() != sigma_audio.size())
+            throw std::runtime_error("H3::denoise: the video and audio schedules differ in length");
+        struct Ctx {
+            std::function<bool(uint32_t, uint32_t)>* fn;
+        } ctx{&progress};
+        auto thunk = [](void* user, uint32_t i, uint32_t n) -> int { return (*static_cast<Ctx*>(user)->fn)(i, n) ? 0 : 1; };
+        uint32_t ran = 0;
+        check(h3_denoise(m_, video.data(), video.size() / kVideoPatch, audio.data(), audio.size() / kAudioChannels, sigma_video.data(),
+                         sigma_audio.data(), uint32_t(sigma_video.size()), progress ? +thunk : nullptr, &ctx, &ran));
+        return ran;
+    }
+
+    // Engine::sigmas(steps, shift) (src/video/engine.cpp:71-88).
+    static std::vector<float> sigmas(uint32_t steps, float shift)
+    {
+        std::vector<float> out(steps < 2 ? 2 : steps);
+        uint32_t n = 0;
+        check(h3_sigmas(steps, shift, out.data(), &n));
+        out.resize(n);
+        return out;
+    }
+
     // set_probe (tests/h3_ref_test.cpp:215-217): temb, mod0, x0, block (layer), norm_out.
     void set_probe(ProbeFn fn)
     {

@@ -11,6 +11,7 @@
 #include <nccl.h>
 
 #include <cstring>
+#include <functional>
 #include <initializer_list>
 #include <string>
 
@@ -257,6 +258,43 @@ int h3_step_device(h3_model* m, const float* video, uint64_t video_rows, const f
             throw StateError("h3_step_device before h3_begin");
         check_io(m, video_rows, audio_rows);
         m->m->step(video, audio, t_video, t_audio, out_video, out_audio, true);
+    });
+}
+
+int h3_sigmas(uint32_t steps, float shift, float* out, uint32_t* points)
+{
+    return guarded([&] {
+        if (!out || !points)
+            throw ArgError("h3_sigmas: null output");
+        if (steps < 2 || !(shift > 0.f))
+            throw ArgError("h3_sigmas: at least 2 points and a positive shift");
+        const std::vector<float> v = h3::sigmas(int(steps), shift);
+        std::memcpy(out, v.data(), v.size() * 4);
+        *points = uint32_t(v.size());
+    });
+}
+
+int h3_denoise(h3_model* m, float* video, uint64_t video_rows, float* audio, uint64_t audio_rows, const float* sigma_video,
+               const float* sigma_audio, uint32_t points, h3_progress_fn progress, void* user, uint32_t* steps_run)
+{
+    return guarded([&] {
+        check_model(m);
+        if (m->m->rows() == 0)
+            throw StateError("h3_denoise before h3_begin");
+        check_io(m, video_rows, audio_rows);
+        if ((video_rows && !video) || (audio_rows && !audio) || !sigma_video || !sigma_audio)
+            throw ArgError("h3_denoise: null argument");
+        if (points < 2)
+            throw ArgError("h3_denoise: at least 2 schedule points");
+        for (uint32_t i = 0; i + 1 < points; ++i)
+            if (!(sigma_video[i] > 0.f) || !(sigma_audio[i] > 0.f))
+                throw ArgError("h3_denoise: every schedule point but the last must be positive");
+        std::function<bool(int, int)> cb;
+        if (progress)
+            cb = [&](int i, int n) { return progress(user, uint32_t(i), uint32_t(n)) == 0; };
+        const int n = m->m->denoise(video, audio, sigma_video, sigma_audio, int(points), cb);
+        if (steps_run)
+            *steps_run = uint32_t(n);
     });
 }
 

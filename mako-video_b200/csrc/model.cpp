@@ -248,6 +248,12 @@ struct Model::Impl {
     CubeGrid grid;
     std::vector<int32_t> h_video_src;
     DevBuf video_src, video_dst, out_video_rows;
+    DevBuf den_video, den_audio, vel_video, vel_audio; // the denoising loop's sample and velocities
+    // Pinned staging of a step's small host tables (row levels, time embeddings), reused once the previous step's
+    // copies have run (upload_done), so consecutive steps queue without draining the stream.
+    uint8_t* pinned = nullptr;
+    size_t pinned_bytes = 0;
+    cudaEvent_t upload_done = nullptr;
     // per global row; lvl_kind: 0 video/text level, 1 audio, 2 conditioning video (0.999), 3 reference audio (1)
     std::vector<uint8_t> h_tags, h_roles, h_lvl_kind;
     std::vector<Segment> segs;
@@ -389,6 +395,10 @@ Model::~Model()
     if (d_)
         for (cudaEvent_t e : d_->ev)
             cudaEventDestroy(e);
+    if (d_ && d_->upload_done)
+        cudaEventDestroy(d_->upload_done);
+    if (d_ && d_->pinned)
+        cudaFreeHost(d_->pinned);
     d_.reset();
     if (stream_)
         cudaStreamDestroy(stream_);
@@ -624,7 +634,24 @@ void Model::step(const float* video, const float* audio, float t_video, float t_
     const int lv_ref_audio = CA > 0 ? level_of(1.0f) : lv_video;
     const int U = int(levels.size());
     {
-        std::vector<uint8_t> midx(M, 0), lidx(M, 0);
+        // staged in pinned memory: [M] mod_idx, [M] lvl_idx, then [U][256] f32 embeddings at a 16-byte offset
+        const size_t emb_off = (size_t(2) * M + 15) & ~size_t(15);
+        const size_t need = emb_off + size_t(U) * 256 * 4;
+        if (!d_->upload_done)
+            H3_CUDA(cudaEventCreateWithFlags(&d_->upload_done, cudaEventDisableTiming));
+        else
+            H3_CUDA(cudaEventSynchronize(d_->upload_done)); // the previous step's copies have read the staging
+        if (need > d_->pinned_bytes) {
+            if (d_->pinned)
+                H3_CUDA(cudaFreeHost(d_->pinned));
+            d_->pinned = nullptr;
+            H3_CUDA(cudaMallocHost(reinterpret_cast<void**>(&d_->pinned), need));
+            d_->pinned_bytes = need;
+        }
+        uint8_t* midx = d_->pinned;
+        uint8_t* lidx = d_->pinned + M;
+        float* emb = reinterpret_cast<float*>(d_->pinned + emb_off);
+        std::memset(midx, 0, size_t(2) * M);
         for (int i = 0; i < M && row0_ + i < S_; ++i) {
             const int g = row0_ + i;
             const int kind = d_->h_lvl_kind[g];
@@ -632,10 +659,9 @@ void Model::step(const float* video, const float* audio, float t_video, float t_
             lidx[i] = uint8_t(lv);
             midx[i] = uint8_t(lv * 3 + d_->h_tags[g]);
         }
-        H3_CUDA(cudaMemcpyAsync(d_->mod_idx.p, midx.data(), M, cudaMemcpyHostToDevice, s));
-        H3_CUDA(cudaMemcpyAsync(d_->lvl_idx.p, lidx.data(), M, cudaMemcpyHostToDevice, s));
+        H3_CUDA(cudaMemcpyAsync(d_->mod_idx.p, midx, M, cudaMemcpyHostToDevice, s));
+        H3_CUDA(cudaMemcpyAsync(d_->lvl_idx.p, lidx, M, cudaMemcpyHostToDevice, s));
         // sinusoidal embeddings [U][256]: cos half first, freq_i = exp(-ln(10000) * i / 128)
-        std::vector<float> emb(size_t(U) * 256);
         for (int u = 0; u < U; ++u)
             for (int i = 0; i < 128; ++i) {
                 const float fr = float(std::exp(-std::log(10000.0) * i / 128.0));
@@ -643,10 +669,9 @@ void Model::step(const float* video, const float* audio, float t_video, float t_
                 emb[u * 256 + i] = float(std::cos(double(a)));
                 emb[u * 256 + 128 + i] = float(std::sin(double(a)));
             }
-        d_->emb.ensure(emb.size() * 4);
-        H3_CUDA(cudaMemcpyAsync(d_->emb.p, emb.data(), emb.size() * 4, cudaMemcpyHostToDevice, s));
-        // host vectors must outlive the async copies
-        H3_CUDA(cudaStreamSynchronize(s));
+        d_->emb.ensure(size_t(U) * 256 * 4);
+        H3_CUDA(cudaMemcpyAsync(d_->emb.p, emb, size_t(U) * 256 * 4, cudaMemcpyHostToDevice, s));
+        H3_CUDA(cudaEventRecord(d_->upload_done, s));
     }
 
     // ---- inputs
@@ -958,6 +983,80 @@ void Model::step(const float* video, const float* audio, float t_video, float t_
         if (const uint32_t e = take_device_error(s))
             throw CudaError("device error " + std::to_string(e) + " during the step (a bounded wait ran out)");
     }
+}
+
+int Model::denoise(float* video, float* audio, const float* sigma_video, const float* sigma_audio, int points,
+                   const std::function<bool(int, int)>& progress)
+{
+    if (!begun_)
+        throw CudaError("denoise before begin");
+    if (points < 2 || !sigma_video || !sigma_audio)
+        throw CudaError("denoise: at least 2 schedule points for video and audio");
+    for (int i = 0; i + 1 < points; ++i)
+        if (!(sigma_video[i] > 0.f) || !(sigma_audio[i] > 0.f))
+            throw CudaError("denoise: every schedule point but the last must be positive");
+    const Layout& l = layout_;
+    const size_t V = size_t(l.video_rows()), A = size_t(l.audio_rows()), C = size_t(l.cond_rows()), CA = size_t(l.cond_audio_rows());
+    const size_t vn = V * c_.video_patch, an = A * c_.audio_channels;
+    cudaStream_t s = stream_;
+    d_->den_video.ensure(std::max<size_t>(vn, 1) * 4);
+    d_->den_audio.ensure(std::max<size_t>(an, 1) * 4);
+    d_->vel_video.ensure(std::max<size_t>(vn, 1) * 4);
+    d_->vel_audio.ensure(std::max<size_t>(an, 1) * 4);
+    float* xv = d_->den_video.as<float>();
+    float* xa = d_->den_audio.as<float>();
+    if (vn)
+        H3_CUDA(cudaMemcpyAsync(xv, video, vn * 4, cudaMemcpyHostToDevice, s));
+    if (an)
+        H3_CUDA(cudaMemcpyAsync(xa, audio, an * 4, cudaMemcpyHostToDevice, s));
+    const int steps = points - 1;
+    int done = 0;
+    for (int i = 0; i < steps; ++i) {
+        const float tv = 1.0f - sigma_video[i], ta = 1.0f - sigma_audio[i];
+        step(xv, xa, tv, ta, d_->vel_video.as<float>(), d_->vel_audio.as<float>(), true);
+        euler_rows(xv + C * c_.video_patch, d_->vel_video.as<float>() + C * c_.video_patch, (V - C) * c_.video_patch, tv,
+                   sigma_video[i], sigma_video[i + 1], s);
+        euler_rows(xa + CA * c_.audio_channels, d_->vel_audio.as<float>() + CA * c_.audio_channels, (A - CA) * c_.audio_channels,
+                   ta, sigma_audio[i], sigma_audio[i + 1], s);
+        launches_ += 2;
+        ++done;
+        if (progress) {
+            H3_CUDA(cudaStreamSynchronize(s));
+            if (const uint32_t e = take_device_error(s))
+                throw CudaError("device error " + std::to_string(e) + " during the denoising loop (a bounded wait ran out)");
+            if (!progress(i + 1, steps))
+                break;
+        }
+    }
+    if (vn)
+        H3_CUDA(cudaMemcpyAsync(video, xv, vn * 4, cudaMemcpyDeviceToHost, s));
+    if (an)
+        H3_CUDA(cudaMemcpyAsync(audio, xa, an * 4, cudaMemcpyDeviceToHost, s));
+    H3_CUDA(cudaStreamSynchronize(s));
+    if (const uint32_t e = take_device_error(s))
+        throw CudaError("device error " + std::to_string(e) + " during the denoising loop (a bounded wait ran out)");
+    return done;
+}
+
+std::vector<float> sigmas(int steps, float shift)
+{
+    if (steps < 2)
+        throw CudaError("sigmas: at least 2 schedule points");
+    if (!(shift > 0.f))
+        throw CudaError("sigmas: the shift must be positive");
+    // torch.linspace(1, 0, steps) in float: the first half counts up from 1, the second half down from 0 (so the
+    // last point is exactly 0); then sigma -> shift * sigma / (1 + (shift - 1) * sigma), consecutive repeats dropped.
+    const float delta = -1.0f / float(steps - 1);
+    std::vector<float> out;
+    for (int i = 0; i < steps; ++i) {
+        const float lin = i < steps / 2 ? 1.0f + float(i) * delta : -(float(steps - 1 - i) * delta);
+        const float num = shift * lin;
+        const float den = 1.0f + (shift - 1.0f) * lin;
+        const float v = num / den;
+        if (out.empty() || out.back() != v)
+            out.push_back(v);
+    }
+    return out;
 }
 
 } // namespace h3

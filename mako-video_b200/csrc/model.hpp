@@ -81,6 +81,10 @@ struct Segment {
 };
 std::vector<Segment> layout_segments(const Layout& l);
 
+// The sampler's noise schedule (Engine::sigmas, src/video/engine.cpp:71-88): `steps` points from 1 to 0 spaced as
+// torch.linspace computes them in float, shifted by s x / (1 + (s - 1) x), consecutive repeats dropped.
+std::vector<float> sigmas(int steps, float shift);
+
 // The rotary frequencies: 16 per axis, base 10000 (1 / 10000^(2i/32) in float).
 void rope_inv_freq(float out[16]);
 // Per-row (cos, sin) of the 48 rotary angles (16 per axis, angle = float(pos) * inv_freq in float).
@@ -114,6 +118,14 @@ public:
     // beyond the error check).
     void step(const float* video, const float* audio, float t_video, float t_audio, float* out_video, float* out_audio,
               bool device_io = false);
+    // The denoising loop on the device (Engine::denoise's step loop): `points` schedule points give points - 1
+    // steps; step i runs the forward at t = 1 - sigma[i] and moves the generated rows (video rows past the
+    // conditioning rows, audio rows past the reference soundtracks) by Euler to sigma[i + 1]. video [V][96] and
+    // audio [A][32] are host memory, read at the start and overwritten with the final sample; the conditioning rows
+    // are unchanged. `progress(i + 1, steps)` runs on the host after each step's work has finished; a false return
+    // stops the loop there (the sample so far is still written back). Returns the steps run.
+    int denoise(float* video, float* audio, const float* sigma_video, const float* sigma_audio, int points,
+                const std::function<bool(int, int)>& progress);
 
     const Config& config() const { return c_; }
     const Layout& layout() const { return layout_; }

@@ -267,6 +267,15 @@ __global__ void pack_bf16_kernel(const float* in, int rows, int cols, __nv_bfloa
     }
 }
 
+__global__ void euler_kernel(float* x, const float* v, size_t n, float st, float ratio, float keep)
+{
+    for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x) {
+        const float xi = x[i];
+        const float x0 = __fadd_rn(xi, __fmul_rn(st, v[i]));
+        x[i] = __fadd_rn(__fmul_rn(ratio, xi), __fmul_rn(keep, x0));
+    }
+}
+
 __global__ void gather_rows_kernel(const float* src, int64_t lds, const int32_t* idx, int rows, int cols, float* dst, int64_t ldd)
 {
     const size_t total = size_t(rows) * cols;
@@ -412,6 +421,15 @@ void pack_bf16_rows(const float* in, int rows, int cols, void* out, int ld_out, 
         return;
     pack_bf16_kernel<<<grid_for(size_t(rows) * ld_out, 256), 256, 0, s>>>(in, rows, cols, static_cast<__nv_bfloat16*>(out), ld_out,
                                                                            src_rows);
+    H3_CUDA(cudaGetLastError());
+}
+
+void euler_rows(float* x, const float* v, size_t n, float t, float sigma, float sigma_next, cudaStream_t s)
+{
+    if (!n)
+        return;
+    const float st = 1.0f - t, ratio = sigma_next / sigma, keep = 1.0f - ratio;
+    euler_kernel<<<grid_for(n, 256), 256, 0, s>>>(x, v, n, st, ratio, keep);
     H3_CUDA(cudaGetLastError());
 }
 

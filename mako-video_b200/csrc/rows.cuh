@@ -49,6 +49,10 @@ void heads_partial(void* qkv_bf16, int rows, int heads, const float* qn_w, const
 // src_rows is given.
 void pack_bf16_rows(const float* in, int rows, int cols, void* out_bf16, int ld_out, cudaStream_t s, const int32_t* src_rows = nullptr);
 
+// The sampler's Euler move of n values in place (src/video/engine.cpp:705-711): x0 = x + (1 - t) v, then
+// x = r x + (1 - r) x0 with r = sigma_next / sigma, every operation rounded on its own (no fused multiply-add).
+void euler_rows(float* x, const float* v, size_t n, float t, float sigma, float sigma_next, cudaStream_t s);
+
 // dst[r][c] = src[idx[r]][c] for c < cols (fp32).
 void gather_rows_f32(const float* src, int64_t lds, const int32_t* idx, int rows, int cols, float* dst, int64_t ldd, cudaStream_t s);
 

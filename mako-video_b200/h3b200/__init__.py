@@ -82,6 +82,7 @@ class h3k_cube_grid(ctypes.Structure):
     _fields_ = [("dense_rows", ctypes.c_int32), ("frames", ctypes.c_int32), ("ph", ctypes.c_int32), ("pw", ctypes.c_int32)]
 
 
+PROGRESS_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32)
 PROBE_FN = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_char_p, ctypes.c_int32, ctypes.POINTER(ctypes.c_float), ctypes.c_uint64)
 
 # Every exported symbol and its signature (restype, argtypes). Tests check the library exports each of them.
@@ -96,6 +97,8 @@ SIGNATURES = {
     "h3_step": (ctypes.c_int, [_P, _P, _U64, _P, _U64, _F, _F, _P, _P]),
     "h3_step_device": (ctypes.c_int, [_P, _P, _U64, _P, _U64, _F, _F, _P, _P]),
     "h3_synchronize": (ctypes.c_int, [_P]),
+    "h3_sigmas": (ctypes.c_int, [_U32, _F, _P, _P]),
+    "h3_denoise": (ctypes.c_int, [_P, _P, _U64, _P, _U64, _P, _P, _U32, PROGRESS_FN, _P, _P]),
     "h3_stream": (_P, [_P]),
     "h3_set_probe": (ctypes.c_int, [_P, PROBE_FN, _P]),
     "h3_layout_rows": (_U64, [ctypes.POINTER(h3_layout)]),
@@ -228,6 +231,14 @@ def rope_table(layout):
     return out
 
 
+def sigmas(steps, shift):
+    """h3_sigmas: the sampler's schedule (Engine::sigmas)."""
+    out = np.zeros(max(steps, 2), np.float32)
+    n = ctypes.c_uint32()
+    check(lib().h3_sigmas(steps, shift, out.ctypes.data, ctypes.byref(n)))
+    return out[:n.value].copy()
+
+
 def packed_order(dense_rows, frames, ph, pw):
     """Row permutation of the packed order the h3k_sparse_* calls and the step use: packed row i holds layout row
     order[i] (the dense rows keep their places; the generated video rows go cube by cube)."""
@@ -293,6 +304,23 @@ class Model:
 
     def synchronize(self):
         check(lib().h3_synchronize(self.h))
+
+    def denoise(self, video, audio, sigma_video, sigma_audio, progress=None):
+        """h3_denoise: the whole step loop on the GPU. Returns (video, audio, steps run); progress(step, steps) -> bool
+        (False stops after that step)."""
+        video = np.array(video, dtype=np.float32, order="C", copy=True)
+        audio = np.array(audio, dtype=np.float32, order="C", copy=True)
+        sv = np.ascontiguousarray(sigma_video, dtype=np.float32)
+        sa = np.ascontiguousarray(sigma_audio, dtype=np.float32)
+        assert sv.shape == sa.shape
+        cb = None
+        if progress is not None:
+            cb = PROGRESS_FN(lambda user, i, n: 0 if progress(int(i), int(n)) else 1)
+        ran = ctypes.c_uint32()
+        check(lib().h3_denoise(self.h, video.ctypes.data, video.shape[0], audio.ctypes.data if audio.size else None, audio.shape[0],
+                               sv.ctypes.data, sa.ctypes.data, sv.size, cb if cb is not None else PROGRESS_FN(), None,
+                               ctypes.byref(ran)))
+        return video, audio, ran.value
 
     @property
     def stream(self):

@@ -349,6 +349,32 @@ def step(cfg, w, L, text, video, audio, t_video, t_audio, allowed_fn=None, int8=
     return out_v.numpy(), out_a.numpy()
 
 
+# ---------------------------------------------------------------------------------------------- the sampler
+
+
+def sigmas(steps, shift):
+    """Engine::sigmas restated (src/video/engine.cpp:71-88): torch.linspace(1, 0, steps) in float32 (first half from
+    the start, second half from the end), shifted by s x / (1 + (s - 1) x) in float32, consecutive repeats dropped."""
+    f = np.float32
+    step = (f(0.0) - f(1.0)) / f(steps - 1)
+    out = []
+    for i in range(steps):
+        base = f(1.0) + f(i) * step if i < steps // 2 else f(0.0) - f(steps - 1 - i) * step
+        v = f(shift) * base / (f(1.0) + (f(shift) - f(1.0)) * base)
+        if not out or out[-1] != v:
+            out.append(v)
+    return np.array(out, np.float32)
+
+
+def euler(x, v, t, sigma, sigma_next):
+    """The sampler's Euler move (src/video/engine.cpp:705-711) in float32, each operation rounded on its own."""
+    f = np.float32
+    st, ratio = f(1.0) - f(t), f(sigma_next) / f(sigma)
+    x = np.asarray(x, np.float32)
+    x0 = x + st * np.asarray(v, np.float32)
+    return ratio * x + (f(1.0) - ratio) * x0
+
+
 # -------------------------------------------------------------------------------------- comparison metric
 
 

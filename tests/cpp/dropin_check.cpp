@@ -36,6 +36,8 @@ int main()
     check(rr.tags.size() == ref.rows() && rr.roles[7] == 1 && rr.roles[7 + 15] == 2 && rr.pos[3 * 7] == 7.0 &&
               rr.pos[3 * (7 + 15)] == 8.0,
           "ref2va layout: rows (picture at the text's length, the soundtrack after it)");
+    const std::vector<float> sv = H3::sigmas(3, 12.0f);
+    check(sv.size() == 3 && sv[0] == 1.0f && sv[2] == 0.0f, "sigmas (tests/geometry_test.cpp:32-36)");
     bool threw = false;
     try {
         mako::mtl::Context ctx;

@@ -207,6 +207,19 @@ def test_layout_refuses_keyframes_with_reference_blocks():
     assert rc == h3b200.H3_ERR_ARG
 
 
+def test_sigmas_match_reference_known_answers():
+    """tests/geometry_test.cpp:32-45 of the reference: 3 points shifted by 12 and 3, and 50 strictly decreasing
+    points ending at 0; plus the whole schedule against the oracle's restatement for several sizes and shifts."""
+    v, a = h3b200.sigmas(3, 12.0), h3b200.sigmas(3, 3.0)
+    assert len(v) == 3 and v[0] == 1.0 and v[2] == 0.0 and abs(v[1] - 12.0 * 0.5 / (1.0 + 11.0 * 0.5)) < 1e-7
+    assert len(a) == 3 and abs(a[1] - 0.75) < 1e-7
+    s50 = h3b200.sigmas(50, 12.0)
+    assert len(s50) == 50 and (np.diff(s50) < 0).all() and s50[-1] == 0.0
+    for steps in (2, 3, 9, 10, 50, 51):
+        for shift in (1.0, 3.0, 5.5, 12.0):
+            np.testing.assert_array_equal(h3b200.sigmas(steps, shift), O.sigmas(steps, shift))
+
+
 def test_rope_table_matches_oracle():
     lay = h3b200.Layout.named("c1")
     got = h3b200.rope_table(lay)

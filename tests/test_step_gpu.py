@@ -142,3 +142,52 @@ def test_step_errors(cuda):
         m.step(video[:-1], audio, 0.5, 0.5)
     assert e.value.code == H.H3_ERR_ARG
     m.close()
+
+
+def _host_loop(m, video, audio, sv, sa, steps, C, CA):
+    video, audio = video.copy(), audio.copy()
+    for i in range(steps):
+        tv, ta = 1.0 - sv[i], 1.0 - sa[i]
+        vv, va = m.step(video, audio, np.float32(tv), np.float32(ta))
+        video[C:] = O.euler(video[C:], vv[C:], np.float32(tv), sv[i], sv[i + 1])
+        audio[CA:] = O.euler(audio[CA:], va[CA:], np.float32(ta), sa[i], sa[i + 1])
+    return video, audio
+
+
+@pytest.mark.parametrize("layout", ["keyframes", "refs"])
+def test_denoise_on_device_equals_step_by_step_host_loop(cuda, layout):
+    """h3_denoise (the sample kept on the GPU, Euler there) against h3_step plus the host Euler of the reference's
+    sampler (src/video/engine.cpp:705-716) over three steps: identical bits; the conditioning rows unchanged."""
+    L = MINI_LAYOUT if layout == "keyframes" else REF_LAYOUT
+    lay, text, video, audio = inputs(L, MINI)
+    sv, sa = H.sigmas(4, 5.0), H.sigmas(4, 3.0)
+    m = H.Model(MINI, seed=2)
+    m.begin(text, lay)
+    gv, ga, ran = m.denoise(video, audio, sv, sa)
+    assert ran == 3
+    hv, ha = _host_loop(m, video, audio, sv, sa, 3, lay.cond_rows, lay.cond_audio_rows)
+    m.close()
+    np.testing.assert_array_equal(gv, hv)
+    np.testing.assert_array_equal(ga, ha)
+    np.testing.assert_array_equal(gv[:lay.cond_rows], video[:lay.cond_rows])
+    np.testing.assert_array_equal(ga[:lay.cond_audio_rows], audio[:lay.cond_audio_rows])
+    assert not np.array_equal(gv[lay.cond_rows:], video[lay.cond_rows:])
+
+
+def test_denoise_progress_reports_and_cancels(cuda):
+    lay, text, video, audio = inputs(MINI_LAYOUT, MINI)
+    sv = H.sigmas(6, 5.0)
+    m = H.Model(MINI, seed=2)
+    m.begin(text, lay)
+    seen = []
+
+    def progress(i, n):
+        seen.append((i, n))
+        return i < 2
+
+    gv, ga, ran = m.denoise(video, audio, sv, sv, progress)
+    assert ran == 2 and seen == [(1, 5), (2, 5)]
+    hv, ha = _host_loop(m, video, audio, sv, sv, 2, lay.cond_rows, lay.cond_audio_rows)
+    m.close()
+    np.testing.assert_array_equal(gv, hv)
+    np.testing.assert_array_equal(ga, ha)
