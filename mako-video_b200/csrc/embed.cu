@@ -50,7 +50,17 @@ __global__ void gemv_f32_kernel(const float* W, const float* b, const float* x, 
     }
 }
 
-// One warp per weight row; each lane streams 16-byte chunks of the row (8 bf16) past L1.
+// One warp per weight row; each lane streams 16-byte chunks of the row (8 bf16) past L1, ADALN_UNROLL loads in
+// flight before their products are summed (the kernel is HBM bound: it needs many bytes in flight per SM).
+constexpr int ADALN_UNROLL = 4;
+
+__device__ __forceinline__ uint4 ld_stream(const uint4* p)
+{
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+
 __global__ void __launch_bounds__(256) adaln_kernel(const __nv_bfloat16* W, const float* b, const float* x, int U, int groups, int G,
                                                     int K, float* out)
 {
@@ -63,25 +73,31 @@ __global__ void __launch_bounds__(256) adaln_kernel(const __nv_bfloat16* W, cons
     for (size_t r = size_t(blockIdx.x) * 8 + warp_id(); r < rows; r += size_t(gridDim.x) * 8) {
         const uint4* w = reinterpret_cast<const uint4*>(W + r * K);
         float acc[MAXU] = {0.f, 0.f, 0.f, 0.f};
-        for (int c = lane_id(); c < k8; c += 32) {
-            uint4 v;
-            asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                         : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                         : "l"(w + c));
-            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
-            float f[8];
+        for (int c0 = lane_id(); c0 < k8; c0 += 32 * ADALN_UNROLL) {
+            uint4 v[ADALN_UNROLL];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float2 t = __bfloat1622float2(h[i]);
-                f[2 * i] = t.x, f[2 * i + 1] = t.y;
-            }
+            for (int q = 0; q < ADALN_UNROLL; ++q)
+                v[q] = c0 + 32 * q < k8 ? ld_stream(w + c0 + 32 * q) : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
-            for (int u = 0; u < MAXU; ++u)
-                if (u < U) {
-                    const float4* xv = reinterpret_cast<const float4*>(xs + u * K + c * 8);
-                    const float4 a = xv[0], bb = xv[1];
-                    acc[u] += f[0] * a.x + f[1] * a.y + f[2] * a.z + f[3] * a.w + f[4] * bb.x + f[5] * bb.y + f[6] * bb.z + f[7] * bb.w;
+            for (int q = 0; q < ADALN_UNROLL; ++q) {
+                const int c = c0 + 32 * q;
+                if (c >= k8)
+                    break;
+                const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v[q]);
+                float f[8];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float2 t = __bfloat1622float2(h[i]);
+                    f[2 * i] = t.x, f[2 * i + 1] = t.y;
                 }
+#pragma unroll
+                for (int u = 0; u < MAXU; ++u)
+                    if (u < U) {
+                        const float4* xv = reinterpret_cast<const float4*>(xs + u * K + c * 8);
+                        const float4 a = xv[0], bb = xv[1];
+                        acc[u] += f[0] * a.x + f[1] * a.y + f[2] * a.z + f[3] * a.w + f[4] * bb.x + f[5] * bb.y + f[6] * bb.z + f[7] * bb.w;
+                    }
+            }
         }
         const size_t g = r / G, j = r % G;
 #pragma unroll

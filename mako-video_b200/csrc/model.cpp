@@ -707,12 +707,24 @@ void Model::step(const float* video, const float* audio, float t_video, float t_
     d_->th.ensure(size_t(U) * d * 4);
     d_->temb.ensure(size_t(U) * td * 4);
     d_->tsilu.ensure(size_t(U) * td * 4);
-    d_->mods.ensure(size_t(L) * U * 18 * d * 4);
+    // With several ranks each computes the AdaLN projections of its share of the blocks (the weights stream from HBM
+    // once per step in all) and an all-gather hands every rank all of them.
+    const int nb = (L + P - 1) / P;
+    const size_t block_mods = size_t(U) * 18 * d;
+    d_->mods.ensure(size_t(nb) * P * block_mods * 4);
     d_->fmods.ensure(size_t(U) * 2 * d * 4);
     gemv_f32(d_->t_in_w.as<float>(), d_->t_in_b.as<float>(), d_->emb.as<float>(), U, d, 256, Act::silu, d_->th.as<float>(), nullptr, s);
     gemv_f32(d_->t_out_w.as<float>(), d_->t_out_b.as<float>(), d_->th.as<float>(), U, td, d, Act::none, d_->temb.as<float>(),
              d_->tsilu.as<float>(), s);
-    adaln_gemv(d_->ada_w.p, d_->ada_b.as<float>(), d_->tsilu.as<float>(), U, L, 18 * d, td, d_->mods.as<float>(), s);
+    {
+        const int b0 = std::min(L, world_.rank * nb), b1 = std::min(L, b0 + nb);
+        float* mine = d_->mods.as<float>() + size_t(world_.rank) * nb * block_mods;
+        if (b1 > b0)
+            adaln_gemv(static_cast<const __nv_bfloat16*>(d_->ada_w.p) + size_t(b0) * 18 * d * td, d_->ada_b.as<float>() + size_t(b0) * 18 * d,
+                       d_->tsilu.as<float>(), U, b1 - b0, 18 * d, td, mine, s);
+        if (P > 1)
+            H3_NCCL(ncclAllGather(mine, d_->mods.p, size_t(nb) * block_mods, ncclFloat32, d_->comm, s));
+    }
     adaln_gemv(d_->fada_w.p, d_->fada_b.as<float>(), d_->tsilu.as<float>(), U, 1, 2 * d, td, d_->fmods.as<float>(), s);
     launches_ += 4;
     mark("adaln");

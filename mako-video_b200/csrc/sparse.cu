@@ -43,26 +43,50 @@ __global__ void cube_pool_kernel(const __nv_bfloat16* q, const __nv_bfloat16* k,
     mk[o] = __fdiv_rn(sk, float(n));
 }
 
-__global__ void __launch_bounds__(1024) cube_scores_kernel(const float* mq, const float* mk, int cubes, float* scores)
+// 64 x 64 scores per CTA, 4 x 4 per thread. The means are staged transposed ([d][cube]) so that a thread reads its
+// four query means and four key means for one d as two 16-byte loads; each score is still one fmaf chain over
+// d = 0..127 in order, as the selection's arithmetic fixes.
+constexpr int CS_T = 64, CS_P = CS_T + 4;
+
+__global__ void __launch_bounds__(256) cube_scores_kernel(const float* mq, const float* mk, int cubes, float* scores)
 {
-    __shared__ float A[32][128];
-    __shared__ float B[32][129];
-    const int h = blockIdx.z, i0 = blockIdx.y * 32, j0 = blockIdx.x * 32;
-    const int tj = threadIdx.x, ti = threadIdx.y;
+    extern __shared__ float cs_smem[];
+    float* A = cs_smem;             // [128][CS_P]: query-cube means, transposed
+    float* B = cs_smem + 128 * CS_P; // [128][CS_P]: key-cube means, transposed
+    const int h = blockIdx.z, i0 = blockIdx.y * CS_T, j0 = blockIdx.x * CS_T;
     const float* qa = mq + size_t(h) * cubes * 128;
     const float* kb = mk + size_t(h) * cubes * 128;
-    for (int e = ti * 32 + tj; e < 32 * 128; e += 1024) {
+    for (int e = threadIdx.x; e < CS_T * 128; e += 256) {
         const int r = e / 128, d = e % 128;
-        A[r][d] = i0 + r < cubes ? qa[size_t(i0 + r) * 128 + d] : 0.f;
-        B[r][d] = j0 + r < cubes ? kb[size_t(j0 + r) * 128 + d] : 0.f;
+        A[d * CS_P + r] = i0 + r < cubes ? qa[size_t(i0 + r) * 128 + d] : 0.f;
+        B[d * CS_P + r] = j0 + r < cubes ? kb[size_t(j0 + r) * 128 + d] : 0.f;
     }
     __syncthreads();
-    float acc = 0.f;
-#pragma unroll 8
-    for (int d = 0; d < 128; ++d)
-        acc = __fmaf_rn(A[ti][d], B[tj][d], acc);
-    if (i0 + ti < cubes && j0 + tj < cubes)
-        scores[(size_t(h) * cubes + i0 + ti) * cubes + j0 + tj] = acc;
+    const int ti = threadIdx.x / 16, tj = threadIdx.x % 16;
+    float acc[4][4] = {};
+#pragma unroll 4
+    for (int d = 0; d < 128; ++d) {
+        const float4 a = *reinterpret_cast<const float4*>(A + d * CS_P + ti * 4);
+        const float4 b = *reinterpret_cast<const float4*>(B + d * CS_P + tj * 4);
+        const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int x = 0; x < 4; ++x)
+#pragma unroll
+            for (int y = 0; y < 4; ++y)
+                acc[x][y] = __fmaf_rn(av[x], bv[y], acc[x][y]);
+    }
+#pragma unroll
+    for (int x = 0; x < 4; ++x) {
+        const int i = i0 + ti * 4 + x;
+        if (i >= cubes)
+            continue;
+#pragma unroll
+        for (int y = 0; y < 4; ++y) {
+            const int j = j0 + tj * 4 + y;
+            if (j < cubes)
+                scores[(size_t(h) * cubes + i) * cubes + j] = acc[x][y];
+        }
+    }
 }
 
 __device__ __forceinline__ uint32_t orderable(float f)
@@ -76,18 +100,28 @@ constexpr int TK_NT = 256;
 // Block-wide exclusive prefix sum of one value per thread; returns the thread's offset, `total` gets the sum.
 __device__ __forceinline__ int block_exscan(int v, int* buf, int& total)
 {
-    buf[threadIdx.x] = v;
-    __syncthreads();
-    for (int o = 1; o < TK_NT; o <<= 1) {
-        const int t = threadIdx.x >= o ? buf[threadIdx.x - o] : 0;
-        __syncthreads();
-        buf[threadIdx.x] += t;
-        __syncthreads();
+    // warp inclusive scans by shuffles, then the warps' totals (buf[0..7]) scanned by every thread
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o)
+            x += t;
     }
-    total = buf[TK_NT - 1];
-    const int ex = buf[threadIdx.x] - v;
+    if (lane == 31)
+        buf[wid] = x;
     __syncthreads();
-    return ex;
+    int before = 0, all = 0;
+#pragma unroll
+    for (int w = 0; w < TK_NT / 32; ++w) {
+        const int t = buf[w];
+        before += w < wid ? t : 0;
+        all += t;
+    }
+    total = all;
+    __syncthreads(); // buf is reused by the next call
+    return before + x - v;
 }
 
 __global__ void __launch_bounds__(TK_NT) cube_topk_kernel(const float* scores, CubeGrid g, int k, int local, int32_t* sel, int32_t* nsel,
@@ -120,19 +154,25 @@ __global__ void __launch_bounds__(TK_NT) cube_topk_kernel(const float* scores, C
         for (int shift = 24; shift >= 0; shift -= 8) {
             hist[threadIdx.x] = 0;
             __syncthreads();
-            for (int j = threadIdx.x; j < n; j += TK_NT)
-                if (!forced(j) && (keys[j] & mask) == prefix)
-                    atomicAdd(&hist[(keys[j] >> shift) & 255], 1);
+            for (int j0 = 0; j0 < n; j0 += TK_NT) {
+                // warp-aggregated: lanes with the same digit add once
+                const int j = j0 + threadIdx.x;
+                const bool in = j < n && !forced(j) && (keys[j] & mask) == prefix;
+                const int dg = in ? int((keys[j] >> shift) & 255) : -1;
+                const unsigned same = __match_any_sync(0xffffffffu, dg);
+                if (in && (__ffs(same) - 1) == (threadIdx.x & 31))
+                    atomicAdd(&hist[dg], __popc(same));
+            }
             __syncthreads();
-            if (threadIdx.x == 0) {
-                int acc = 0, dg = 255;
-                for (; dg > 0; --dg) {
-                    if (acc + hist[dg] >= remaining)
-                        break;
-                    acc += hist[dg];
-                }
-                sh_digit = dg;
-                sh_acc = acc;
+            // The digit: the highest one whose bins from 255 down to it hold at least `remaining` keys (bin b is
+            // thread 255 - b's, so an exclusive scan over threads gives each bin the count above it).
+            const int b = TK_NT - 1 - threadIdx.x;
+            const int hb = hist[b];
+            int all;
+            const int above = block_exscan(hb, scan, all);
+            if (above < remaining && above + hb >= remaining) {
+                sh_digit = b;
+                sh_acc = above;
             }
             __syncthreads();
             remaining -= sh_acc;
@@ -267,8 +307,14 @@ void cube_pool(const void* q, const void* k, int64_t rs, int heads, const CubeGr
 
 void cube_scores(const float* mq, const float* mk, int heads, int cubes, float* scores, cudaStream_t s)
 {
-    const dim3 grid((cubes + 31) / 32, (cubes + 31) / 32, heads);
-    cube_scores_kernel<<<grid, dim3(32, 32), 0, s>>>(mq, mk, cubes, scores);
+    const dim3 grid((cubes + CS_T - 1) / CS_T, (cubes + CS_T - 1) / CS_T, heads);
+    const size_t smem = size_t(2) * 128 * CS_P * sizeof(float);
+    static bool attr = false;
+    if (!attr) {
+        H3_CUDA(cudaFuncSetAttribute(cube_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+        attr = true;
+    }
+    cube_scores_kernel<<<grid, 256, smem, s>>>(mq, mk, cubes, scores);
     H3_CUDA(cudaGetLastError());
 }
 
