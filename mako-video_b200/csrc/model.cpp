@@ -205,7 +205,10 @@ struct DevBuf {
             return;
         release();
         H3_CUDA(cudaMalloc(&p, n));
+        // The legacy-stream memset is not ordered with the model's non-blocking stream: finish it before anything is
+        // queued there (growth is rare: the first step of a layout or of more noise levels).
         H3_CUDA(cudaMemset(p, 0, n));
+        H3_CUDA(cudaDeviceSynchronize());
         bytes = n;
     }
     template <class T>

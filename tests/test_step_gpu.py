@@ -191,3 +191,42 @@ def test_denoise_progress_reports_and_cancels(cuda):
     m.close()
     np.testing.assert_array_equal(gv, hv)
     np.testing.assert_array_equal(ga, ha)
+
+
+EDGE = dict(dim=256, heads=2, ffn=512, blocks=2, time_dim=128, text_dim=256)
+
+
+@pytest.mark.parametrize("layout", [
+    dict(text=1, frames=1, h=2, w=2, audio=0),                                              # two rows in all
+    dict(text=3, frames=5, h=6, w=10, audio=3),                                             # cubes cut short on every axis
+    dict(text=130, frames=9, h=10, w=2, audio=65, cond_frames=2, cond_last=[0, 1]),          # odd sizes, keyframes
+    dict(text=5, frames=2, h=4, w=4, audio=0, refs=[dict(kind="audio", audio=7)]),           # a lone reference soundtrack
+])
+def test_step_edge_layouts(cuda, layout):
+    """Small and ragged layouts (row counts that fill no tile, one-row cubes, cubes cut short in frames, rows and
+    columns, odd audio and text counts, keyframes at both ends, a lone reference soundtrack): dense against the
+    oracle; sparse with every cube selected against dense; sparse at 0.3 with local 3 finite and repeatable."""
+    lay, text, video, audio = inputs(layout, EDGE)
+
+    def run(sparse, local=1):
+        m = H.Model(EDGE, seed=4, sparse_ratio=sparse, sparse_local=local)
+        m.begin(text, lay)
+        out = m.step(video, audio, 0.6, 0.3)
+        m.close()
+        return out
+
+    dv, da = run(0.0)
+    ov, oa = O.step(EDGE, O.make_weights(EDGE, 4), layout, text, video, audio, 0.6, 0.3)
+    for g, o, wdt in ((dv, ov, 96), (da, oa, 32)):
+        if o.size:
+            rel, cos = O.diff(g, o, wdt)
+            assert rel < VEL_REL and cos > VEL_COS, (rel, cos)
+    sv, sa = run(1.0)
+    for g, o, wdt in ((sv, dv, 96), (sa, da, 32)):
+        if o.size:
+            rel, cos = O.diff(g, o, wdt)
+            assert rel < 1e-2 and cos > 0.9999, (rel, cos)
+    p1, p2 = run(0.3, 3), run(0.3, 3)
+    for a, b in zip(p1, p2):
+        assert np.isfinite(a).all()
+        np.testing.assert_array_equal(a, b)
