@@ -251,6 +251,11 @@ int h3k_adaln(const void* W, const float* b, const float* x, int32_t U, int32_t 
 int h3k_heads(const float* x, int64_t ldx, int32_t rows, const float* W, const float* b, int32_t N, int32_t K, float* out, int64_t ldo,
               void* stream);
 
+/* Failure-detection self-test (no counterpart in the reference): a kernel waits on an mbarrier that nothing arrives
+ * on; the wait gives up after about budget_cycles SM clocks (at most 4e9), records its error and the kernel ends.
+ * Returns H3_ERR_DEVICE with the device error, as a step whose pipeline wait ran out does; the context stays usable
+ * and the error word is cleared. */
+int h3k_wait_selftest(uint64_t budget_cycles, void* stream);
 /* Waits for `stream` and reports a device-side failure (bounded wait ran out) as H3_ERR_DEVICE. */
 int h3k_check(void* stream);
 

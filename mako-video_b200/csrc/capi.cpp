@@ -621,6 +621,18 @@ int h3k_heads(const float* x, int64_t ldx, int32_t rows, const float* W, const f
     });
 }
 
+int h3k_wait_selftest(uint64_t budget_cycles, void* stream)
+{
+    return guarded([&] {
+        h3::wait_selftest((long long)budget_cycles, st(stream));
+        H3_CUDA(cudaStreamSynchronize(st(stream)));
+        const uint32_t e = h3::take_device_error(st(stream));
+        if (e)
+            throw DeviceError("device error " + std::to_string(e) + ": the self-test's bounded wait ran out, as it must");
+        throw StateError("h3k_wait_selftest: the wait did not give up");
+    });
+}
+
 int h3k_check(void* stream)
 {
     return guarded([&] {

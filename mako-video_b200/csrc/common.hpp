@@ -34,4 +34,7 @@ int num_sms();
 // address space (null counts as accessible; callers check their own required arguments).
 bool device_accessible(const void* p);
 
+// Queues the bounded-wait self-test (a wait on an mbarrier nothing arrives on, given up after budget_cycles).
+void wait_selftest(long long budget_cycles, cudaStream_t s);
+
 } // namespace h3

@@ -8,6 +8,7 @@
 #include "rows.cuh"
 
 #include <nccl.h>
+#include <nvtx3/nvToolsExt.h>
 
 #include <algorithm>
 #include <cmath>
@@ -19,6 +20,16 @@ namespace h3 {
 
 // ------------------------------------------------------------------------------------------------ layout rows
 namespace {
+
+// NVTX range over a scope (the step, each block, each denoising step): what a profiler's timeline groups the
+// launches by, free when no tool is attached.
+struct NvtxRange {
+    explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+    explicit NvtxRange(const std::string& name) { nvtxRangePushA(name.c_str()); }
+    ~NvtxRange() { nvtxRangePop(); }
+    NvtxRange(const NvtxRange&) = delete;
+    NvtxRange& operator=(const NvtxRange&) = delete;
+};
 
 // Time position of generated latent frame f, in audio-latent units (40 a second): the frames before it at 24 fps,
 // the video VAE packing 17 frames into 5 latents as (1, 4, 4, 4, 4).
@@ -611,6 +622,7 @@ void Model::step(const float* video, const float* audio, float t_video, float t_
 {
     if (!begun_)
         throw CudaError("step before begin");
+    NvtxRange step_range("h3.step");
     cudaStream_t s = stream_;
     const Layout& l = layout_;
     const int d = c_.dim, inner = c_.inner(), F = c_.ffn, td = c_.time_dim, L = c_.blocks;
@@ -796,6 +808,7 @@ void Model::step(const float* video, const float* audio, float t_video, float t_
         H3_NCCL(ncclAllReduce(d_->barrier_word.p, d_->barrier_word.p, 1, ncclInt32, ncclSum, d_->comm, s));
     };
     for (int bl = 0; bl < L; ++bl) {
+        NvtxRange block_range("h3.block " + std::to_string(bl));
         Impl::Block& B = d_->blocks[bl];
         const float* mod = d_->mods.as<float>() + size_t(bl) * U * 18 * d;
         // attention half
@@ -1027,6 +1040,7 @@ int Model::denoise(float* video, float* audio, const float* sigma_video, const f
     const int steps = points - 1;
     int done = 0;
     for (int i = 0; i < steps; ++i) {
+        NvtxRange denoise_range("h3.denoise " + std::to_string(i));
         const float tv = 1.0f - sigma_video[i], ta = 1.0f - sigma_audio[i];
         step(xv, xa, tv, ta, d_->vel_video.as<float>(), d_->vel_audio.as<float>(), true);
         euler_rows(xv + C * c_.video_patch, d_->vel_video.as<float>() + C * c_.video_patch, (V - C) * c_.video_patch, tv,

@@ -98,6 +98,7 @@ SIGNATURES = {
     "h3_step_device": (ctypes.c_int, [_P, _P, _U64, _P, _U64, _F, _F, _P, _P]),
     "h3_synchronize": (ctypes.c_int, [_P]),
     "h3_sigmas": (ctypes.c_int, [_U32, _F, _P, _P]),
+    "h3k_wait_selftest": (ctypes.c_int, [_U64, _P]),
     "h3_denoise": (ctypes.c_int, [_P, _P, _U64, _P, _U64, _P, _P, _U32, PROGRESS_FN, _P, _P]),
     "h3_stream": (_P, [_P]),
     "h3_set_probe": (ctypes.c_int, [_P, PROBE_FN, _P]),

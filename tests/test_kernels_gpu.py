@@ -434,3 +434,22 @@ def test_host_pointers_are_refused_before_any_launch(cuda):
                                       ctypes.byref(grid), 0.5, 1, ptr(t[:, 0]), Hh * 128, stream())
     assert rc == H.H3_ERR_ARG
     sync()  # the context is intact
+
+
+def test_bounded_wait_gives_up_and_the_context_survives(cuda):
+    """Failure detection without a GPU fault: a wait on an mbarrier nothing arrives on runs out after its cycle budget
+    (~1 ms here), the kernel ends, the host reads H3_ERR_DEVICE, and the next kernels run normally."""
+    import time
+    t0 = time.time()
+    rc = H.lib().h3k_wait_selftest(2_000_000, stream())
+    assert rc == H.H3_ERR_DEVICE, rc
+    assert b"ran out" in H.lib().h3_last_error()
+    assert time.time() - t0 < 10
+    sync()  # the error word was cleared: h3k_check reports nothing
+    S, Hh = 256, 2
+    t = (torch.randn(S, 3, Hh, 128, device=cuda)).bfloat16()
+    out = torch.zeros(S, Hh, 128, device=cuda, dtype=torch.bfloat16)
+    H.check(H.lib().h3k_attention(ptr(t[:, 0]), ptr(t[:, 1]), ptr(t[:, 2]), 3 * Hh * 128, Hh, S, ptr(out), Hh * 128, stream()))
+    sync()
+    want = O.attention(t[:, 0].float().cpu(), t[:, 1].float().cpu(), t[:, 2].float().cpu(), None)
+    assert rel(out.float().cpu(), want) < 1e-2
