@@ -409,7 +409,18 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
     const int warp = warp_id();
-    const int tile = blockIdx.x, head = blockIdx.y;
+    // Sparse launches are 1-D and longest first: the dense-row query tiles (which see every key, several times a video
+    // tile's work) of every head, then each head's video tiles together (they share the head's keys in L2).
+    int tile = blockIdx.x, head = blockIdx.y;
+    if constexpr (SPARSE) {
+        const int vt = (p.grid.cubes() + 1) / 2, dt = p.q_tiles - vt;
+        const int id = blockIdx.x;
+        if (id < p.heads * dt) {
+            head = id % p.heads, tile = vt + id / p.heads;
+        } else {
+            head = (id - p.heads * dt) / vt, tile = (id - p.heads * dt) % vt;
+        }
+    }
     int nkv;
     int4 qr; // (first row of query half 0, of half 1 or -1, rows of half 0, rows of half 1)
     const int4* entries = nullptr;
@@ -719,7 +730,7 @@ void attention(const AttnParams& p, cudaStream_t s)
     // Dense: two query tiles per CTA share every K/V tile (half the shared-memory traffic per FLOP). Sparse: query
     // tiles have their own key lists, so one tile per CTA with double-buffered scores.
     if (sparse)
-        attn3_kernel<true><<<dim3(p.q_tiles, p.heads), NT3, A3_SMEM, s>>>(maps, p);
+        attn3_kernel<true><<<p.q_tiles * p.heads, NT3, A3_SMEM, s>>>(maps, p);
     else
         attn2_kernel<A2_SPLIT><<<dim3((p.rows + 255) / 256, p.heads), NT2, A2_SMEM, s>>>(maps, p);
     H3_CUDA(cudaGetLastError());
