@@ -33,13 +33,14 @@ struct Smem {
     static constexpr int A_BYTES = BM * KBYTES;
     static constexpr int B_BYTES = BN * KBYTES;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    // the q/k/v epilogue stages one head tile (128 rows x 128 dims bf16, two 128-byte-swizzled halves) for TMA
-    static constexpr int STAGING = EPI == Epi::qkv ? BM * 256 : 0;
+    // the q/k/v and SwiGLU epilogues stage one 128 x 128 bf16 tile (two 128-byte-swizzled halves) for TMA stores
+    static constexpr int STAGING = (EPI == Epi::qkv || EPI == Epi::swiglu) ? BM * 256 : 0;
     static constexpr int TOTAL = STAGES * STAGE_BYTES + STAGING + 1024 /* alignment slack */ + 256 /* barriers */;
 };
 
-// Destination tensor maps of the q/k/v epilogue, one per rank that owns heads: (dim, q/k/v x head slot, row) over
-// that rank's block of this rank's rows, in its receive buffer (fused exchange) or in this rank's send layout.
+// Destination tensor maps of the TMA-store epilogues. q/k/v: one per rank that owns heads, (dim, q/k/v x head slot,
+// row) over that rank's block of this rank's rows, in its receive buffer (fused exchange) or in this rank's send
+// layout. SwiGLU: m[0] is the output [M][ldo] (box 64 columns x 128 rows).
 struct OutMaps {
     CUtensorMap m[8];
 };
@@ -51,6 +52,12 @@ __device__ __forceinline__ void tma_store_3d(const void* tmap, const void* smem_
     asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
                      reinterpret_cast<uint64_t>(tmap)),
                  "r"(smem_u32(smem_src)), "r"(c0), "r"(c1), "r"(c2)
+                 : "memory");
+}
+__device__ __forceinline__ void tma_store_2d(const void* tmap, const void* smem_src, int32_t c0, int32_t c1)
+{
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(reinterpret_cast<uint64_t>(tmap)),
+                 "r"(smem_u32(smem_src)), "r"(c0), "r"(c1)
                  : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
@@ -172,14 +179,17 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tacc
             }
         }
     } else if constexpr (EPI == Epi::swiglu) {
-        // Gate columns [0,128) and value columns [128,256) of the tile pair up; 128 outputs per tile.
+        // Gate columns [0,128) and value columns [128,256) of the tile pair up: 128 outputs per row, staged as two
+        // 128-byte-swizzled halves of 64 columns and written by two TMA stores (rows past M are clipped by the store,
+        // so every thread takes part in the staging).
+        if (threadIdx.x == 64)
+            bulk_wait_read0(); // the previous tile's stores have read the staging buffer
+        epi_bar();
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
             float g[32], u[32];
             load_acc<IS_I8, 1>(taddr, c * 32, g, a_scale, IS_I8 ? bsc + c * 32 : nullptr);
             load_acc<IS_I8, 1>(taddr, 128 + c * 32, u, a_scale, IS_I8 ? bsc + 128 + c * 32 : nullptr);
-            if (!valid)
-                continue;
             if (p.bias) {
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
@@ -190,8 +200,20 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tacc
 #pragma unroll
             for (int i = 0; i < 32; ++i)
                 g[i] = silu(g[i]) * u[i];
-            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + size_t(gm) * p.ldo + n0 / 2 + c * 32;
-            store_bf16x32(dst, g);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int chunk = (c & 1) * 4 + q;
+                const uint4 w = make_uint4(pack_bf16x2(g[8 * q + 0], g[8 * q + 1]), pack_bf16x2(g[8 * q + 2], g[8 * q + 3]),
+                                           pack_bf16x2(g[8 * q + 4], g[8 * q + 5]), pack_bf16x2(g[8 * q + 6], g[8 * q + 7]));
+                *reinterpret_cast<uint4*>(stage + (c >> 1) * (BM * 128) + row * 128 + ((chunk ^ (row & 7)) << 4)) = w;
+            }
+        }
+        fence_proxy_async_smem();
+        epi_bar();
+        if (threadIdx.x == 64) {
+            tma_store_2d(&om->m[0], stage, n0 / 2, m0);
+            tma_store_2d(&om->m[0], stage + BM * 128, n0 / 2 + 64, m0);
+            bulk_commit();
         }
     } else {
 #pragma unroll 1
@@ -368,8 +390,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             if (elect_one_lane())
                 mbar_arrive(&tempty[acc]);
         }
-        if (EPI == Epi::qkv && threadIdx.x == 64)
-            bulk_wait0(); // the head tiles' TMA stores are complete
+        if ((EPI == Epi::qkv || EPI == Epi::swiglu) && threadIdx.x == 64)
+            bulk_wait0(); // the staged tiles' TMA stores are complete
     }
     tc_fence_before();
     __syncthreads();
@@ -418,6 +440,12 @@ void launch(const void* A, const void* B, const GemmParams& p, cudaStream_t s)
             const __nv_bfloat16* base = static_cast<const __nv_bfloat16*>(p.peer_out[r] ? p.peer_out[r] : p.out) + block;
             om.m[r] = make_tmap(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, odims, ostr, obox);
         }
+    }
+    if constexpr (EPI == Epi::swiglu) {
+        const uint64_t odims[2] = {uint64_t(p.N / 2), uint64_t(p.M)};
+        const uint64_t ostr[1] = {uint64_t(p.ldo) * 2};
+        const uint32_t obox[2] = {64, 128};
+        om.m[0] = make_tmap(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.out, odims, ostr, obox);
     }
     gemm_kernel<BN, EPI, IS_I8><<<grid, NUM_THREADS, smem, s>>>(ta, tb, p, om);
     H3_CUDA(cudaGetLastError());
