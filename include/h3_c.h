@@ -107,6 +107,19 @@ int h3_step_device(h3_model* m, const float* video, uint64_t video_rows, const f
 /* Waits for the model's stream and reports a device-side failure of the queued work as H3_ERR_DEVICE. */
 int h3_synchronize(h3_model* m);
 
+/* H3::add_lora(path, scale, strict) (src/video/engine.cpp:114; docs/architecture.md:108-116): merges a safetensors
+ * file of Diffusers-named LoRA adapters into the weights, W += scale * alpha / rank * B A (bf16 matrices; int8
+ * matrices are requantised per row). Targets: transformer_blocks.N.attn.to_q/to_k/to_v/to_out.0, ff.net.0.proj
+ * (Diffusers' [value; gate] rows rotated to [gate; value]), ff.net.2, adaln_proj.linear (rows re-laid out from
+ * (chunk, modality) to (modality, chunk)). Token-refiner targets are skipped; with strict, any other unknown name
+ * fails. merged / skipped (may be NULL) get the counts. */
+int h3_add_lora(h3_model* m, const char* path, float scale, int32_t strict, uint32_t* merged, uint32_t* skipped);
+
+/* Reads a LoRA file's adapter list without a model (host only): `names` gets the adapter target names (prefixes
+ * stripped), '\n'-separated, NUL-terminated, truncated to cap bytes; *count the adapters, *rank the first one's
+ * rank, *alpha the file's "alpha" metadata (0 when absent). Any pointer may be NULL. No counterpart in the reference. */
+int h3_lora_inspect(const char* path, char* names, uint64_t cap, uint32_t* count, uint32_t* rank, float* alpha);
+
 /* Engine::sigmas(steps, shift) (src/video/engine.cpp:71-88): the schedule from 1 to 0, torch.linspace's float
  * spacing, shifted by s x / (1 + (s - 1) x), consecutive repeats dropped. Writes up to `steps` points to out and
  * their count to *points. Host only. */

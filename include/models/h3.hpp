@@ -105,8 +105,8 @@ public:
 
     // set_sparse(ratio, local) (src/video/engine.cpp:112).
     void set_sparse(float ratio, uint32_t local) { check(h3_set_sparse(m_, ratio, local)); }
-    // add_lora (src/video/engine.cpp:114): merging adapters is a load-time step that is not built.
-    void add_lora(const std::string&, float, bool) { throw std::runtime_error("H3::add_lora: LoRA merging is not built"); }
+    // add_lora(path, scale, strict) (src/video/engine.cpp:114): merges a Diffusers-named LoRA file into the weights.
+    void add_lora(const std::string& path, float scale, bool strict) { check(h3_add_lora(m_, path.c_str(), scale, strict ? 1 : 0, nullptr, nullptr)); }
 
     // begin(text [T][5120], layout) (src/video/engine.cpp:700).
     void begin(std::span<const float> text, const Layout& l)

@@ -6,13 +6,16 @@
 #include "gemm.cuh"
 #include "model.hpp"
 #include "rows.cuh"
+#include "safetensors.hpp"
 #include "sparse.cuh"
 
 #include <nccl.h>
 
+#include <algorithm>
 #include <cstring>
 #include <functional>
 #include <initializer_list>
+#include <memory>
 #include <string>
 
 struct h3_model {
@@ -57,7 +60,7 @@ int guarded(F&& f)
         const std::string w = e.what();
         if (w.find("device error") != std::string::npos)
             return H3_ERR_DEVICE;
-        if (w.find("config") == 0 || w.find("world") == 0 || w.find("begin:") == 0 || w.find("gemm:") == 0 ||
+        if (w.find("config") == 0 || w.find("world") == 0 || w.find("begin:") == 0 || w.find("gemm:") == 0 || w.find("add_lora:") == 0 ||
             w.find("sparse") != std::string::npos || w.find("attention:") == 0)
             return H3_ERR_ARG;
         return H3_ERR_CUDA;
@@ -258,6 +261,71 @@ int h3_step_device(h3_model* m, const float* video, uint64_t video_rows, const f
             throw StateError("h3_step_device before h3_begin");
         check_io(m, video_rows, audio_rows);
         m->m->step(video, audio, t_video, t_audio, out_video, out_audio, true);
+    });
+}
+
+int h3_add_lora(h3_model* m, const char* path, float scale, int32_t strict, uint32_t* merged, uint32_t* skipped)
+{
+    return guarded([&] {
+        check_model(m);
+        if (!path)
+            throw ArgError("h3_add_lora: null path");
+        h3::Model::LoraResult r;
+        try {
+            r = m->m->add_lora(path, scale, strict != 0);
+        } catch (const h3::CudaError&) {
+            throw;
+        } catch (const std::runtime_error& e) { // the file's own problems (safetensors reader)
+            throw ArgError(e.what());
+        }
+        if (merged)
+            *merged = uint32_t(r.merged);
+        if (skipped)
+            *skipped = uint32_t(r.skipped);
+    });
+}
+
+int h3_lora_inspect(const char* path, char* names, uint64_t cap, uint32_t* count, uint32_t* rank, float* alpha)
+{
+    return guarded([&] {
+        if (!path)
+            throw ArgError("h3_lora_inspect: null path");
+        std::unique_ptr<h3::SafeTensors> st;
+        try {
+            st = std::make_unique<h3::SafeTensors>(path);
+        } catch (const std::runtime_error& e) {
+            throw ArgError(e.what());
+        }
+        std::string list;
+        uint32_t n = 0, r = 0;
+        for (const auto& [name, t] : st->tensors()) {
+            for (const char* suf : {".lora_A.weight", ".lora_down.weight"}) {
+                const std::string sfx(suf);
+                if (name.size() < sfx.size() || name.compare(name.size() - sfx.size(), sfx.size(), sfx) != 0)
+                    continue;
+                std::string target = name.substr(0, name.size() - sfx.size());
+                for (const char* pre : {"base_model.model.", "diffusion_model.", "transformer."})
+                    if (target.rfind(pre, 0) == 0)
+                        target = target.substr(std::strlen(pre));
+                list += (n ? "\n" : "") + target;
+                if (!n && !t.shape.empty())
+                    r = uint32_t(t.shape[0]);
+                ++n;
+            }
+        }
+        if (names && cap) {
+            const size_t k = std::min<size_t>(list.size(), size_t(cap - 1));
+            std::memcpy(names, list.data(), k);
+            names[k] = 0;
+        }
+        if (count)
+            *count = n;
+        if (rank)
+            *rank = r;
+        if (alpha) {
+            const auto it = st->metadata().find("alpha");
+            *alpha = it == st->metadata().end() ? 0.f : std::stof(it->second);
+        }
     });
 }
 

@@ -6,6 +6,7 @@
 #include "embed.cuh"
 #include "gemm.cuh"
 #include "rows.cuh"
+#include "safetensors.hpp"
 
 #include <nccl.h>
 #include <nvtx3/nvToolsExt.h>
@@ -1086,6 +1087,144 @@ std::vector<float> sigmas(int steps, float shift)
             out.push_back(v);
     }
     return out;
+}
+
+Model::LoraResult Model::add_lora(const std::string& path, float scale, bool strict)
+{
+    const SafeTensors st(path);
+    const int d = c_.dim, inner = c_.inner(), F = c_.ffn, td = c_.time_dim, L = c_.blocks;
+    cudaStream_t s = stream_;
+    LoraResult res;
+    auto strip = [](std::string n) {
+        for (const char* pre : {"base_model.model.", "diffusion_model.", "transformer."})
+            if (n.rfind(pre, 0) == 0)
+                n = n.substr(std::strlen(pre));
+        return n;
+    };
+    auto ends_with = [](const std::string& a, const std::string& b) {
+        return a.size() >= b.size() && a.compare(a.size() - b.size(), b.size(), b) == 0;
+    };
+    float file_alpha = 0.f;
+    if (const auto it = st.metadata().find("alpha"); it != st.metadata().end())
+        file_alpha = std::stof(it->second);
+    enum Kind { kQ, kK, kV, kOut, kFc1, kFc2, kAda, kNone };
+    struct Item {
+        std::string a, b, prefix;
+        Kind kind;
+        int block, r, in, out;
+        float sc;
+    };
+    // every adapter is checked (name, shapes) before any weight changes
+    std::vector<Item> plan;
+    for (const auto& [name, t] : st.tensors()) {
+        std::string a_suffix;
+        for (const char* suf : {".lora_A.weight", ".lora_down.weight"})
+            if (ends_with(name, suf))
+                a_suffix = suf;
+        if (a_suffix.empty())
+            continue;
+        const std::string prefix = name.substr(0, name.size() - a_suffix.size());
+        const std::string b_name = prefix + (a_suffix == ".lora_A.weight" ? ".lora_B.weight" : ".lora_up.weight");
+        const std::string target = strip(prefix);
+        if (!st.tensors().count(b_name))
+            throw CudaError("add_lora: " + name + " has no matching " + b_name);
+        // transformer_blocks.N.<module>
+        int block = -1;
+        std::string module;
+        if (target.rfind("transformer_blocks.", 0) == 0) {
+            const size_t dot = target.find('.', 19);
+            if (dot != std::string::npos) {
+                block = std::atoi(target.substr(19, dot - 19).c_str());
+                module = target.substr(dot + 1);
+            }
+        }
+        Kind kind = kNone;
+        if (module == "attn.to_q") kind = kQ;
+        else if (module == "attn.to_k") kind = kK;
+        else if (module == "attn.to_v") kind = kV;
+        else if (module == "attn.to_out.0") kind = kOut;
+        else if (module == "ff.net.0.proj") kind = kFc1;
+        else if (module == "ff.net.2") kind = kFc2;
+        else if (module == "adaln_proj.linear") kind = kAda;
+        if (kind == kNone || block < 0 || block >= L) {
+            const bool known = target.rfind("token_refiner", 0) == 0;
+            if (strict && !known)
+                throw CudaError("add_lora: no H3 weight is named " + target);
+            ++res.skipped;
+            continue;
+        }
+        const SafeTensor& ta = t;
+        const SafeTensor& tb = st.tensors().at(b_name);
+        if (ta.shape.size() != 2 || tb.shape.size() != 2 || ta.shape[0] != tb.shape[1])
+            throw CudaError("add_lora: " + prefix + ": lora_A [r][in] and lora_B [out][r] shapes disagree");
+        const int r = int(ta.shape[0]), in = int(ta.shape[1]), out = int(tb.shape[0]);
+        const int want_in = kind == kOut ? inner : kind == kFc2 ? F : kind == kAda ? td : d;
+        const int want_out = kind <= kV ? inner : kind == kFc1 ? 2 * F : kind == kAda ? 18 * d : d;
+        if (in != want_in || out != want_out || r <= 0)
+            throw CudaError("add_lora: " + prefix + " is " + std::to_string(out) + " x " + std::to_string(in) + ", the weight " +
+                            std::to_string(want_out) + " x " + std::to_string(want_in));
+        float alpha = float(r);
+        if (const auto it = st.tensors().find(prefix + ".alpha"); it != st.tensors().end())
+            alpha = st.read_f32(prefix + ".alpha").at(0);
+        else if (file_alpha > 0.f)
+            alpha = file_alpha;
+        plan.push_back(Item{name, b_name, prefix, kind, block, r, in, out, scale * alpha / float(r)});
+    }
+    for (const Item& it : plan) {
+        const Kind kind = it.kind;
+        const int block = it.block, r = it.r, in = it.in, out = it.out;
+        // the adapter's row i lands on stored row map[i] of the target matrix
+        std::vector<int32_t> map(out);
+        for (int i = 0; i < out; ++i) {
+            int row = i;
+            if (kind == kK)
+                row = inner + i;
+            else if (kind == kV)
+                row = 2 * inner + i;
+            else if (kind == kFc1) {
+                const int logical = i < F ? F + i : i - F; // Diffusers [value; gate] -> [gate; value]
+                row = logical < F ? (logical / 128) * 256 + logical % 128 : ((logical - F) / 128) * 256 + 128 + (logical - F) % 128;
+            } else if (kind == kAda) {
+                const int c = (i / d) / 3, md = (i / d) % 3, j = i % d; // Diffusers (chunk, modality) -> (modality, chunk)
+                row = block * 18 * d + (md * 6 + c) * d + j;
+            }
+            map[i] = row;
+        }
+        const std::vector<float> A = st.read_f32(it.a), Bm = st.read_f32(it.b);
+        DevBuf dA, dB, dmap;
+        dA.ensure(A.size() * 4), dB.ensure(Bm.size() * 4), dmap.ensure(map.size() * 4);
+        H3_CUDA(cudaMemcpyAsync(dA.p, A.data(), A.size() * 4, cudaMemcpyHostToDevice, s));
+        H3_CUDA(cudaMemcpyAsync(dB.p, Bm.data(), Bm.size() * 4, cudaMemcpyHostToDevice, s));
+        H3_CUDA(cudaMemcpyAsync(dmap.p, map.data(), map.size() * 4, cudaMemcpyHostToDevice, s));
+        Impl::Block& B = d_->blocks[block];
+        DevBuf* w = nullptr;
+        DevBuf *q = nullptr, *qs = nullptr;
+        int rows_total = 0;
+        bool i8 = false;
+        switch (kind) {
+        case kQ: case kK: case kV: w = &B.qkv_w, q = &B.qkv_q, qs = &B.qkv_s, rows_total = 3 * inner, i8 = int8_ & kInt8Qkv; break;
+        case kOut: w = &B.out_w, q = &B.out_q, qs = &B.out_s, rows_total = d, i8 = int8_ & kInt8Out; break;
+        case kFc1: w = &B.fc1_w, q = &B.fc1_q, qs = &B.fc1_s, rows_total = 2 * F, i8 = int8_ & kInt8Fc1; break;
+        case kFc2: w = &B.fc2_w, q = &B.fc2_q, qs = &B.fc2_s, rows_total = d, i8 = int8_ & kInt8Fc2; break;
+        default: w = &d_->ada_w; break;
+        }
+        if (!i8) {
+            lora_merge(dB.as<float>(), dA.as<float>(), out, in, r, it.sc, dmap.as<int32_t>(), w->p, in, nullptr, nullptr, s);
+        } else {
+            // int8 rows: dequantised, merged into a bf16 copy, requantised per row (the rows the adapter covers)
+            DevBuf tmp;
+            tmp.ensure(size_t(rows_total) * in * 2);
+            lora_merge(dB.as<float>(), dA.as<float>(), out, in, r, it.sc, dmap.as<int32_t>(), tmp.p, in, q->as<int8_t>(), qs->as<float>(), s);
+            const int first = kind == kK ? inner : kind == kV ? 2 * inner : 0;
+            quant_weight_rows(static_cast<__nv_bfloat16*>(tmp.p) + size_t(first) * in, out, in, q->as<int8_t>() + size_t(first) * in,
+                              qs->as<float>() + first, s);
+            H3_CUDA(cudaStreamSynchronize(s));
+        }
+        H3_CUDA(cudaStreamSynchronize(s)); // the host copies and temporaries go out of scope
+        ++res.merged;
+        res.rank = r;
+    }
+    return res;
 }
 
 } // namespace h3

@@ -127,6 +127,18 @@ public:
     int denoise(float* video, float* audio, const float* sigma_video, const float* sigma_audio, int points,
                 const std::function<bool(int, int)>& progress);
 
+    // LoRA merge at load (H3::add_lora, src/video/engine.cpp:114; docs/architecture.md:108-116): a safetensors file
+    // of Diffusers-named adapters (transformer_blocks.N.attn.to_q / to_k / to_v / to_out.0, ff.net.0.proj, ff.net.2,
+    // adaln_proj.linear; X.lora_A.weight [r][in], X.lora_B.weight [out][r]; alpha from X.alpha or the file's
+    // "alpha" metadata, else r) merged as W += scale * alpha / r * B A into the bf16 matrices, or into the int8 rows
+    // by requantizing them. Diffusers orders fc1 [value; gate] (this build [gate; value]) and the AdaLN rows
+    // (chunk, modality) (this build (modality, chunk)); the adapter's rows are permuted to match. Targets this build
+    // does not have (the token refiner's) are skipped and counted; with `strict`, any other unknown name is an error.
+    struct LoraResult {
+        int merged = 0, skipped = 0, rank = 0;
+    };
+    LoraResult add_lora(const std::string& path, float scale, bool strict);
+
     const Config& config() const { return c_; }
     const Layout& layout() const { return layout_; }
     int rows() const { return S_; }

@@ -276,6 +276,49 @@ __global__ void euler_kernel(float* x, const float* v, size_t n, float st, float
     }
 }
 
+// 64 x 64 outputs per CTA, 4 x 4 per thread; B and A staged through shared memory 32 of the rank at a time.
+__global__ void __launch_bounds__(256) lora_merge_kernel(const float* B, const float* A, int out, int in, int r, float s,
+                                                         const int32_t* row_map, __nv_bfloat16* W, int64_t ldw, const int8_t* q,
+                                                         const float* qscale)
+{
+    __shared__ float Bs[32][64 + 1]; // [k][i]
+    __shared__ float As[32][64 + 4]; // [k][j]
+    const int i0 = blockIdx.y * 64, j0 = blockIdx.x * 64;
+    const int ti = threadIdx.x / 16, tj = threadIdx.x % 16;
+    float acc[4][4] = {};
+    for (int k0 = 0; k0 < r; k0 += 32) {
+        for (int e = threadIdx.x; e < 32 * 64; e += 256) {
+            const int k = e / 64, x = e % 64;
+            Bs[k][x] = (i0 + x < out && k0 + k < r) ? B[size_t(i0 + x) * r + k0 + k] : 0.f;
+            As[k][x] = (j0 + x < in && k0 + k < r) ? A[size_t(k0 + k) * in + j0 + x] : 0.f;
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int k = 0; k < 32; ++k)
+#pragma unroll
+            for (int a = 0; a < 4; ++a)
+#pragma unroll
+                for (int b = 0; b < 4; ++b)
+                    acc[a][b] = fmaf(Bs[k][ti * 4 + a], As[k][tj * 4 + b], acc[a][b]);
+        __syncthreads();
+    }
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+        const int i = i0 + ti * 4 + a;
+        if (i >= out)
+            continue;
+        const size_t wr = size_t(row_map[i]);
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            const int j = j0 + tj * 4 + b;
+            if (j >= in)
+                continue;
+            const float base = q ? float(q[wr * ldw + j]) * qscale[wr] : __bfloat162float(W[wr * ldw + j]);
+            W[wr * ldw + j] = __float2bfloat16_rn(base + s * acc[a][b]);
+        }
+    }
+}
+
 __global__ void gather_rows_kernel(const float* src, int64_t lds, const int32_t* idx, int rows, int cols, float* dst, int64_t ldd)
 {
     const size_t total = size_t(rows) * cols;
@@ -430,6 +473,16 @@ void euler_rows(float* x, const float* v, size_t n, float t, float sigma, float 
         return;
     const float st = 1.0f - t, ratio = sigma_next / sigma, keep = 1.0f - ratio;
     euler_kernel<<<grid_for(n, 256), 256, 0, s>>>(x, v, n, st, ratio, keep);
+    H3_CUDA(cudaGetLastError());
+}
+
+void lora_merge(const float* B, const float* A, int out, int in, int r, float s, const int32_t* row_map, void* W, int64_t ldw,
+                const int8_t* q, const float* qscale, cudaStream_t st)
+{
+    if (out <= 0 || in <= 0 || r <= 0)
+        return;
+    const dim3 grid((in + 63) / 64, (out + 63) / 64);
+    lora_merge_kernel<<<grid, 256, 0, st>>>(B, A, out, in, r, s, row_map, static_cast<__nv_bfloat16*>(W), ldw, q, qscale);
     H3_CUDA(cudaGetLastError());
 }
 

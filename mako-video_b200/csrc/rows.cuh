@@ -64,6 +64,11 @@ void fill_synthetic(void* dst, int is_bf16, uint64_t n, uint64_t seed, uint32_t 
 // Per-output-row int8 quantisation of a bf16 weight [rows][K]: scale[r] = max|w_r| / 127.
 void quant_weight_rows(const void* w_bf16, int rows, int K, int8_t* q, float* scale, cudaStream_t s);
 
+// LoRA merge (W += s * B A): for i < out, j < in, W[row_map[i]][j] = bf16(base + s * sum_k B[i][k] A[k][j]) with B
+// [out][r] and A [r][in] fp32, base the current bf16 weight, or q[row][j] * qscale[row] when q (int8 rows) is given.
+void lora_merge(const float* B, const float* A, int out, int in, int r, float s, const int32_t* row_map, void* W_bf16, int64_t ldw,
+                const int8_t* q, const float* qscale, cudaStream_t st);
+
 // Permute fc1's rows from [gate (F); value (F)] to 128-row groups [gate g; value g] for the fused SwiGLU epilogue.
 void interleave_gate_value(const void* w_bf16, int F, int K, void* out_bf16, cudaStream_t s);
 void interleave_gate_value_f32(const float* b, int F, float* out, cudaStream_t s);

@@ -98,6 +98,8 @@ SIGNATURES = {
     "h3_step_device": (ctypes.c_int, [_P, _P, _U64, _P, _U64, _F, _F, _P, _P]),
     "h3_synchronize": (ctypes.c_int, [_P]),
     "h3_sigmas": (ctypes.c_int, [_U32, _F, _P, _P]),
+    "h3_add_lora": (ctypes.c_int, [_P, ctypes.c_char_p, _F, _I32, _P, _P]),
+    "h3_lora_inspect": (ctypes.c_int, [ctypes.c_char_p, _P, _U64, _P, _P, _P]),
     "h3k_wait_selftest": (ctypes.c_int, [_U64, _P]),
     "h3_denoise": (ctypes.c_int, [_P, _P, _U64, _P, _U64, _P, _P, _U32, PROGRESS_FN, _P, _P]),
     "h3_stream": (_P, [_P]),
@@ -232,6 +234,15 @@ def rope_table(layout):
     return out
 
 
+def lora_inspect(path):
+    """h3_lora_inspect: (target names, rank, alpha metadata or 0)."""
+    buf = ctypes.create_string_buffer(1 << 20)
+    n, r, a = ctypes.c_uint32(), ctypes.c_uint32(), ctypes.c_float()
+    check(lib().h3_lora_inspect(str(path).encode(), buf, len(buf), ctypes.byref(n), ctypes.byref(r), ctypes.byref(a)))
+    names = buf.value.decode().split("\n") if n.value else []
+    return names, r.value, a.value
+
+
 def sigmas(steps, shift):
     """h3_sigmas: the sampler's schedule (Engine::sigmas)."""
     out = np.zeros(max(steps, 2), np.float32)
@@ -281,6 +292,12 @@ class Model:
             self.close()
         except Exception:
             pass
+
+    def add_lora(self, path, scale=1.0, strict=True):
+        """h3_add_lora: returns (merged, skipped) adapter counts."""
+        merged, skipped = ctypes.c_uint32(), ctypes.c_uint32()
+        check(lib().h3_add_lora(self.h, str(path).encode(), scale, 1 if strict else 0, ctypes.byref(merged), ctypes.byref(skipped)))
+        return merged.value, skipped.value
 
     def set_sparse(self, ratio, local=1):
         check(lib().h3_set_sparse(self.h, ratio, local))

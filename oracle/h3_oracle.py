@@ -30,6 +30,7 @@ Semantics (each a choice where the reference's prose leaves it open):
     d->32 (audio rows) (architecture.md:66-67).
 """
 import math
+import re
 
 import numpy as np
 import torch
@@ -347,6 +348,47 @@ def step(cfg, w, L, text, video, audio, t_video, t_audio, allowed_fn=None, int8=
     out_v = xn[vi] @ w["hv_w"].T + w["hv_b"]
     out_a = xn[ai] @ w["ha_w"].T + w["ha_b"]
     return out_v.numpy(), out_a.numpy()
+
+
+# ---------------------------------------------------------------------------------------------- LoRA merge
+
+
+def apply_lora(cfg, w, adapters, scale, alpha=None):
+    """TransformerRuntime::add_lora restated (architecture.md:108-116): for each Diffusers-named adapter
+    {target: (A [r][in], B [out][r])}, W += scale * alpha / r * B A in fp32, the sum rounded to bf16. The q/k/v
+    targets are the stacked thirds of qkv_w; ff.net.0.proj is [value; gate] in Diffusers and [gate; value] here (rows
+    rotated by half); adaln_proj.linear's rows go from (chunk, modality) to (modality, chunk) (h3_ref_test.cpp:229-241).
+    Targets that are not block matrices are skipped. Returns the number merged."""
+    d, inner, F = cfg["dim"], cfg["heads"] * 128, cfg["ffn"]
+    merged = 0
+    for tgt, (A, B) in adapters.items():
+        m = re.match(r"transformer_blocks\.(\d+)\.(.+)$", tgt)
+        if not m:
+            continue
+        blk, mod = int(m.group(1)), m.group(2)
+        A, B = torch.as_tensor(A, dtype=torch.float32), torch.as_tensor(B, dtype=torch.float32)
+        r = A.shape[0]
+        s = scale * (alpha if alpha else r) / r
+        delta = s * (B @ A)
+        out = delta.shape[0]
+        if mod in ("attn.to_q", "attn.to_k", "attn.to_v"):
+            key, rows = "qkv_w", torch.arange(out) + {"attn.to_q": 0, "attn.to_k": inner, "attn.to_v": 2 * inner}[mod]
+        elif mod == "attn.to_out.0":
+            key, rows = "out_w", torch.arange(out)
+        elif mod == "ff.net.0.proj":
+            key, rows = "fc1_w", (torch.arange(out) + F) % (2 * F)
+        elif mod == "ff.net.2":
+            key, rows = "fc2_w", torch.arange(out)
+        elif mod == "adaln_proj.linear":
+            i = torch.arange(out)
+            c, md, j = (i // d) // 3, (i // d) % 3, i % d
+            key, rows = "ada_w", (md * 6 + c) * d + j
+        else:
+            continue
+        W = w["blocks"][blk][key]
+        W[rows] = bf(W[rows] + delta)
+        merged += 1
+    return merged
 
 
 # ---------------------------------------------------------------------------------------------- the sampler

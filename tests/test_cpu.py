@@ -220,6 +220,40 @@ def test_sigmas_match_reference_known_answers():
             np.testing.assert_array_equal(h3b200.sigmas(steps, shift), O.sigmas(steps, shift))
 
 
+def test_lora_inspect_reads_names_rank_and_alpha(tmp_path):
+    """The safetensors reader behind H3::add_lora: adapter names (file prefixes stripped), rank, the "alpha" metadata."""
+    from tests import safetensors_util as ST
+    rng = np.random.default_rng(0)
+    t = {}
+    for name in ("transformer.transformer_blocks.0.attn.to_q", "transformer.transformer_blocks.3.ff.net.2",
+                 "transformer.token_refiner.blocks.0.attn.to_k"):
+        t[name + ".lora_A.weight"] = rng.standard_normal((16, 64))
+        t[name + ".lora_B.weight"] = rng.standard_normal((32, 16))
+    path = tmp_path / "adapter.safetensors"
+    ST.write(path, t, metadata={"alpha": 8})
+    names, rank, alpha = h3b200.lora_inspect(path)
+    assert sorted(names) == ["token_refiner.blocks.0.attn.to_k", "transformer_blocks.0.attn.to_q", "transformer_blocks.3.ff.net.2"]
+    assert rank == 16 and alpha == 8.0
+
+
+@pytest.mark.parametrize("damage", ["truncated", "garbage", "outside"])
+def test_lora_inspect_refuses_malformed_files(tmp_path, damage):
+    from tests import safetensors_util as ST
+    path = tmp_path / "bad.safetensors"
+    ST.write(path, {"a.lora_A.weight": np.ones((2, 4)), "a.lora_B.weight": np.ones((4, 2))})
+    raw = path.read_bytes()
+    if damage == "truncated":
+        raw = raw[:20]
+    elif damage == "garbage":
+        raw = raw[:8] + b"{not json" + raw[17:]
+    else:
+        raw = raw[:-8]  # the last tensor's bytes run past the end of the file
+    path.write_bytes(raw)
+    rc = h3b200.lib().h3_lora_inspect(str(path).encode(), None, 0, None, None, None)
+    assert rc == h3b200.H3_ERR_ARG
+    assert h3b200.lib().h3_last_error()
+
+
 def test_rope_table_matches_oracle():
     lay = h3b200.Layout.named("c1")
     got = h3b200.rope_table(lay)

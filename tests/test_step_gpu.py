@@ -230,3 +230,110 @@ def test_step_edge_layouts(cuda, layout):
     for a, b in zip(p1, p2):
         assert np.isfinite(a).all()
         np.testing.assert_array_equal(a, b)
+
+
+def _lora_file(path, cfg, rank=16, seed=3, extra=()):
+    """A Diffusers-named LoRA over several kinds of target (two q/k/v thirds, the out projection, fc1 with its
+    [value; gate] rows, fc2, an AdaLN projection) plus a token-refiner target this build skips."""
+    from tests import safetensors_util as ST
+    d, inner, F, td = cfg["dim"], cfg["heads"] * 128, cfg["ffn"], cfg["time_dim"]
+    shapes = {"transformer_blocks.0.attn.to_q": (inner, d), "transformer_blocks.0.attn.to_v": (inner, d),
+              "transformer_blocks.0.attn.to_out.0": (d, inner), "transformer_blocks.1.ff.net.0.proj": (2 * F, d),
+              "transformer_blocks.1.ff.net.2": (d, F), "transformer_blocks.2.adaln_proj.linear": (18 * d, td),
+              "token_refiner.blocks.0.attn.to_q": (d, d)}
+    shapes.update(dict(extra))
+    rng = np.random.default_rng(seed)
+    tensors, adapters = {}, {}
+    for name, (out, inn) in shapes.items():
+        # large enough that every merged matrix moves the output well past the parity tolerance
+        A = rng.standard_normal((rank, inn)) * 0.15
+        B = rng.standard_normal((out, rank)) * 0.15
+        tensors["transformer." + name + ".lora_A.weight"] = A
+        tensors["transformer." + name + ".lora_B.weight"] = B
+        adapters[name] = (ST.bf16_values(A), ST.bf16_values(B))  # the values the BF16 file holds
+    ST.write(path, tensors, metadata={"alpha": 8})
+    return adapters
+
+
+def test_add_lora_merges_like_the_oracle(cuda, tmp_path):
+    """H3::add_lora on a BF16 LoRA file: the merged step against the oracle with the same adapters merged in its own
+    layout; and far from the unmerged model, so every mapped target took effect."""
+    path = tmp_path / "turbo.safetensors"
+    adapters = _lora_file(path, MINI)
+    lay, text, video, audio = inputs(MINI_LAYOUT, MINI)
+    m = H.Model(MINI, seed=0)
+    merged, skipped = m.add_lora(path, scale=0.7)
+    assert (merged, skipped) == (6, 1)
+    m.begin(text, lay)
+    gv, ga = m.step(video, audio, 0.7, 0.4)
+    m.close()
+    w = O.make_weights(MINI, 0)
+    ov0, _ = O.step(MINI, w, MINI_LAYOUT, text, video, audio, 0.7, 0.4)
+    assert O.apply_lora(MINI, w, adapters, 0.7, alpha=8.0) == 6
+    ov, oa = O.step(MINI, w, MINI_LAYOUT, text, video, audio, 0.7, 0.4)
+    for g, o, wdt in ((gv, ov, 96), (ga, oa, 32)):
+        rel, cos = O.diff(g, o, wdt)
+        assert rel < VEL_REL and cos > VEL_COS, (rel, cos)
+    assert O.diff(ov0, ov, 96)[0] > 2 * VEL_REL  # the merge moves the model past the tolerance
+
+
+LORA_TARGETS = ["transformer_blocks.0.attn.to_q", "transformer_blocks.0.attn.to_v", "transformer_blocks.0.attn.to_out.0",
+                "transformer_blocks.1.ff.net.0.proj", "transformer_blocks.1.ff.net.2", "transformer_blocks.2.adaln_proj.linear"]
+
+
+@pytest.mark.parametrize("target", LORA_TARGETS)
+def test_add_lora_each_target_moves_the_step_like_the_oracle(cuda, tmp_path, target):
+    """One adapter at a time: the change it makes to the velocities on the GPU against the change the oracle's own
+    merge makes (the bf16 noise of the two GPU runs largely cancels in the difference, so a row mapped to the wrong
+    place would show as an unrelated change)."""
+    from tests import safetensors_util as ST
+    path = tmp_path / "one.safetensors"
+    adapters = _lora_file(path, MINI)
+    ST.write(path, {"transformer." + target + ".lora_A.weight": adapters[target][0].numpy(),
+                    "transformer." + target + ".lora_B.weight": adapters[target][1].numpy()}, metadata={"alpha": 8})
+    lay, text, video, audio = inputs(MINI_LAYOUT, MINI)
+    outs = []
+    for merge in (False, True):
+        m = H.Model(MINI, seed=0)
+        if merge:
+            assert m.add_lora(path, scale=2.0) == (1, 0)
+        m.begin(text, lay)
+        outs.append(m.step(video, audio, 0.7, 0.4)[0])
+        m.close()
+    w = O.make_weights(MINI, 0)
+    o0, _ = O.step(MINI, w, MINI_LAYOUT, text, video, audio, 0.7, 0.4)
+    O.apply_lora(MINI, w, {target: adapters[target]}, 2.0, alpha=8.0)
+    o1, _ = O.step(MINI, w, MINI_LAYOUT, text, video, audio, 0.7, 0.4)
+    d_gpu, d_ref = outs[1] - outs[0], o1 - o0
+    rel = np.linalg.norm(d_gpu - d_ref) / np.linalg.norm(d_ref)
+    assert np.linalg.norm(d_ref) > 1e-3 * np.linalg.norm(o0)
+    assert rel < 0.2, rel
+
+
+def test_add_lora_int8_and_strict(cuda, tmp_path):
+    """int8 weights take the adapters by requantising their rows (close to the bf16 merge); strict refuses names that
+    match no H3 weight; a file with a bad shape is refused."""
+    path = tmp_path / "turbo.safetensors"
+    adapters = _lora_file(path, MINI)
+    lay, text, video, audio = inputs(MINI_LAYOUT, MINI)
+    m = H.Model(MINI, seed=0, int8_mask=H.INT8_QKV | H.INT8_OUT | H.INT8_FC1 | H.INT8_FC2)
+    assert m.add_lora(path, scale=0.7) == (6, 1)
+    m.begin(text, lay)
+    gv, _ = m.step(video, audio, 0.7, 0.4)
+    m.close()
+    w = O.make_weights(MINI, 0)
+    O.apply_lora(MINI, w, adapters, 0.7, alpha=8.0)
+    ov, _ = O.step(MINI, w, MINI_LAYOUT, text, video, audio, 0.7, 0.4, int8=15)
+    rel, cos = O.diff(gv, ov, 96)
+    assert rel < 3e-2 and cos > 0.995, (rel, cos)
+    bad = tmp_path / "unknown.safetensors"
+    _lora_file(bad, MINI, extra=[("transformer_blocks.0.attn.to_z", (512, 512))])
+    m = H.Model(MINI, seed=0)
+    with pytest.raises(H.H3Error):
+        m.add_lora(bad, strict=True)
+    assert m.add_lora(bad, strict=False) == (6, 2)
+    wrong = tmp_path / "wrong.safetensors"
+    _lora_file(wrong, MINI, extra=[("transformer_blocks.0.ff.net.2", (512, 999))])
+    with pytest.raises(H.H3Error):
+        m.add_lora(wrong)
+    m.close()
