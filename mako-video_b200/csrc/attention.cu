@@ -4,8 +4,9 @@
 // meanwhile, exact after the final division).
 //   attn2_kernel  dense: two 128-row query tiles per CTA share each K/V tile; the tensor core alternates between the
 //                 tiles so one tile's MMAs overlap the other tile's softmax.
-//   attn3_kernel  sparse (and usable dense): one query tile per CTA with two S buffers, so S_{j+1} is computed while
-//                 the softmax works on S_j; query tiles carry their own key lists.
+//   attn3_kernel  sparse: one query tile of two units (cubes) per CTA, each unit with its own key list, as two
+//                 M = 64 MMAs into the two lane halves of TMEM; two S buffers, so S(j+1) is computed while the softmax
+//                 works on S(j).
 // Every tile is four 64x64 TMA boxes (two 64-row units x two 64-dim halves) of consecutive rows: in the packed row
 // order each 4x4x4 latent cube is one run of rows, so a sparse unit is the same plain box as a dense one (the rows
 // past a cut-short cube's count belong to the next unit and are masked).
@@ -50,21 +51,12 @@ __device__ __forceinline__ __nv_bfloat16* out_ptr(const AttnParams& p, int row, 
            (size_t(p.my_rank) * p.rows_per_rank + local) * (size_t(p.heads) * 128) + head * 128 + d0;
 }
 
-// Key block j of a tile that sees every row: rows [128 j, 128 j + 128) as two 64-row units.
+// Key block j of a query unit that sees every row: rows [128 j, 128 j + 128) as two 64-row key units, in the pass
+// list entry format (first row of key unit 0, of key unit 1 or -1, rows of unit 0 | rows of unit 1 << 8, 0).
 __device__ __forceinline__ int4 every_row_block(int j, int rows)
 {
     const int na = min(max(rows - 128 * j, 0), 64), nb = min(max(rows - 128 * j - 64, 0), 64);
-    return make_int4(128 * j, nb > 0 ? 128 * j + 64 : -1, 15, na | (nb << 8));
-}
-
-// Visible keys of half kh of block entry e for query half qh, as a 64-bit mask over the unit's loaded rows.
-__device__ __forceinline__ uint64_t block_key_mask(const int4& e, int qh, int kh)
-{
-    const int first = kh ? e.y : e.x;
-    const int n = (e.w >> (8 * kh)) & 0xff;
-    if (first < 0 || n <= 0 || !((e.z >> (2 * qh + kh)) & 1))
-        return 0ull;
-    return n >= 64 ? ~0ull : (1ull << n) - 1;
+    return make_int4(128 * j, nb > 0 ? 128 * j + 64 : -1, na | (nb << 8), 0);
 }
 
 // ------------------------------------------------------------------------------------------------------------
@@ -371,14 +363,19 @@ __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid
 }
 
 // ------------------------------------------------------------------------------------------------------------
-// One query tile (128 rows) per CTA with double-buffered scores, dense or sparse.
-//   warp 0      TMA: Q once; K_j into a 3-stage ring (freed as soon as S_j is done), V_j into a 2-stage ring
-//   warp 1      MMA: S_0, S_1 up front; then per block PV_j (A = P_j from TMEM) and S_{j+2} into the buffer S_j
-//               leaves, so S_{j+1} is always ready when the softmax finishes block j
-//   warps 2..9  softmax: two warps per query row, each over one 64-key unit of the block (hc = 0, 1), agreeing on
-//               the row maximum through shared memory; P_j (bf16) written back over S_j's first 64 columns.
-// TMEM: S buffer 0 | S buffer 1 | O (128 columns each). S_{j+2} overwrites P_j only after PV_j read it (one thread
-// issues both, and the tensor core runs them in order). The softmax of block j may rescale O only once PV_{j-1} is
+// Sparse attention: one CTA per query tile of two units (two cubes, or two chunks of dense rows), each unit with its
+// own key list, so no unit computes scores against keys only the other one selected. The tensor core runs M = 64
+// MMAs: unit a's 64 query rows land in TMEM lanes 0-15 of every 32-lane subpartition, unit b's in lanes 16-31 (the
+// lane offset of the MMA's TMEM address), so the two units' S and O share columns and every softmax warp holds 16 rows
+// of each. Per step j: S_a(j) = Q_a K_a(j)^T and S_b(j) = Q_b K_b(j)^T (128 keys each), then P_x(j) V_x(j) into O_x.
+//   warp 0      TMA: Q once; per step K_a, K_b into a 3-slot ring (freed as soon as their S MMAs are done) and V_a,
+//               V_b into a 2-slot ring
+//   warp 1      MMA: S(0), S(1) up front; then per step PV_a(j), PV_b(j) (A = P from TMEM) and S(j+2) into the S
+//               buffer step j leaves, so S(j+1) is ready when the softmax finishes step j
+//   warps 2..9  softmax: two warps per 32-lane quarter, each over one 64-key half of the step (hc = 0, 1), agreeing on
+//               the row maximum through shared memory; P (bf16) written back over S's first 64 columns
+// TMEM: S buffer 0 | S buffer 1 | O (128 columns each). S(j+2) overwrites P(j) only after PV(j) read it (one thread
+// issues both, and the tensor core runs them in order). The softmax of step j may rescale O only once PV(j-1) is
 // done (it waits for that only when a rescale is needed).
 constexpr int A3_KST = 3, A3_VST = 2;
 constexpr int NT3 = 64 + 256;
@@ -388,8 +385,8 @@ constexpr int A3_OFF_V = A3_OFF_K + A3_KST * TILE;
 constexpr int A3_OFF_BAR = A3_OFF_V + A3_VST * TILE;
 constexpr int A3_OFF_RED = A3_OFF_BAR + 256;
 constexpr int A3_SMEM = A3_OFF_RED + 3 * 2 * 128 * 4 + 1024;
+constexpr uint32_t LANE16 = 16u << 16; // TMEM address of lane 16: unit b's half of each subpartition
 
-template <bool SPARSE>
 __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ Maps maps, const AttnParams p)
 {
     extern __shared__ uint8_t smem_raw[];
@@ -409,35 +406,25 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
     const int warp = warp_id();
-    // Sparse launches are 1-D and longest first: the dense-row query tiles (which see every key, several times a video
+    // Launches are 1-D and longest first: the dense-row query tiles (which see every key, several times a video
     // tile's work) of every head, then each head's video tiles together (they share the head's keys in L2).
-    int tile = blockIdx.x, head = blockIdx.y;
-    if constexpr (SPARSE) {
+    int tile, head;
+    {
         const int vt = (p.grid.cubes() + 1) / 2, dt = p.q_tiles - vt;
         const int id = blockIdx.x;
-        if (id < p.heads * dt) {
+        if (id < p.heads * dt)
             head = id % p.heads, tile = vt + id / p.heads;
-        } else {
+        else
             head = (id - p.heads * dt) / vt, tile = (id - p.heads * dt) % vt;
-        }
     }
-    int nkv;
-    int4 qr; // (first row of query half 0, of half 1 or -1, rows of half 0, rows of half 1)
-    const int4* entries = nullptr;
-    bool every = true; // the tile sees every row
-    if constexpr (SPARSE) {
-        nkv = p.nblocks[head * p.q_tiles + tile];
-        every = nkv < 0;
-        if (every)
-            nkv = (p.rows + 127) / 128;
-        qr = p.q_rows[tile];
-        entries = p.blocks + (size_t(head) * p.q_tiles + tile) * p.max_blocks;
-    } else {
+    int nkv = p.nblocks[head * p.q_tiles + tile];
+    const bool every = nkv < 0;
+    if (every)
         nkv = (p.rows + 127) / 128;
-        const int4 e = every_row_block(tile, p.rows);
-        qr = make_int4(e.x, e.y, e.w & 0xff, e.w >> 8);
-    }
-    auto entry = [&](int j) -> int4 { return every ? every_row_block(j, p.rows) : entries[j]; };
+    const int4 qr = p.q_rows[tile]; // (first row of unit a, of unit b or -1, rows of a, rows of b)
+    const int4* entries = p.blocks + (size_t(head) * p.q_tiles + tile) * p.max_blocks;
+    // step j's keys for query unit x
+    auto entry = [&](int j, int x) -> int4 { return every ? every_row_block(j, p.rows) : entries[2 * j + x]; };
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
@@ -469,105 +456,119 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
 
     if (nkv > 0 && warp == 0 && elect_one_lane()) {
         // ------------------------------------------------------------------------------------------ TMA
+        // Q: unit a's rows into rows 0-63 of the tile, unit b's into rows 64-127 (unit a's again if there is no b)
         mbar_arrive_expect_tx(q_full, TILE);
         load_rows(smem + A3_OFF_Q, 0, qr.x, head, &maps.q, q_full);
         load_rows(smem + A3_OFF_Q, 1, qr.y < 0 ? qr.x : qr.y, head, &maps.q, q_full);
-        // K runs ahead of V by up to the depth of its ring; each list entry is fetched while the ring slot is awaited
-        int jk = 0, jv = 0;
-        int4 ek = entry(0), ev = ek;
+        // Ring items i = 2 j + x (step j, query unit x): K runs ahead of V by up to the depth of its ring. A padding
+        // entry (no key unit) loads row 0: the keys are masked.
+        const int items = 2 * nkv;
+        int ik = 0, iv = 0;
         bool ok = true;
-        while (ok && jv < nkv) {
-            const bool k_turn = jk < nkv && jk < jv + A3_KST;
+        while (ok && iv < items) {
+            const bool k_turn = ik < items && ik < iv + A3_KST;
+            const int i = k_turn ? ik : iv;
+            const int4 e = entry(i >> 1, i & 1);
+            const int r0 = e.x < 0 ? 0 : e.x, r1 = e.y < 0 ? r0 : e.y;
             if (k_turn) {
-                const int s = jk % A3_KST;
-                if (!(ok = mbar_wait(&k_empty[s], ((jk / A3_KST) & 1) ^ 1)))
+                const int s = ik % A3_KST;
+                if (!(ok = mbar_wait(&k_empty[s], ((ik / A3_KST) & 1) ^ 1)))
                     break;
                 mbar_arrive_expect_tx(&k_full[s], TILE);
-                load_rows(smem + A3_OFF_K + s * TILE, 0, ek.x, head, &maps.k, &k_full[s]);
-                load_rows(smem + A3_OFF_K + s * TILE, 1, ek.y < 0 ? ek.x : ek.y, head, &maps.k, &k_full[s]);
-                if (++jk < nkv)
-                    ek = entry(jk);
+                load_rows(smem + A3_OFF_K + s * TILE, 0, r0, head, &maps.k, &k_full[s]);
+                load_rows(smem + A3_OFF_K + s * TILE, 1, r1, head, &maps.k, &k_full[s]);
+                ++ik;
             } else {
-                const int s = jv % A3_VST;
-                if (!(ok = mbar_wait(&v_empty[s], ((jv / A3_VST) & 1) ^ 1)))
+                const int s = iv % A3_VST;
+                if (!(ok = mbar_wait(&v_empty[s], ((iv / A3_VST) & 1) ^ 1)))
                     break;
                 mbar_arrive_expect_tx(&v_full[s], TILE);
-                load_rows(smem + A3_OFF_V + s * TILE, 0, ev.x, head, &maps.v, &v_full[s]);
-                load_rows(smem + A3_OFF_V + s * TILE, 1, ev.y < 0 ? ev.x : ev.y, head, &maps.v, &v_full[s]);
-                if (++jv < nkv)
-                    ev = entry(jv);
+                load_rows(smem + A3_OFF_V + s * TILE, 0, r0, head, &maps.v, &v_full[s]);
+                load_rows(smem + A3_OFF_V + s * TILE, 1, r1, head, &maps.v, &v_full[s]);
+                ++iv;
             }
         }
     } else if (nkv > 0 && warp == 1 && elect_one_lane()) {
         // ------------------------------------------------------------------------------------------ MMA
-        const uint32_t id_s = idesc_bf16(128, 128);
-        const uint32_t id_pv = idesc_bf16(128, 128, false, true);
+        const uint32_t id_s = idesc_bf16(64, 128);
+        const uint32_t id_pv = idesc_bf16(64, 128, false, true);
         const uint32_t sq = smem_u32(smem + A3_OFF_Q);
-        auto issue_s = [&](int j) {
-            const int s = j % A3_KST;
-            const uint32_t sk = smem_u32(smem + A3_OFF_K + s * TILE);
+        // S(j) for both query units (unit x: query rows at 8192 x within each dim half, lanes at 16 x)
+        auto issue_s = [&](int j) -> bool {
+            for (int x = 0; x < 2; ++x) {
+                const int i = 2 * j + x, s = i % A3_KST;
+                if (!mbar_wait(&k_full[s], (i / A3_KST) & 1))
+                    return false;
+                tc_fence_after();
+                const uint32_t sk = smem_u32(smem + A3_OFF_K + s * TILE);
 #pragma unroll
-            for (int kk = 0; kk < 8; ++kk) {
-                const uint32_t off = (kk >> 2) * HALF + (kk & 3) * 32;
-                mma_bf16_ss(tmem + (j & 1) * 128, sdesc_sw128(sq + off, 16, 1024), sdesc_sw128(sk + off, 16, 1024), id_s, kk > 0);
+                for (int kk = 0; kk < 8; ++kk) {
+                    const uint32_t off = (kk >> 2) * HALF + (kk & 3) * 32;
+                    mma_bf16_ss(tmem + (j & 1) * 128 + (x ? LANE16 : 0u), sdesc_sw128(sq + x * 8192 + off, 16, 1024),
+                                sdesc_sw128(sk + off, 16, 1024), id_s, kk > 0);
+                }
+                mma_commit(&k_empty[s]);
             }
             mma_commit(&s_full[j & 1]);
-            mma_commit(&k_empty[s]);
+            return true;
         };
         bool ok = mbar_wait(q_full, 0);
-        for (int j = 0; j < 2 && j < nkv && ok; ++j) {
-            if ((ok = mbar_wait(&k_full[j % A3_KST], (j / A3_KST) & 1))) {
-                tc_fence_after();
-                issue_s(j);
-            }
-        }
+        for (int j = 0; j < 2 && j < nkv && ok; ++j)
+            ok = issue_s(j);
         for (int j = 0; j < nkv && ok; ++j) {
-            const int sv = j % A3_VST;
-            if (!(ok = mbar_wait(p_full, j & 1) && mbar_wait(&v_full[sv], (j / A3_VST) & 1)))
+            if (!(ok = mbar_wait(p_full, j & 1)))
                 break;
-            tc_fence_after();
-            const uint32_t vb = smem_u32(smem + A3_OFF_V + sv * TILE);
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk)
-                mma_bf16_ts(tmem + T_O, tmem + (j & 1) * 128 + kk * 8, sdesc_sw128(vb + kk * 2048, HALF, 1024), id_pv, (j | kk) != 0);
-            mma_commit(pv_done);
-            mma_commit(&v_empty[sv]);
-            if (j + 2 < nkv) {
-                if (!(ok = mbar_wait(&k_full[(j + 2) % A3_KST], ((j + 2) / A3_KST) & 1)))
+            for (int x = 0; x < 2 && ok; ++x) {
+                const int i = 2 * j + x, sv = i % A3_VST;
+                if (!(ok = mbar_wait(&v_full[sv], (i / A3_VST) & 1)))
                     break;
                 tc_fence_after();
-                issue_s(j + 2);
+                const uint32_t vb = smem_u32(smem + A3_OFF_V + sv * TILE);
+                const uint32_t lane = x ? LANE16 : 0u;
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk)
+                    mma_bf16_ts(tmem + T_O + lane, tmem + (j & 1) * 128 + lane + kk * 8, sdesc_sw128(vb + kk * 2048, HALF, 1024), id_pv,
+                                (j | kk) != 0);
+                mma_commit(&v_empty[sv]);
             }
+            if (!ok)
+                break;
+            mma_commit(pv_done);
+            if (j + 2 < nkv)
+                ok = issue_s(j + 2);
         }
         mma_commit(drain);
         mbar_wait(drain, 0);
     } else if (nkv > 0 && warp >= 2) {
         // -------------------------------------------------------------------------------------- softmax
-        const int hc = (warp - 2) >> 2; // key unit of the block this warp handles
+        const int hc = (warp - 2) >> 2; // 64-key half of the step this warp handles
         const int quarter = warp & 3;
-        const int row = quarter * 32 + lane_id();
-        const int qh = row >> 6;
+        const int row = quarter * 32 + lane_id(); // TMEM lane
+        const int x = (lane_id() >> 4) & 1;       // query unit of this lane's row
+        const int m = quarter * 16 + (lane_id() & 15); // the row's index inside its unit
         const uint32_t lane_base = uint32_t(quarter * 32) << 16;
         const uint32_t tO = tmem + lane_base + T_O + hc * 64;
         float* red = reinterpret_cast<float*>(smem + A3_OFF_RED); // [3 slots][2 slices][128 rows]
         const float sl2 = p.scale * 1.4426950408889634f;
-        float m = -INFINITY, l = 0.f;
+        float m_run = -INFINITY, l = 0.f;
         bool ok = true;
-        int4 e_next = entry(0);
+        int4 e_next = entry(0, x);
         for (int j = 0; j < nkv; ++j) {
             const uint32_t tS = tmem + lane_base + (j & 1) * 128;
-            // Keys this slice may see (not past the unit's rows, unit selected for this query half). km is the same for
-            // the whole warp (its rows share the query half qh), so a slice with no visible key skips its scores.
+            // The keys of this slice the row may see: the first n rows of its unit's key unit hc
             const int4 e = e_next;
             if (j + 1 < nkv)
-                e_next = entry(j + 1);
-            const uint64_t km = block_key_mask(e, qh, hc);
+                e_next = entry(j + 1, x);
+            const int first = hc ? e.y : e.x;
+            const int n = first < 0 ? 0 : min((e.z >> (8 * hc)) & 0xff, 64);
+            // the whole warp may skip the exponentials only when neither unit's rows see a key here
+            const bool warp_dead = __all_sync(0xffffffffu, n == 0);
             if (!(ok = mbar_wait(&s_full[j & 1], (j >> 1) & 1)))
                 break;
             tc_fence_after();
             float s[64];
             float mx = -INFINITY;
-            if (km != 0ull) {
+            if (!warp_dead) {
                 {
                     uint32_t r[2][32];
                     tmem_ld32(tS + hc * 64, r[0]);
@@ -579,10 +580,10 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
                         for (int i = 0; i < 32; ++i)
                             s[c * 32 + i] = __uint_as_float(r[c][i]);
                 }
-                if (km != ~0ull) {
+                if (n < 64) {
 #pragma unroll
                     for (int c = 0; c < 64; ++c)
-                        if (!((km >> c) & 1))
+                        if (c >= n)
                             s[c] = -INFINITY;
                 }
                 float mp[8];
@@ -608,21 +609,21 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
                 mx = fmaxf(mx, slot[(hc ^ 1) * 128 + row]);
             }
             const float m_cand = mx * sl2;
-            const bool need = m_cand > m + kRescaleThreshold;
-            const float m_use = need ? m_cand : m;
-            const float alpha = need ? ex2_approx(m - m_use) : 1.f;
+            const bool need = m_cand > m_run + kRescaleThreshold;
+            const float m_use = need ? m_cand : m_run;
+            const float alpha = need ? ex2_approx(m_run - m_use) : 1.f;
             const float msub = m_use == -INFINITY ? 0.f : m_use;
             const float2 scale2 = make_float2(sl2, sl2), neg2 = make_float2(-msub, -msub);
             uint32_t pk[32];
             float rs = 0.f;
-            if (km != 0ull) {
+            if (!warp_dead) {
                 float2 sp[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
                 for (int c = 0; c < 32; ++c) {
-                    const float2 x = fma2(make_float2(s[2 * c], s[2 * c + 1]), scale2, neg2);
-                    const float2 e = make_float2(ex2_approx(x.x), ex2_approx(x.y));
-                    sp[c & 3] = add2(sp[c & 3], e);
-                    pk[c] = pack_bf16x2(e.x, e.y);
+                    const float2 xx = fma2(make_float2(s[2 * c], s[2 * c + 1]), scale2, neg2);
+                    const float2 ev = make_float2(ex2_approx(xx.x), ex2_approx(xx.y));
+                    sp[c & 3] = add2(sp[c & 3], ev);
+                    pk[c] = pack_bf16x2(ev.x, ev.y);
                 }
                 const float2 s01 = add2(add2(sp[0], sp[1]), add2(sp[2], sp[3]));
                 rs = s01.x + s01.y;
@@ -632,7 +633,7 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
                     pk[c] = 0u;
             }
             if (j > 0 && __any_sync(0xffffffffu, need)) {
-                // O holds PV_0..PV_{j-2} for sure; wait for PV_{j-1} before scaling it
+                // O holds PV(0..j-2) for sure; wait for PV(j-1) before scaling it
                 if (!(ok = mbar_wait(pv_done, (j - 1) & 1)))
                     break;
                 tc_fence_after();
@@ -648,7 +649,7 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
                 }
             }
             l = l * alpha + rs;
-            m = m_use;
+            m_run = m_use;
             tmem_st32(tS + hc * 32, pk);
             tmem_wait_st();
             tc_fence_before();
@@ -667,8 +668,8 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
         }
         if (ok && mbar_wait(pv_done, (nkv - 1) & 1)) {
             tc_fence_after();
-            const int first = qh ? qr.y : qr.x, nq = qh ? qr.w : qr.z;
-            const int out_row = first >= 0 && (row & 63) < nq ? first + (row & 63) : -1;
+            const int first = x ? qr.y : qr.x, nq = x ? qr.w : qr.z;
+            const int out_row = first >= 0 && m < nq ? first + m : -1;
             const float inv = l > 0.f ? 1.f / l : 0.f;
             __nv_bfloat16* dst = out_ptr(p, out_row, head, hc * 64);
 #pragma unroll 1
@@ -722,7 +723,7 @@ void attention(const AttnParams& p, cudaStream_t s)
     static bool attr[2] = {false, false};
     if (!attr[sparse]) {
         if (sparse)
-            H3_CUDA(cudaFuncSetAttribute(attn3_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, A3_SMEM));
+            H3_CUDA(cudaFuncSetAttribute(attn3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, A3_SMEM));
         else
             H3_CUDA(cudaFuncSetAttribute(attn2_kernel<A2_SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize, A2_SMEM));
         attr[sparse] = true;
@@ -730,7 +731,7 @@ void attention(const AttnParams& p, cudaStream_t s)
     // Dense: two query tiles per CTA share every K/V tile (half the shared-memory traffic per FLOP). Sparse: query
     // tiles have their own key lists, so one tile per CTA with double-buffered scores.
     if (sparse)
-        attn3_kernel<true><<<p.q_tiles * p.heads, NT3, A3_SMEM, s>>>(maps, p);
+        attn3_kernel<<<p.q_tiles * p.heads, NT3, A3_SMEM, s>>>(maps, p);
     else
         attn2_kernel<A2_SPLIT><<<dim3((p.rows + 255) / 256, p.heads), NT2, A2_SMEM, s>>>(maps, p);
     H3_CUDA(cudaGetLastError());

@@ -73,11 +73,12 @@ struct AttnParams {
     int rows_per_rank = 0, my_rank = 0;
     float scale = 0.08838834764831845f; // 1 / sqrt(128)
 
-    // Sparse mode (blocks != null; rows in the packed order above). Query tile t is two units, q_rows[t] = (first
-    // row a, first row b or -1, rows of a, rows of b). For head h it visits nblocks[h * q_tiles + t] key blocks
-    // blocks[(h * q_tiles + t) * max_blocks + j] = (first row a, first row b or -1, keep, rows of a | rows of b << 8):
-    // 64 keys from each first row, of which the unit's row count are its tokens; `keep` bit (2 * qh + kh) is set when
-    // query half qh may see key unit kh. nblocks -1: the tile sees every row (128-row blocks over all rows).
+    // Sparse mode (blocks != null; rows in the packed order above). Query tile t is two units (two cubes, or two
+    // chunks of dense rows), q_rows[t] = (first row a, first row b or -1, rows of a, rows of b); each unit has its
+    // own key list. For head h the tile takes nblocks[h * q_tiles + t] steps; step j has one entry per query unit,
+    // blocks[(h * q_tiles + t) * max_blocks + 2 j + x] = (first row of key unit 0, of key unit 1 or -1, rows of unit 0
+    // | rows of unit 1 << 8, 0): 64 keys from each first row, of which the unit's row count are its tokens (an entry
+    // of -1s is padding). nblocks -1: both query units see every row (128-row blocks over all rows).
     const int4* blocks = nullptr;
     const int32_t* nblocks = nullptr;
     const int4* q_rows = nullptr;

@@ -21,7 +21,7 @@ void sparse_sizes(const CubeGrid& g, float ratio, int local, int& kcap, int& q_t
     kcap = std::max(sparse_k(ratio, g.cubes()), sparse_forced(local));
     kcap = std::min(kcap, g.cubes());
     q_tiles = (g.cubes() + 1) / 2 + (g.dense_units() + 1) / 2;
-    max_blocks = (2 * kcap + g.dense_units() + 1) / 2;
+    max_blocks = 2 * ((kcap + g.dense_units() + 1) / 2); // two entries (one per cube of the tile) a step
 }
 
 namespace {
@@ -250,50 +250,38 @@ __global__ void build_passes_kernel(const int32_t* sel, const int32_t* nsel, int
         return;
     const int h = idx / q_tiles, t = idx % q_tiles;
     if (t >= vt) {
-        nblocks[idx] = -1; // dense query rows attend every unit
+        nblocks[idx] = -1; // dense query rows attend every row
         return;
     }
-    const int c0 = 2 * t, c1 = 2 * t + 1;
-    const int32_t* A = sel + (size_t(h) * nc + c0) * kcap;
-    const int na = nsel[size_t(h) * nc + c0];
-    const int32_t* B = c1 < nc ? sel + (size_t(h) * nc + c1) * kcap : nullptr;
-    const int nb = c1 < nc ? nsel[size_t(h) * nc + c1] : 0;
+    // Each cube of the tile gets its own list: its selected cubes (ascending) then every dense unit, two units a
+    // step; the shorter list is padded with empty entries.
+    const int max_steps = max_blocks / 2;
     int4* out = blocks + size_t(idx) * max_blocks;
-    int ia = 0, ib = 0, nout = 0;
-    int pend_u = -1, pend_bits = 0; // a unit waiting for its pair partner
-    auto emit = [&](int u, int bits) {
-        if (pend_u < 0) {
-            pend_u = u, pend_bits = bits;
-        } else {
-            // keep bit (2 * qh + kh): unit a is kh 0, unit b is kh 1
-            const int keep = (pend_bits & 1) | ((bits & 1) << 1) | ((pend_bits & 2) << 1) | ((bits & 2) << 2);
-            const int2 sa = span_of(pend_u, g), sb = span_of(u, g);
-            if (nout < max_blocks)
-                out[nout] = make_int4(sa.x, sb.x, keep, sa.y | (sb.y << 8));
-            ++nout;
-            pend_u = -1;
-        }
-    };
-    while (ia < na || ib < nb) {
-        const int a = ia < na ? A[ia] : 0x7fffffff, b = ib < nb ? B[ib] : 0x7fffffff;
-        if (a == b) {
-            emit(a, 3), ++ia, ++ib;
-        } else if (a < b) {
-            emit(a, 1), ++ia;
-        } else {
-            emit(b, 2), ++ib;
+    int steps = 0;
+    for (int x = 0; x < 2; ++x) {
+        const int c = 2 * t + x;
+        const int32_t* L = c < nc ? sel + (size_t(h) * nc + c) * kcap : nullptr;
+        const int n = c < nc ? nsel[size_t(h) * nc + c] : -nd; // a missing cube gets no units at all
+        const int len = n + nd;
+        const int st = (len + 1) / 2;
+        steps = max(steps, st);
+        for (int s2 = 0; s2 < min(st, max_steps); ++s2) {
+            int2 sp[2];
+            for (int k = 0; k < 2; ++k) {
+                const int i = 2 * s2 + k;
+                sp[k] = i < len ? span_of(i < n ? L[i] : nc + (i - n), g) : make_int2(-1, 0);
+            }
+            out[2 * s2 + x] = make_int4(sp[0].x, sp[1].x, sp[0].y | (sp[1].y << 8), 0);
         }
     }
-    for (int u = 0; u < nd; ++u)
-        emit(nc + u, 3);
-    if (pend_u >= 0) {
-        const int keep = (pend_bits & 1) | ((pend_bits & 2) << 1);
-        const int2 sa = span_of(pend_u, g);
-        if (nout < max_blocks)
-            out[nout] = make_int4(sa.x, -1, keep, sa.y);
-        ++nout;
+    steps = min(steps, max_steps);
+    for (int x = 0; x < 2; ++x) {
+        const int c = 2 * t + x;
+        const int len = (c < nc ? nsel[size_t(h) * nc + c] : -nd) + nd;
+        for (int s2 = (len + 1) / 2; s2 < steps; ++s2)
+            out[2 * s2 + x] = make_int4(-1, -1, 0, 0);
     }
-    nblocks[idx] = min(nout, max_blocks);
+    nblocks[idx] = steps;
 }
 
 } // namespace
