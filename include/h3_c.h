@@ -34,6 +34,9 @@ typedef struct h3_config {
     uint32_t video_patch;    /* 96 (H3::kVideoPatch: a 2x2 patch of 24 channels) */
     uint32_t audio_channels; /* 32 (H3::kAudioChannels) */
     float eps;               /* RMS norm epsilon */
+    uint32_t refiner_blocks; /* token refiner blocks run over the text rows in h3_begin (MiniMax-H3: 2; 0: none, at most
+                              * 2). Plain pre-norm blocks of the step's widths without modulation or rotary positions,
+                              * then a weighted RMS norm (docs/architecture.md:25-27). */
 } h3_config;
 
 /* A reference block of a ref2va layout (H3::Layout::Reference, src/video/engine.cpp:604-616;
@@ -67,8 +70,9 @@ typedef struct h3_world {
     uint8_t nccl_id[128];    /* from h3_nccl_unique_id on rank 0, passed to every rank */
 } h3_world;
 
-/* Probe callback (H3::set_probe, tests/h3_ref_test.cpp:215-217): name is one of temb, mod0, x0, block, norm_out;
- * layer is the block for "block" and -1 otherwise; data is host memory valid during the call. Single-rank only. */
+/* Probe callback (H3::set_probe, tests/h3_ref_test.cpp:215-217): name is one of txt (the text rows after the token
+ * refiner, from h3_begin; tests/h3_ref_test.cpp:219), temb, mod0, x0, block, norm_out; layer is the block for "block"
+ * and -1 otherwise; data is host memory valid during the call. Single-rank only. */
 typedef void (*h3_probe_fn)(void* user, const char* name, int32_t layer, const float* data, uint64_t n);
 
 /* The message of the last failed call on this thread ("" if none). */

@@ -101,7 +101,7 @@ public:
     H3& operator=(const H3&) = delete;
 
     // MiniMax-H3's shape.
-    static h3_config h3_mini_h3() { return h3_config{kDim, 56, 14336, 50, kTimeDim, kText, kVideoPatch, kAudioChannels, 1e-6f}; }
+    static h3_config h3_mini_h3() { return h3_config{kDim, 56, 14336, 50, kTimeDim, kText, kVideoPatch, kAudioChannels, 1e-6f, 2}; }
 
     // set_sparse(ratio, local) (src/video/engine.cpp:112).
     void set_sparse(float ratio, uint32_t local) { check(h3_set_sparse(m_, ratio, local)); }

@@ -197,9 +197,11 @@ int h3_create(const h3_config* cfg, const char* weights, uint32_t int8_mask, flo
         h3::Config c;
         c.dim = int(cfg->dim), c.heads = int(cfg->heads), c.ffn = int(cfg->ffn), c.blocks = int(cfg->blocks);
         c.time_dim = int(cfg->time_dim), c.text_dim = int(cfg->text_dim), c.video_patch = int(cfg->video_patch);
-        c.audio_channels = int(cfg->audio_channels), c.eps = cfg->eps;
+        c.audio_channels = int(cfg->audio_channels), c.eps = cfg->eps, c.refiner = int(cfg->refiner_blocks);
         if (c.video_patch != 96 || c.audio_channels != 32)
             throw ArgError("h3_create: video_patch must be 96 and audio_channels 32");
+        if (cfg->refiner_blocks > 2)
+            throw ArgError("h3_create: at most 2 token refiner blocks (MiniMax-H3 has 2)");
         h3::World wd;
         if (world) {
             wd.rank = world->rank, wd.size = world->size;

@@ -233,7 +233,9 @@ struct DevBuf {
 // Synthetic tensor ids (fixed: the CPU oracle regenerates the same values from them).
 enum : uint32_t {
     kTInW = 1, kTInB, kTOutW, kTOutB, kVpW, kVpB, kApW, kApB, kCondW, kCondB, kFadaW, kFadaB, kHvW, kHvB, kHaW, kHaB,
+    kRefinerNorm = 17,
     kBlockBase = 100, kBlockStride = 20,
+    kRefinerBase = 60, // token refiner block r (r < 2) at kRefinerBase + kBlockStride * r, without the AdaLN ids
 };
 enum : uint32_t { kAdaW = 0, kAdaB, kNorm1, kQkvW, kQkvB, kQn, kKn, kOutW, kOutB, kNorm2, kFc1W, kFc1B, kFc2W, kFc2B };
 
@@ -253,6 +255,8 @@ struct Model::Impl {
         DevBuf qkv_q, qkv_s, out_q, out_s, fc1_q, fc1_s, fc2_q, fc2_s; // int8 rows and scales
     };
     std::vector<Block> blocks;
+    std::vector<Block> refiner; // token refiner blocks (bf16 only; no AdaLN)
+    DevBuf refiner_norm;        // [d] weight of the refiner's final RMS norm
     // per layout
     DevBuf x_text;     // [T][d] f32
     DevBuf rope;       // [S_local][48][2]
@@ -396,6 +400,33 @@ Model::Model(const Config& c, uint64_t seed, uint32_t int8_mask, const World& wo
         if (int8_ & kInt8Fc2)
             quant(b.fc2_w, b.fc2_q, b.fc2_s, d, F);
     }
+    if (c.refiner < 0 || c.refiner > 2)
+        throw CudaError("config: at most 2 token refiner blocks");
+    d_->refiner.resize(c.refiner);
+    for (int r = 0; r < c.refiner; ++r) {
+        const uint32_t base = kRefinerBase + kBlockStride * r;
+        Impl::Block& b = d_->refiner[r];
+        fill(b.norm1, d, false, base + kNorm1, 1.f, kStd);
+        fill(b.qkv_w, size_t(3) * inner * d, true, base + kQkvW, 0.f, kStd);
+        fill(b.qkv_b, size_t(3) * inner, false, base + kQkvB, 0.f, kStd);
+        fill(b.qn, 128, false, base + kQn, 1.f, kStd);
+        fill(b.kn, 128, false, base + kKn, 1.f, kStd);
+        fill(b.out_w, size_t(d) * inner, true, base + kOutW, 0.f, kStd);
+        fill(b.out_b, d, false, base + kOutB, 0.f, kStd);
+        fill(b.norm2, d, false, base + kNorm2, 1.f, kStd);
+        DevBuf w, bias;
+        fill(w, size_t(2) * F * d, true, base + kFc1W, 0.f, kStd);
+        fill(bias, size_t(2) * F, false, base + kFc1B, 0.f, kStd);
+        b.fc1_w.ensure(size_t(2) * F * d * 2);
+        b.fc1_b.ensure(size_t(2) * F * 4);
+        interleave_gate_value(w.p, F, d, b.fc1_w.p, s);
+        interleave_gate_value_f32(bias.as<float>(), F, b.fc1_b.as<float>(), s);
+        H3_CUDA(cudaStreamSynchronize(s));
+        fill(b.fc2_w, size_t(d) * F, true, base + kFc2W, 0.f, kStd);
+        fill(b.fc2_b, d, false, base + kFc2B, 0.f, kStd);
+    }
+    if (c.refiner > 0)
+        fill(d_->refiner_norm, d, false, kRefinerNorm, 1.f, kStd);
     H3_CUDA(cudaStreamSynchronize(s));
     if (take_device_error(s))
         throw CudaError("device error during weight set-up");
@@ -528,7 +559,9 @@ void Model::begin(const float* text, int T, const Layout& l)
         g.M = T, g.N = d, g.K = c_.text_dim;
         g.out = d_->x_text.p, g.ldo = d, g.bias = d_->cond_b.as<float>();
         gemm_bf16(tpk.p, d_->cond_w.p, g, Epi::f32, s);
+        refine_text(T);
         H3_CUDA(cudaStreamSynchronize(s));
+        emit_probe("txt", -1, d_->x_text.as<float>(), size_t(T) * d);
     }
     // the packed row order: generated video rows cube by cube
     CubeGrid& g = d_->grid;
@@ -601,6 +634,79 @@ void Model::begin(const float* text, int T, const Layout& l)
     }
     H3_CUDA(cudaStreamSynchronize(s));
     begun_ = true;
+}
+
+// The token refiner over the text rows x_text (docs/architecture.md:25-27: "a two-block token refiner (plain pre-norm
+// blocks, no rotary positions), then its final RMS norm"). Each block is the step's block with its modulation
+// replaced by a constant table (shift 0, scale 0, gate 1: plain RMS norms and plain residual adds) and the rotary
+// table by the identity (cos 1, sin 0), so it runs on the step's own kernels: the modulated norm, the q/k/v GEMM with
+// the per-head q/k norms in its epilogue, dense attention over the T text rows (all heads, on every rank: the text is
+// replicated), the out and fc2 GEMMs with the residual add in their epilogues and fc1 with the fused SwiGLU. The final
+// norm is x = RMSNorm(x) * refiner_norm. Always bf16 (the int8 mask is for the step's projections).
+void Model::refine_text(int T)
+{
+    const int R = int(d_->refiner.size());
+    if (R == 0 || T <= 0)
+        return;
+    cudaStream_t s = stream_;
+    const int d = c_.dim, inner = c_.inner(), F = c_.ffn, H = c_.heads;
+    DevBuf h, qkv, o, rope, mod, midx, xn;
+    h.ensure(size_t(T) * d * 2);
+    qkv.ensure(size_t(T) * std::max(3 * inner, F) * 2);
+    o.ensure(size_t(T) * inner * 2);
+    midx.ensure(size_t(T)); // zeros: every row reads modulation 0
+    xn.ensure(size_t(T) * d * 4);
+    {
+        std::vector<float> id(size_t(T) * 96);
+        for (size_t i = 0; i < id.size(); i += 2)
+            id[i] = 1.f, id[i + 1] = 0.f;
+        rope.ensure(id.size() * 4);
+        H3_CUDA(cudaMemcpyAsync(rope.p, id.data(), id.size() * 4, cudaMemcpyHostToDevice, s));
+        std::vector<float> m(size_t(6) * d, 0.f); // shift, scale, gate of attention, then of the FFN
+        std::fill(m.begin() + size_t(2) * d, m.begin() + size_t(3) * d, 1.f);
+        std::fill(m.begin() + size_t(5) * d, m.end(), 1.f);
+        mod.ensure(m.size() * 4);
+        H3_CUDA(cudaMemcpyAsync(mod.p, m.data(), m.size() * 4, cudaMemcpyHostToDevice, s));
+        H3_CUDA(cudaStreamSynchronize(s)); // the host vectors go out of scope
+    }
+    float* x = d_->x_text.as<float>();
+    const uint8_t* mi = midx.as<uint8_t>();
+    for (int r = 0; r < R; ++r) {
+        const Impl::Block& B = d_->refiner[r];
+        RmsModParams rp;
+        rp.x = x, rp.ldx = d, rp.rows = T, rp.d = d, rp.w = B.norm1.as<float>(), rp.mod = mod.as<float>(), rp.mod_idx = mi;
+        rp.mod_slots = 6, rp.shift_slot = 0, rp.scale_slot = 1, rp.eps = c_.eps, rp.out_kind = RowOut::bf16, rp.out = h.p, rp.ldo = d;
+        rms_mod_rows(rp, s);
+        GemmParams gq;
+        gq.M = T, gq.N = 3 * inner, gq.K = d;
+        gq.out = qkv.p, gq.bias = B.qkv_b.as<float>(), gq.rope = rope.as<float>(), gq.qn_w = B.qn.as<float>(), gq.kn_w = B.kn.as<float>();
+        gq.eps = c_.eps, gq.inner = inner, gq.heads_per_rank = H, gq.rows_local = T;
+        gemm_bf16(h.p, B.qkv_w.p, gq, Epi::qkv, s);
+        const __nv_bfloat16* q = qkv.as<__nv_bfloat16>();
+        AttnParams ap;
+        ap.q = q, ap.k = q + H * 128, ap.v = q + 2 * H * 128, ap.row_stride = 3 * H * 128, ap.heads = H, ap.rows = T;
+        ap.out = o.p, ap.out_row_stride = inner;
+        attention(ap, s);
+        GemmParams go;
+        go.M = T, go.N = d, go.K = inner;
+        go.x = x, go.ldx = d, go.bias = B.out_b.as<float>(), go.mod = mod.as<float>(), go.mod_idx = mi, go.gate_slot = 2, go.dim = d;
+        gemm_bf16(o.p, B.out_w.p, go, Epi::gate_resid, s);
+        rp.w = B.norm2.as<float>(), rp.shift_slot = 3, rp.scale_slot = 4;
+        rms_mod_rows(rp, s);
+        GemmParams g1;
+        g1.M = T, g1.N = 2 * F, g1.K = d, g1.out = qkv.p, g1.ldo = F, g1.bias = B.fc1_b.as<float>();
+        gemm_bf16(h.p, B.fc1_w.p, g1, Epi::swiglu, s);
+        GemmParams g2;
+        g2.M = T, g2.N = d, g2.K = F;
+        g2.x = x, g2.ldx = d, g2.bias = B.fc2_b.as<float>(), g2.mod = mod.as<float>(), g2.mod_idx = mi, g2.gate_slot = 5, g2.dim = d;
+        gemm_bf16(qkv.p, B.fc2_w.p, g2, Epi::gate_resid, s);
+    }
+    RmsModParams fp;
+    fp.x = x, fp.ldx = d, fp.rows = T, fp.d = d, fp.w = d_->refiner_norm.as<float>(), fp.mod = mod.as<float>(), fp.mod_idx = mi;
+    fp.mod_slots = 6, fp.shift_slot = 0, fp.scale_slot = 1, fp.eps = c_.eps, fp.out_kind = RowOut::f32, fp.out = xn.p, fp.ldo = d;
+    rms_mod_rows(fp, s);
+    H3_CUDA(cudaMemcpyAsync(x, xn.p, size_t(T) * d * 4, cudaMemcpyDeviceToDevice, s));
+    H3_CUDA(cudaStreamSynchronize(s)); // the temporaries are freed on return
 }
 
 void Model::emit_probe(const char* name, int layer, const float* dev, size_t n, bool rows)

@@ -18,6 +18,7 @@ struct Config {
     int dim = 5120, heads = 40, ffn = 13824, blocks = 48, time_dim = 2560;
     int text_dim = 5120, video_patch = 96, audio_channels = 32;
     float eps = 1e-6f;
+    int refiner = 2; // token refiner blocks over the text rows (begin); 0 skips the refiner
     int inner() const { return heads * 128; }
 };
 
@@ -111,7 +112,8 @@ public:
 
     void set_sparse(float ratio, int local);
     void set_probe(Probe p) { probe_ = std::move(p); }
-    // Caches the text rows (condition_proj of the text embeddings [T][text_dim]) and the layout's row tables.
+    // Caches the text rows (condition_proj of the text embeddings [T][text_dim], then the token refiner) and the
+    // layout's row tables.
     void begin(const float* text, int T, const Layout& l);
     // One forward: video [V][96] and audio [A][32] rows (host or device memory) to velocities of the same shapes.
     // With `device_io` the pointers are device pointers and the step stays on `stream` (no host synchronisation
@@ -132,8 +134,9 @@ public:
     // adaln_proj.linear; X.lora_A.weight [r][in], X.lora_B.weight [out][r]; alpha from X.alpha or the file's
     // "alpha" metadata, else r) merged as W += scale * alpha / r * B A into the bf16 matrices, or into the int8 rows
     // by requantizing them. Diffusers orders fc1 [value; gate] (this build [gate; value]) and the AdaLN rows
-    // (chunk, modality) (this build (modality, chunk)); the adapter's rows are permuted to match. Targets this build
-    // does not have (the token refiner's) are skipped and counted; with `strict`, any other unknown name is an error.
+    // (chunk, modality) (this build (modality, chunk)); the adapter's rows are permuted to match. The token refiner's
+    // targets (its Diffusers module names are not documented in the reference) are skipped and counted; with
+    // `strict`, any other unknown name is an error.
     struct LoraResult {
         int merged = 0, skipped = 0, rank = 0;
     };
@@ -166,6 +169,7 @@ private:
     std::vector<std::pair<std::string, float>> stage_ms_;
     bool begun_ = false;
     void alloc_activations();
+    void refine_text(int T); // the token refiner over x_text (begin)
     void map_peers(); // the ranks' receive buffers, mapped into every rank (sequence-parallel, fused exchange)
     // Copies a device tensor to the host and hands it to the probe; with `rows` set it is [S][n / S] in the packed row
     // order and is handed over in the layout's row order.

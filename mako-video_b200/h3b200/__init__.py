@@ -20,11 +20,11 @@ INT8_QKV, INT8_OUT, INT8_FC1, INT8_FC2 = 1, 2, 4, 8
 # Model shapes (h3_config): the benchmark's synthetic stacks and the real MiniMax-H3.
 CONFIGS = {
     # one tiny block
-    "c1": dict(dim=1024, heads=8, ffn=2816, blocks=1, time_dim=512, text_dim=5120),
+    "c1": dict(dim=1024, heads=8, ffn=2816, blocks=1, time_dim=512, text_dim=5120, refiner=2),
     # the 768p stack
-    "c2": dict(dim=5120, heads=40, ffn=13824, blocks=48, time_dim=2560, text_dim=5120),
+    "c2": dict(dim=5120, heads=40, ffn=13824, blocks=48, time_dim=2560, text_dim=5120, refiner=2),
     # MiniMax-H3 itself (docs/architecture.md:23-27, 47-67 of the reference)
-    "h3": dict(dim=5376, heads=56, ffn=14336, blocks=50, time_dim=2688, text_dim=5120),
+    "h3": dict(dim=5376, heads=56, ffn=14336, blocks=50, time_dim=2688, text_dim=5120, refiner=2),
 }
 
 # Layouts (h3_layout): latent h / w are twice the patch grid.
@@ -47,7 +47,7 @@ class H3Error(RuntimeError):
 class h3_config(ctypes.Structure):
     _fields_ = [("dim", ctypes.c_uint32), ("heads", ctypes.c_uint32), ("ffn", ctypes.c_uint32), ("blocks", ctypes.c_uint32),
                 ("time_dim", ctypes.c_uint32), ("text_dim", ctypes.c_uint32), ("video_patch", ctypes.c_uint32),
-                ("audio_channels", ctypes.c_uint32), ("eps", ctypes.c_float)]
+                ("audio_channels", ctypes.c_uint32), ("eps", ctypes.c_float), ("refiner_blocks", ctypes.c_uint32)]
 
 
 class h3_layout_ref(ctypes.Structure):
@@ -158,7 +158,8 @@ def check(rc):
 
 def make_config(name_or_dict, eps=1e-6):
     c = CONFIGS[name_or_dict] if isinstance(name_or_dict, str) else name_or_dict
-    return h3_config(c["dim"], c["heads"], c["ffn"], c["blocks"], c["time_dim"], c.get("text_dim", 5120), 96, 32, eps)
+    return h3_config(c["dim"], c["heads"], c["ffn"], c["blocks"], c["time_dim"], c.get("text_dim", 5120), 96, 32, eps,
+                     c.get("refiner", 0))
 
 
 class Layout:

@@ -80,7 +80,9 @@ def synthetic(n, seed, tensor_id, mean=0.0, stdev=0.02, bf16=False):
 
 # tensor ids, as the library assigns them
 T_IN_W, T_IN_B, T_OUT_W, T_OUT_B, VP_W, VP_B, AP_W, AP_B, COND_W, COND_B, FADA_W, FADA_B, HV_W, HV_B, HA_W, HA_B = range(1, 17)
+REFINER_NORM = 17
 BLOCK_BASE, BLOCK_STRIDE = 100, 20
+REFINER_BASE = 60  # token refiner block r at REFINER_BASE + BLOCK_STRIDE * r (r < 2), the block sub-ids without ADA_*
 ADA_W, ADA_B, NORM1, QKV_W, QKV_B, QN, KN, OUT_W, OUT_B, NORM2, FC1_W, FC1_B, FC2_W, FC2_B = range(14)
 
 
@@ -101,10 +103,8 @@ def make_weights(cfg, seed, blocks=None):
         "ha_w": t(32 * d, HA_W, (32, d)), "ha_b": t(32, HA_B, (32,)),
         "blocks": [],
     }
-    for l in range(L):
-        b = BLOCK_BASE + BLOCK_STRIDE * l
-        w["blocks"].append({
-            "ada_w": t(18 * d * td, b + ADA_W, (18 * d, td), bf16=True), "ada_b": t(18 * d, b + ADA_B, (18 * d,)),
+    def block(b):
+        return {
             "norm1": t(d, b + NORM1, (d,), mean=1.0),
             "qkv_w": t(3 * inner * d, b + QKV_W, (3 * inner, d), bf16=True), "qkv_b": t(3 * inner, b + QKV_B, (3 * inner,)),
             "qn": t(128, b + QN, (128,), mean=1.0), "kn": t(128, b + KN, (128,), mean=1.0),
@@ -112,7 +112,15 @@ def make_weights(cfg, seed, blocks=None):
             "norm2": t(d, b + NORM2, (d,), mean=1.0),
             "fc1_w": t(2 * F * d, b + FC1_W, (2 * F, d), bf16=True), "fc1_b": t(2 * F, b + FC1_B, (2 * F,)),
             "fc2_w": t(d * F, b + FC2_W, (d, F), bf16=True), "fc2_b": t(d, b + FC2_B, (d,)),
-        })
+        }
+
+    for l in range(L):
+        b = BLOCK_BASE + BLOCK_STRIDE * l
+        w["blocks"].append(dict(block(b), ada_w=t(18 * d * td, b + ADA_W, (18 * d, td), bf16=True),
+                                ada_b=t(18 * d, b + ADA_B, (18 * d,))))
+    w["refiner"] = [block(REFINER_BASE + BLOCK_STRIDE * r) for r in range(cfg.get("refiner", 0))]
+    if w["refiner"]:
+        w["refiner_norm"] = t(d, REFINER_NORM, (d,), mean=1.0)
     return w
 
 
@@ -264,13 +272,38 @@ def bf(t):
     return torch.from_numpy(bf16_round(t.numpy()))
 
 
+def refine(cfg, w, x, R, eps):
+    """The token refiner over the text rows after condition_proj (architecture.md:25-27: "a two-block token refiner
+    (plain pre-norm blocks, no rotary positions), then its final RMS norm"): per block x += attn(norm1(x)),
+    x += swiglu_ffn(norm2(x)), with the step's widths, per-head q/k RMS norms, no modulation (no gates) and no rotary
+    positions; then x = RMSNorm(x) * refiner_norm. The block internals beyond that sentence are this build's choice
+    (the refiner's code is not in the reference tree)."""
+    if not w.get("refiner"):
+        return x
+    H, F = cfg["heads"], cfg["ffn"]
+    T = x.shape[0]
+    for B in w["refiner"]:
+        h = rms(x, eps) * B["norm1"]
+        qkv = (R(h) @ B["qkv_w"].T + B["qkv_b"]).reshape(T, 3, H, 128)
+        q = R(rms(qkv[:, 0], eps) * B["qn"])
+        k = R(rms(qkv[:, 1], eps) * B["kn"])
+        v = R(qkv[:, 2])
+        o = attention(q, k, v).reshape(T, H * 128)
+        x = x + (R(o) @ B["out_w"].T + B["out_b"])
+        h = rms(x, eps) * B["norm2"]
+        gv = R(h) @ B["fc1_w"].T + B["fc1_b"]
+        a = torch.nn.functional.silu(gv[:, :F]) * gv[:, F:]
+        x = x + (R(a) @ B["fc2_w"].T + B["fc2_b"])
+    return rms(x, eps) * w["refiner_norm"]
+
+
 def step(cfg, w, L, text, video, audio, t_video, t_audio, allowed_fn=None, int8=0, probes=None, eps=1e-6,
          round_activations=False):
     """One forward: velocities for every video row [V][96] (conditioning rows first) and audio row [A][32] (reference
     soundtrack rows first), in the inputs' row order.
     allowed_fn(block, q, k) -> [H][S][S] bool restricts attention (sparse); int8 a mask (1 qkv, 2 out, 4 fc1, 8 fc2)
-    switching those projections to the int8 dequant path; probes(name, layer, array) sees temb, mod0, x0, block l and
-    norm_out. round_activations rounds every GEMM and attention input to bf16 as the GPU path does."""
+    switching those projections to the int8 dequant path; probes(name, layer, array) sees txt (the text rows after the
+    token refiner), temb, mod0, x0, block l and norm_out. round_activations rounds every GEMM and attention input to bf16 as the GPU path does."""
     d, H, F = cfg["dim"], cfg["heads"], cfg["ffn"]
     T = L["text"]
     pos, tags, roles = layout_rows(L)
@@ -305,7 +338,10 @@ def step(cfg, w, L, text, video, audio, t_video, t_audio, allowed_fn=None, int8=
     # packed input
     x = torch.zeros(S, d)
     if T:
-        x[:T] = bf(torch.from_numpy(np.asarray(text, np.float32))) @ w["cond_w"].T + w["cond_b"]
+        xt = refine(cfg, w, bf(torch.from_numpy(np.asarray(text, np.float32))) @ w["cond_w"].T + w["cond_b"], R, eps)
+        x[:T] = xt
+        if probes:
+            probes("txt", -1, xt.numpy().copy())
     vin = torch.from_numpy(np.asarray(video, np.float32).reshape(V, 96))
     ain = torch.from_numpy(np.asarray(audio, np.float32).reshape(A, 32))
     vi, ai = torch.from_numpy(video_rows), torch.from_numpy(audio_rows)

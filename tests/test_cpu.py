@@ -305,3 +305,21 @@ def test_create_refuses_checkpoint_paths_without_touching_the_gpu():
     rc = L.h3_create(ctypes.byref(cfg), b"/models/minimax-h3/FL2VA/transformer", 0, 0.0, 1, None, 0, ctypes.byref(h))
     assert rc == h3b200.H3_ERR_ARG and not h.value
     assert b"synthetic" in L.h3_last_error()
+
+
+def test_oracle_token_refiner_ends_in_its_weighted_rms_norm():
+    """The oracle's token refiner (architecture.md:25-27): refiner blocks change the text rows, and the output is
+    RMSNorm(x) * refiner_norm, so every row divided by the weight has unit RMS; without refiner blocks the rows pass
+    unchanged."""
+    import torch
+
+    cfg = dict(dim=256, heads=2, ffn=512, blocks=0, time_dim=128, text_dim=256, refiner=2)
+    w = O.make_weights(cfg, 5)
+    assert len(w["refiner"]) == 2 and w["refiner_norm"].shape == (256,)
+    x = torch.from_numpy(O.synthetic(7 * 256, 5, 9, 0.0, 1.0).reshape(7, 256))
+    y = O.refine(cfg, w, x, lambda t: t, 1e-6)
+    r = (y / w["refiner_norm"]).pow(2).mean(-1).sqrt()
+    np.testing.assert_allclose(r.numpy(), 1.0, rtol=1e-4)
+    assert not torch.allclose(y, O.rms(x, 1e-6) * w["refiner_norm"], atol=1e-3)  # the blocks did something
+    w0 = O.make_weights(dict(cfg, refiner=0), 5)
+    assert O.refine(cfg, w0, x, lambda t: t, 1e-6) is x

@@ -1,6 +1,7 @@
 """The whole step through the C ABI (h3_create / h3_begin / h3_step) against the CPU oracle on the same synthetic
 weights and inputs, probe by probe as the reference's harness compares the Diffusers tensors
-(tests/h3_ref_test.cpp:214-250): time embedding, block-0 modulation, packed input, blocks, final norm, velocities."""
+(tests/h3_ref_test.cpp:214-250): the text after the token refiner, time embedding, block-0 modulation, packed input,
+blocks, final norm, velocities."""
 import numpy as np
 import pytest
 
@@ -9,8 +10,8 @@ from oracle import h3_oracle as O
 
 pytestmark = pytest.mark.gpu
 
-# tests/h3_ref_test.cpp:228-249
-TOL = {"temb": 1e-4, "mod0": 5e-3, "x0": 5e-3, "block": 1e-2, "norm_out": 6e-2}
+# tests/h3_ref_test.cpp:219, 228-249
+TOL = {"txt": 5e-3, "temb": 1e-4, "mod0": 5e-3, "x0": 5e-3, "block": 1e-2, "norm_out": 6e-2}
 # north star: bf16 path vs the fp32 oracle
 VEL_REL, VEL_COS = 1e-2, 0.999
 
@@ -59,7 +60,7 @@ def test_step_c1_matches_oracle(cuda):
     assert launches > 5
 
 
-MINI = dict(dim=512, heads=4, ffn=1280, blocks=3, time_dim=256, text_dim=512)
+MINI = dict(dim=512, heads=4, ffn=1280, blocks=3, time_dim=256, text_dim=512, refiner=2)
 MINI_LAYOUT = dict(text=40, frames=6, h=12, w=14, audio=24, cond_frames=1, cond_last=[1])
 
 
@@ -193,7 +194,7 @@ def test_denoise_progress_reports_and_cancels(cuda):
     np.testing.assert_array_equal(ga, ha)
 
 
-EDGE = dict(dim=256, heads=2, ffn=512, blocks=2, time_dim=128, text_dim=256)
+EDGE = dict(dim=256, heads=2, ffn=512, blocks=2, time_dim=128, text_dim=256, refiner=1)
 
 
 @pytest.mark.parametrize("layout", [
