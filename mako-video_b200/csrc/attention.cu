@@ -399,8 +399,10 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
     uint64_t* v_full = k_empty + A3_KST;           // [A3_VST]
     uint64_t* v_empty = v_full + A3_VST;           // [A3_VST]
     uint64_t* s_full = v_empty + A3_VST;           // [2] per S buffer
-    uint64_t* p_full = s_full + 2;
-    uint64_t* pv_done = p_full + 1;
+    // p_full per S buffer too: the softmax may finish steps j and j + 1 before the MMA warp waits for P(j), and a
+    // single barrier would then be two phases ahead of that wait; step j + 2 needs S(j + 2), issued after PV(j).
+    uint64_t* p_full = s_full + 2;                 // [2] per S buffer
+    uint64_t* pv_done = p_full + 2;
     uint64_t* xchg = pv_done + 1;
     uint64_t* drain = xchg + 1;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -438,7 +440,8 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
         }
         mbar_init(&s_full[0], 1);
         mbar_init(&s_full[1], 1);
-        mbar_init(p_full, 8);
+        mbar_init(&p_full[0], 8);
+        mbar_init(&p_full[1], 8);
         mbar_init(pv_done, 1);
         mbar_init(xchg, 8);
         mbar_init(drain, 1);
@@ -516,7 +519,7 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
         for (int j = 0; j < 2 && j < nkv && ok; ++j)
             ok = issue_s(j);
         for (int j = 0; j < nkv && ok; ++j) {
-            if (!(ok = mbar_wait(p_full, j & 1)))
+            if (!(ok = mbar_wait(&p_full[j & 1], (j >> 1) & 1)))
                 break;
             for (int x = 0; x < 2 && ok; ++x) {
                 const int i = 2 * j + x, sv = i % A3_VST;
@@ -655,7 +658,7 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
             tc_fence_before();
             __syncwarp();
             if (elect_one_lane())
-                mbar_arrive(p_full);
+                mbar_arrive(&p_full[j & 1]);
         }
         if (ok) {
             float* slot = red + 2 * 256;
@@ -666,7 +669,9 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
             ok = mbar_wait(xchg, nkv & 1);
             l = slot[row] + slot[128 + row];
         }
-        if (ok && mbar_wait(pv_done, (nkv - 1) & 1)) {
+        // The last two PVs may both be pending here (S(j) completing implies only PV(j - 2) did), which a parity wait
+        // on pv_done cannot tell apart; drain completes once, after every MMA of the CTA.
+        if (ok && mbar_wait(drain, 0)) {
             tc_fence_after();
             const int first = x ? qr.y : qr.x, nq = x ? qr.w : qr.z;
             const int out_row = first >= 0 && m < nq ? first + m : -1;
