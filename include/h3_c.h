@@ -37,6 +37,11 @@ typedef struct h3_config {
     uint32_t refiner_blocks; /* token refiner blocks run over the text rows in h3_begin (MiniMax-H3: 2; 0: none, at most
                               * 2). Plain pre-norm blocks of the step's widths without modulation or rotary positions,
                               * then a weighted RMS norm (docs/architecture.md:25-27). */
+    uint32_t curve_dims;     /* 0: the full model (time embedder, SiLU, [18 dim][time_dim] AdaLN projections). 8: a pruned
+                              * checkpoint (docs/architecture.md:57-60): no time embedder; a level t reads the curve
+                              * adaln_t_table [1025][8] at t * 1024 with linear interpolation, and every block's AdaLN
+                              * projection is [18 dim][8] (the final layer's [2 dim][8]) applied in fp32 without SiLU
+                              * (curve_mods; tools/check_pruned_curve.py:43-70). */
 } h3_config;
 
 /* A reference block of a ref2va layout (H3::Layout::Reference, src/video/engine.cpp:604-616;
@@ -71,8 +76,8 @@ typedef struct h3_world {
 } h3_world;
 
 /* Probe callback (H3::set_probe, tests/h3_ref_test.cpp:215-217): name is one of txt (the text rows after the token
- * refiner, from h3_begin; tests/h3_ref_test.cpp:219), temb, mod0, x0, block, norm_out; layer is the block for "block"
- * and -1 otherwise; data is host memory valid during the call. Single-rank only. */
+ * refiner, from h3_begin; tests/h3_ref_test.cpp:219), temb (not for a pruned checkpoint, which has no time embedder),
+ * mod0, x0, block, norm_out; layer is the block for "block" and -1 otherwise; data is host memory valid during the call. Single-rank only. */
 typedef void (*h3_probe_fn)(void* user, const char* name, int32_t layer, const float* data, uint64_t n);
 
 /* The message of the last failed call on this thread ("" if none). */

@@ -101,7 +101,7 @@ public:
     H3& operator=(const H3&) = delete;
 
     // MiniMax-H3's shape.
-    static h3_config h3_mini_h3() { return h3_config{kDim, 56, 14336, 50, kTimeDim, kText, kVideoPatch, kAudioChannels, 1e-6f, 2}; }
+    static h3_config h3_mini_h3() { return h3_config{kDim, 56, 14336, 50, kTimeDim, kText, kVideoPatch, kAudioChannels, 1e-6f, 2, 0}; }
 
     // set_sparse(ratio, local) (src/video/engine.cpp:112).
     void set_sparse(float ratio, uint32_t local) { check(h3_set_sparse(m_, ratio, local)); }
@@ -157,7 +157,8 @@ public:
         return out;
     }
 
-    // set_probe (tests/h3_ref_test.cpp:215-217): temb, mod0, x0, block (layer), norm_out.
+    // set_probe (tests/h3_ref_test.cpp:215-217): txt (from begin: the text after the token refiner), temb (not for a
+    // pruned checkpoint), mod0, x0, block (layer), norm_out.
     void set_probe(ProbeFn fn)
     {
         probe_ = std::move(fn);

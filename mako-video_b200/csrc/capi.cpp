@@ -202,6 +202,9 @@ int h3_create(const h3_config* cfg, const char* weights, uint32_t int8_mask, flo
             throw ArgError("h3_create: video_patch must be 96 and audio_channels 32");
         if (cfg->refiner_blocks > 2)
             throw ArgError("h3_create: at most 2 token refiner blocks (MiniMax-H3 has 2)");
+        if (cfg->curve_dims != 0 && cfg->curve_dims != 8)
+            throw ArgError("h3_create: curve_dims is 0 (full model) or 8 (pruned checkpoint)");
+        c.curve = int(cfg->curve_dims);
         h3::World wd;
         if (world) {
             wd.rank = world->rank, wd.size = world->size;

@@ -1,4 +1,4 @@
-// Time-embedding MLP, AdaLN projections and the fp32 heads.
+// Time-embedding MLP, AdaLN projections (full and pruned-curve) and the fp32 heads.
 #include "common.hpp"
 #include "embed.cuh"
 #include "ptx.cuh"
@@ -46,6 +46,38 @@ __global__ void gemv_f32_kernel(const float* W, const float* b, const float* x, 
                 if (out2)
                     out2[size_t(u) * N + n] = __bfloat162float(__float2bfloat16_rn(silu(v)));
             }
+        }
+    }
+}
+
+// Pruned checkpoints: one thread per projection row (K fp32 weights, a 32-byte row at K = 8, so a warp reads 1 KB of
+// consecutive rows), all U curve points from shared memory; an fmaf chain over k from the bias.
+constexpr int CM_MAXK = 16;
+
+__global__ void __launch_bounds__(256) curve_mods_kernel(const float* W, const float* b, const float* c, int U, size_t rows, int G, int K,
+                                                         float* out)
+{
+    __shared__ float cs[MAXU * CM_MAXK];
+    for (int i = threadIdx.x; i < U * K; i += blockDim.x)
+        cs[i] = c[i];
+    __syncthreads();
+    for (size_t r = size_t(blockIdx.x) * blockDim.x + threadIdx.x; r < rows; r += size_t(gridDim.x) * blockDim.x) {
+        float w[CM_MAXK];
+#pragma unroll
+        for (int k = 0; k < CM_MAXK; ++k)
+            w[k] = k < K ? __ldg(W + r * K + k) : 0.f;
+        const float bias = __ldg(b + r);
+        const size_t g = r / G, j = r - g * G;
+#pragma unroll
+        for (int u = 0; u < MAXU; ++u) {
+            if (u >= U)
+                break;
+            float acc = bias;
+#pragma unroll
+            for (int k = 0; k < CM_MAXK; ++k)
+                if (k < K)
+                    acc = fmaf(w[k], cs[u * K + k], acc);
+            out[(g * U + u) * G + j] = acc;
         }
     }
 }
@@ -196,6 +228,18 @@ void adaln_gemv(const void* W, const float* b, const float* x, int U, int groups
     const size_t rows = size_t(groups) * G;
     const int grid = int(std::min<size_t>((rows + 7) / 8, size_t(num_sms()) * 8));
     adaln_kernel<<<grid, 256, smem, s>>>(static_cast<const __nv_bfloat16*>(W), b, x, U, groups, G, K, out);
+    H3_CUDA(cudaGetLastError());
+}
+
+void curve_mods(const float* W, const float* b, const float* c, int U, int groups, int G, int K, float* out, cudaStream_t s)
+{
+    if (U < 1 || U > MAXU || K < 1 || K > CM_MAXK)
+        throw CudaError("curve_mods: 1 to 4 curve points of at most 16 coordinates");
+    const size_t rows = size_t(groups) * G;
+    if (!rows)
+        return;
+    const int grid = int(std::min<size_t>((rows + 255) / 256, size_t(num_sms()) * 8));
+    curve_mods_kernel<<<grid, 256, 0, s>>>(W, b, c, U, rows, G, K, out);
     H3_CUDA(cudaGetLastError());
 }
 

@@ -17,6 +17,10 @@ void gemv_f32(const float* W, const float* b, const float* x, int U, int N, int 
 // out[(g * U + u) * G + j] = sum_k W[g * G + j][k] * x[u][k] + b[g * G + j].
 void adaln_gemv(const void* W_bf16, const float* b, const float* x, int U, int groups, int G, int K, float* out, cudaStream_t s);
 
+// Pruned checkpoints' AdaLN projections (curve_mods): for each group g of G weight rows (fp32 [groups * G][K], K <= 16),
+// out[(g * U + u) * G + j] = sum_k W[g * G + j][k] * c[u][k] + b[g * G + j], c the curve points [U][K].
+void curve_mods(const float* W, const float* b, const float* c, int U, int groups, int G, int K, float* out, cudaStream_t s);
+
 // out[r * ldo + j] = sum_k x[r][k] * W[j][k] + b[j]  (fp32; N <= 128, K a multiple of 32)
 void heads_f32(const float* x, int64_t ldx, int rows, const float* W, const float* b, int N, int K, float* out, int64_t ldo,
                cudaStream_t s);

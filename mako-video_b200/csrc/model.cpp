@@ -233,13 +233,14 @@ struct DevBuf {
 // Synthetic tensor ids (fixed: the CPU oracle regenerates the same values from them).
 enum : uint32_t {
     kTInW = 1, kTInB, kTOutW, kTOutB, kVpW, kVpB, kApW, kApB, kCondW, kCondB, kFadaW, kFadaB, kHvW, kHvB, kHaW, kHaB,
-    kRefinerNorm = 17,
+    kRefinerNorm = 17, kCurveTable = 18,
     kBlockBase = 100, kBlockStride = 20,
     kRefinerBase = 60, // token refiner block r (r < 2) at kRefinerBase + kBlockStride * r, without the AdaLN ids
 };
 enum : uint32_t { kAdaW = 0, kAdaB, kNorm1, kQkvW, kQkvB, kQn, kKn, kOutW, kOutB, kNorm2, kFc1W, kFc1B, kFc2W, kFc2B };
 
 constexpr float kStd = 0.02f;
+constexpr float kCurveStd = 4.0f; // synthetic adaln_t_table values: modulations of the same size as the full model's
 
 } // namespace
 
@@ -247,8 +248,9 @@ struct Model::Impl {
     // weights
     DevBuf t_in_w, t_in_b, t_out_w, t_out_b;
     DevBuf vp_w, vp_b, ap_w, ap_b, cond_w, cond_b;
-    DevBuf ada_w, ada_b;   // all blocks: [L][18 d][t_dim] bf16, [L][18 d] f32
-    DevBuf fada_w, fada_b; // [2 d][t_dim], [2 d]
+    DevBuf ada_w, ada_b;   // all blocks: [L][18 d][t_dim] bf16 ([L][18 d][8] f32 for a pruned checkpoint), [L][18 d] f32
+    DevBuf fada_w, fada_b; // [2 d][t_dim] bf16 ([2 d][8] f32 pruned), [2 d]
+    std::vector<float> curve_table; // pruned checkpoint: adaln_t_table [1025][8] (host copy; read per step)
     DevBuf hv_w, hv_b, ha_w, ha_b;
     struct Block {
         DevBuf norm1, qkv_w, qkv_b, qn, kn, out_w, out_b, norm2, fc1_w, fc1_b, fc2_w, fc2_b;
@@ -332,10 +334,23 @@ Model::Model(const Config& c, uint64_t seed, uint32_t int8_mask, const World& wo
         b.ensure(n * (bf16 ? 2 : 4));
         fill_synthetic(b.p, bf16, n, seed, id, mean, stdev, s);
     };
-    fill(d_->t_in_w, size_t(d) * 256, false, kTInW, 0.f, kStd);
-    fill(d_->t_in_b, d, false, kTInB, 0.f, kStd);
-    fill(d_->t_out_w, size_t(td) * d, false, kTOutW, 0.f, kStd);
-    fill(d_->t_out_b, td, false, kTOutB, 0.f, kStd);
+    const bool pruned = c.curve > 0;
+    if (c.curve != 0 && c.curve != 8)
+        throw CudaError("config: curve_dims is 0 or 8");
+    const int ka = pruned ? c.curve : td; // the AdaLN projections' input width
+    if (!pruned) {
+        fill(d_->t_in_w, size_t(d) * 256, false, kTInW, 0.f, kStd);
+        fill(d_->t_in_b, d, false, kTInB, 0.f, kStd);
+        fill(d_->t_out_w, size_t(td) * d, false, kTOutW, 0.f, kStd);
+        fill(d_->t_out_b, td, false, kTOutB, 0.f, kStd);
+    } else {
+        // adaln_t_table [1025][8]: generated on the device like every weight, kept on the host for the per-step lookup
+        DevBuf tab;
+        fill(tab, size_t(1025) * c.curve, false, kCurveTable, 0.f, kCurveStd);
+        d_->curve_table.resize(size_t(1025) * c.curve);
+        H3_CUDA(cudaMemcpyAsync(d_->curve_table.data(), tab.p, d_->curve_table.size() * 4, cudaMemcpyDeviceToHost, s));
+        H3_CUDA(cudaStreamSynchronize(s));
+    }
     fill(d_->vp_w, size_t(d) * c.video_patch, true, kVpW, 0.f, kStd);
     fill(d_->vp_b, d, false, kVpB, 0.f, kStd);
     fill(d_->ap_w, size_t(d) * 64, true, kApW, 0.f, 0.f); // padded to 64 inputs; the first 32 columns filled below
@@ -348,19 +363,20 @@ Model::Model(const Config& c, uint64_t seed, uint32_t int8_mask, const World& wo
     fill(d_->ap_b, d, false, kApB, 0.f, kStd);
     fill(d_->cond_w, size_t(d) * c.text_dim, true, kCondW, 0.f, kStd);
     fill(d_->cond_b, d, false, kCondB, 0.f, kStd);
-    fill(d_->fada_w, size_t(2) * d * td, true, kFadaW, 0.f, kStd);
+    fill(d_->fada_w, size_t(2) * d * ka, !pruned, kFadaW, 0.f, kStd);
     fill(d_->fada_b, size_t(2) * d, false, kFadaB, 0.f, kStd);
     fill(d_->hv_w, size_t(c.video_patch) * d, false, kHvW, 0.f, kStd);
     fill(d_->hv_b, c.video_patch, false, kHvB, 0.f, kStd);
     fill(d_->ha_w, size_t(c.audio_channels) * d, false, kHaW, 0.f, kStd);
     fill(d_->ha_b, c.audio_channels, false, kHaB, 0.f, kStd);
     // AdaLN projections of every block in one tensor (one GEMV reads them all): block l at offset l * 18 d * td.
-    d_->ada_w.ensure(size_t(L) * 18 * d * td * 2);
+    d_->ada_w.ensure(size_t(L) * 18 * d * ka * (pruned ? 4 : 2));
     d_->ada_b.ensure(size_t(L) * 18 * d * 4);
     d_->blocks.resize(L);
     for (int l = 0; l < L; ++l) {
         const uint32_t base = kBlockBase + kBlockStride * l;
-        fill_synthetic(d_->ada_w.as<uint8_t>() + size_t(l) * 18 * d * td * 2, 1, size_t(18) * d * td, seed, base + kAdaW, 0.f, kStd, s);
+        fill_synthetic(d_->ada_w.as<uint8_t>() + size_t(l) * 18 * d * ka * (pruned ? 4 : 2), !pruned, size_t(18) * d * ka, seed, base + kAdaW,
+                       0.f, kStd, s);
         fill_synthetic(d_->ada_b.as<float>() + size_t(l) * 18 * d, 0, size_t(18) * d, seed, base + kAdaB, 0.f, kStd, s);
         Impl::Block& b = d_->blocks[l];
         fill(b.norm1, d, false, base + kNorm1, 1.f, kStd);
@@ -783,16 +799,32 @@ void Model::step(const float* video, const float* audio, float t_video, float t_
         }
         H3_CUDA(cudaMemcpyAsync(d_->mod_idx.p, midx, M, cudaMemcpyHostToDevice, s));
         H3_CUDA(cudaMemcpyAsync(d_->lvl_idx.p, lidx, M, cudaMemcpyHostToDevice, s));
-        // sinusoidal embeddings [U][256]: cos half first, freq_i = exp(-ln(10000) * i / 128)
-        for (int u = 0; u < U; ++u)
-            for (int i = 0; i < 128; ++i) {
-                const float fr = float(std::exp(-std::log(10000.0) * i / 128.0));
-                const float a = levels[u] * fr;
-                emb[u * 256 + i] = float(std::cos(double(a)));
-                emb[u * 256 + 128 + i] = float(std::sin(double(a)));
+        if (c_.curve) {
+            // pruned checkpoint: the curve adaln_t_table [1025][8] read at t * 1024 with linear interpolation
+            // (tools/check_pruned_curve.py:66-70, the hypothesis the reference implements), [U][8]; in double, rounded
+            // to float at the end (a float position would move the weight by an ulp of t * 1024, ~3e-5 near 341)
+            const int K8 = c_.curve;
+            const float* tab = d_->curve_table.data();
+            for (int u = 0; u < U; ++u) {
+                const double pos = std::min(std::max(double(levels[u]) * 1024.0, 0.0), 1024.0);
+                const int i0 = std::min(int(std::floor(pos)), 1023);
+                const double w = pos - double(i0);
+                for (int k = 0; k < K8; ++k)
+                    emb[u * K8 + k] = float((1.0 - w) * double(tab[i0 * K8 + k]) + w * double(tab[(i0 + 1) * K8 + k]));
             }
-        d_->emb.ensure(size_t(U) * 256 * 4);
-        H3_CUDA(cudaMemcpyAsync(d_->emb.p, emb, size_t(U) * 256 * 4, cudaMemcpyHostToDevice, s));
+        } else {
+            // sinusoidal embeddings [U][256]: cos half first, freq_i = exp(-ln(10000) * i / 128)
+            for (int u = 0; u < U; ++u)
+                for (int i = 0; i < 128; ++i) {
+                    const float fr = float(std::exp(-std::log(10000.0) * i / 128.0));
+                    const float a = levels[u] * fr;
+                    emb[u * 256 + i] = float(std::cos(double(a)));
+                    emb[u * 256 + 128 + i] = float(std::sin(double(a)));
+                }
+        }
+        const size_t emb_bytes = size_t(U) * (c_.curve ? c_.curve : 256) * 4;
+        d_->emb.ensure(emb_bytes);
+        H3_CUDA(cudaMemcpyAsync(d_->emb.p, emb, emb_bytes, cudaMemcpyHostToDevice, s));
         H3_CUDA(cudaEventRecord(d_->upload_done, s));
     }
 
@@ -835,6 +867,13 @@ void Model::step(const float* video, const float* audio, float t_video, float t_
     const size_t block_mods = size_t(U) * 18 * d;
     d_->mods.ensure(size_t(nb) * P * block_mods * 4);
     d_->fmods.ensure(size_t(U) * 2 * d * 4);
+    if (c_.curve) {
+        // pruned checkpoint (curve_mods): every block's [18 d][8] projection of the curve point, fp32, no SiLU; tiny,
+        // so every rank computes all blocks
+        curve_mods(d_->ada_w.as<float>(), d_->ada_b.as<float>(), d_->emb.as<float>(), U, L, 18 * d, c_.curve, d_->mods.as<float>(), s);
+        curve_mods(d_->fada_w.as<float>(), d_->fada_b.as<float>(), d_->emb.as<float>(), U, 1, 2 * d, c_.curve, d_->fmods.as<float>(), s);
+        launches_ += 2;
+    } else {
     gemv_f32(d_->t_in_w.as<float>(), d_->t_in_b.as<float>(), d_->emb.as<float>(), U, d, 256, Act::silu, d_->th.as<float>(), nullptr, s);
     gemv_f32(d_->t_out_w.as<float>(), d_->t_out_b.as<float>(), d_->th.as<float>(), U, td, d, Act::none, d_->temb.as<float>(),
              d_->tsilu.as<float>(), s);
@@ -849,8 +888,10 @@ void Model::step(const float* video, const float* audio, float t_video, float t_
     }
     adaln_gemv(d_->fada_w.p, d_->fada_b.as<float>(), d_->tsilu.as<float>(), U, 1, 2 * d, td, d_->fmods.as<float>(), s);
     launches_ += 4;
+    }
     mark("adaln");
-    emit_probe("temb", -1, d_->temb.as<float>(), size_t(U) * td);
+    if (!c_.curve)
+        emit_probe("temb", -1, d_->temb.as<float>(), size_t(U) * td);
     emit_probe("mod0", -1, d_->mods.as<float>(), size_t(U) * 18 * d);
 
     // ---- packed input x0 for this rank's rows [row0, row0 + M)
@@ -1252,8 +1293,10 @@ Model::LoraResult Model::add_lora(const std::string& path, float scale, bool str
         else if (module == "ff.net.0.proj") kind = kFc1;
         else if (module == "ff.net.2") kind = kFc2;
         else if (module == "adaln_proj.linear") kind = kAda;
-        if (kind == kNone || block < 0 || block >= L) {
-            const bool known = target.rfind("token_refiner", 0) == 0;
+        if (kind == kNone || block < 0 || block >= L || (kind == kAda && c_.curve)) {
+            // Known but not merged: the token refiner's targets, and the AdaLN projections of a pruned checkpoint
+            // (its [18 d][8] projections of the curve are not the full model's [18 d][time_dim] ones the adapter is for).
+            const bool known = target.rfind("token_refiner", 0) == 0 || (kind == kAda && c_.curve && block >= 0 && block < L);
             if (strict && !known)
                 throw CudaError("add_lora: no H3 weight is named " + target);
             ++res.skipped;

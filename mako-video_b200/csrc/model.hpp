@@ -19,6 +19,7 @@ struct Config {
     int text_dim = 5120, video_patch = 96, audio_channels = 32;
     float eps = 1e-6f;
     int refiner = 2; // token refiner blocks over the text rows (begin); 0 skips the refiner
+    int curve = 0;   // 0: full time embedder + AdaLN; 8: pruned checkpoint (adaln_t_table curve, [18 d][8] projections)
     int inner() const { return heads * 128; }
 };
 

@@ -47,7 +47,8 @@ class H3Error(RuntimeError):
 class h3_config(ctypes.Structure):
     _fields_ = [("dim", ctypes.c_uint32), ("heads", ctypes.c_uint32), ("ffn", ctypes.c_uint32), ("blocks", ctypes.c_uint32),
                 ("time_dim", ctypes.c_uint32), ("text_dim", ctypes.c_uint32), ("video_patch", ctypes.c_uint32),
-                ("audio_channels", ctypes.c_uint32), ("eps", ctypes.c_float), ("refiner_blocks", ctypes.c_uint32)]
+                ("audio_channels", ctypes.c_uint32), ("eps", ctypes.c_float), ("refiner_blocks", ctypes.c_uint32),
+                ("curve_dims", ctypes.c_uint32)]
 
 
 class h3_layout_ref(ctypes.Structure):
@@ -159,7 +160,7 @@ def check(rc):
 def make_config(name_or_dict, eps=1e-6):
     c = CONFIGS[name_or_dict] if isinstance(name_or_dict, str) else name_or_dict
     return h3_config(c["dim"], c["heads"], c["ffn"], c["blocks"], c["time_dim"], c.get("text_dim", 5120), 96, 32, eps,
-                     c.get("refiner", 0))
+                     c.get("refiner", 0), c.get("curve", 0))
 
 
 class Layout:

@@ -81,6 +81,8 @@ def synthetic(n, seed, tensor_id, mean=0.0, stdev=0.02, bf16=False):
 # tensor ids, as the library assigns them
 T_IN_W, T_IN_B, T_OUT_W, T_OUT_B, VP_W, VP_B, AP_W, AP_B, COND_W, COND_B, FADA_W, FADA_B, HV_W, HV_B, HA_W, HA_B = range(1, 17)
 REFINER_NORM = 17
+CURVE_TABLE = 18  # pruned checkpoints: adaln_t_table [1025][curve]
+CURVE_STD = 4.0
 BLOCK_BASE, BLOCK_STRIDE = 100, 20
 REFINER_BASE = 60  # token refiner block r at REFINER_BASE + BLOCK_STRIDE * r (r < 2), the block sub-ids without ADA_*
 ADA_W, ADA_B, NORM1, QKV_W, QKV_B, QN, KN, OUT_W, OUT_B, NORM2, FC1_W, FC1_B, FC2_W, FC2_B = range(14)
@@ -92,17 +94,22 @@ def make_weights(cfg, seed, blocks=None):
     inner = H * 128
     L = cfg["blocks"] if blocks is None else blocks
     t = lambda n, tid, shape, mean=0.0, bf16=False: torch.from_numpy(synthetic(n, seed, tid, mean, 0.02, bf16).reshape(shape))
+    K8 = cfg.get("curve", 0)  # pruned checkpoint: the AdaLN projections read an 8-point curve instead of silu(temb)
+    ka = K8 if K8 else td
     w = {
-        "t_in_w": t(d * 256, T_IN_W, (d, 256)), "t_in_b": t(d, T_IN_B, (d,)),
-        "t_out_w": t(td * d, T_OUT_W, (td, d)), "t_out_b": t(td, T_OUT_B, (td,)),
         "vp_w": t(d * 96, VP_W, (d, 96), bf16=True), "vp_b": t(d, VP_B, (d,)),
         "ap_w": t(d * 32, AP_W, (d, 32), bf16=True), "ap_b": t(d, AP_B, (d,)),
         "cond_w": t(d * tx, COND_W, (d, tx), bf16=True), "cond_b": t(d, COND_B, (d,)),
-        "fada_w": t(2 * d * td, FADA_W, (2 * d, td), bf16=True), "fada_b": t(2 * d, FADA_B, (2 * d,)),
+        "fada_w": t(2 * d * ka, FADA_W, (2 * d, ka), bf16=not K8), "fada_b": t(2 * d, FADA_B, (2 * d,)),
         "hv_w": t(96 * d, HV_W, (96, d)), "hv_b": t(96, HV_B, (96,)),
         "ha_w": t(32 * d, HA_W, (32, d)), "ha_b": t(32, HA_B, (32,)),
         "blocks": [],
     }
+    if K8:
+        w["curve_table"] = torch.from_numpy(synthetic(1025 * K8, seed, CURVE_TABLE, 0.0, CURVE_STD).reshape(1025, K8))
+    else:
+        w.update({"t_in_w": t(d * 256, T_IN_W, (d, 256)), "t_in_b": t(d, T_IN_B, (d,)),
+                  "t_out_w": t(td * d, T_OUT_W, (td, d)), "t_out_b": t(td, T_OUT_B, (td,))})
     def block(b):
         return {
             "norm1": t(d, b + NORM1, (d,), mean=1.0),
@@ -116,7 +123,7 @@ def make_weights(cfg, seed, blocks=None):
 
     for l in range(L):
         b = BLOCK_BASE + BLOCK_STRIDE * l
-        w["blocks"].append(dict(block(b), ada_w=t(18 * d * td, b + ADA_W, (18 * d, td), bf16=True),
+        w["blocks"].append(dict(block(b), ada_w=t(18 * d * ka, b + ADA_W, (18 * d, ka), bf16=not K8),
                                 ada_b=t(18 * d, b + ADA_B, (18 * d,))))
     w["refiner"] = [block(REFINER_BASE + BLOCK_STRIDE * r) for r in range(cfg.get("refiner", 0))]
     if w["refiner"]:
@@ -219,6 +226,21 @@ def time_embedding(levels, w):
     temb = h @ w["t_out_w"].T + w["t_out_b"]
     s = torch.from_numpy(bf16_round(torch.nn.functional.silu(temb).numpy()))
     return temb, s
+
+
+def curve_points(levels, table):
+    """Pruned checkpoints (architecture.md:57-60): the 8-point curve c(t) read from adaln_t_table [1025][8] at
+    t * 1024 with linear interpolation, clamped to the table (tools/check_pruned_curve.py:66-70, `c_of`, the t * 1024
+    hypothesis the reference implements); in double from the float level and table, rounded to float at the end, as
+    the library does it. [U][8]."""
+    tab = np.asarray(table, np.float32).astype(np.float64)
+    out = np.zeros((len(levels), tab.shape[1]), np.float32)
+    for u, t in enumerate(levels):
+        pos = min(max(float(np.float32(t)) * 1024.0, 0.0), 1024.0)
+        i0 = min(int(math.floor(pos)), 1023)
+        wt = pos - i0
+        out[u] = ((1.0 - wt) * tab[i0] + wt * tab[i0 + 1]).astype(np.float32)
+    return torch.from_numpy(out)
 
 
 def rms(x, eps):
@@ -332,9 +354,12 @@ def step(cfg, w, L, text, video, audio, t_video, t_audio, allowed_fn=None, int8=
     lvl = np.array([lv_a if r == 3 else (lv_c if r == 1 else (lv_r if r == 2 else lv_v)) for r in roles], np.int64)
     midx = torch.from_numpy(lvl * 3 + tags.astype(np.int64))
     U = len(levels)
-    temb, s = time_embedding(levels, w)
-    if probes:
-        probes("temb", -1, temb.numpy())
+    if "curve_table" in w:
+        s = curve_points(levels, w["curve_table"])  # no time embedder: the projections read the curve, no SiLU
+    else:
+        temb, s = time_embedding(levels, w)
+        if probes:
+            probes("temb", -1, temb.numpy())
     # packed input
     x = torch.zeros(S, d)
     if T:

@@ -6,6 +6,9 @@ mounted; the fixtures travel, the reference does not):
                   on seeded small weights)
   rope_freq.npy   the rotary frequencies exactly as tools/dump_h3_ref.py:140-141 builds them (the expression taken from
                   the file's syntax tree and evaluated with torch on the CPU)
+  curve.npz       a pruned checkpoint's curve lookup exactly as tools/check_pruned_curve.py:66-70 does it (its function
+                  `c_of`, taken from the file's syntax tree and executed in float64 on a seeded [1025][8] table, at the
+                  t * 1024 positions the reference implements, and past both ends)
   geometry.json   the known answers of tests/geometry_test.cpp:22-43 (read as text)
 
     python tests/golden/make_golden.py [/path/to/reference]
@@ -54,6 +57,21 @@ def time_adaln(ref):
              **{k: v.numpy() for k, v in w.items()})
 
 
+def curve(ref):
+    path = os.path.join(ref, "tools", "check_pruned_curve.py")
+    mod = functions_from(path, ["c_of"])
+    g = torch.Generator().manual_seed(4321)
+    table = torch.randn(1025, 8, generator=g, dtype=torch.float64) * 4.0
+    ns = {"torch": torch, "math": math, "table": table}
+    exec(compile(mod, path, "exec"), ns)
+    # the levels as the step receives them (float), so the comparison measures the lookup and not the rounding of t
+    ts = [float(np.float32(t)) for t in (0.0, 1e-4, 0.0769230769, 0.25, 0.3333333, 0.5, 0.7, 0.9, 0.999, 0.99999, 1.0)]
+    c = np.stack([ns["c_of"](t * 1024).numpy() for t in ts])
+    outside = np.stack([ns["c_of"](p).numpy() for p in (-3.5, 1030.25)])
+    np.savez(os.path.join(HERE, "curve.npz"), table=table.numpy(), t=np.array(ts), c=c, outside_pos=np.array([-3.5, 1030.25]),
+             outside=outside)
+
+
 def rope_freq(ref):
     path = os.path.join(ref, "tools", "dump_h3_ref.py")
     tree = ast.parse(open(path).read())
@@ -82,4 +100,5 @@ if __name__ == "__main__":
     time_adaln(ref)
     rope_freq(ref)
     geometry(ref)
+    curve(ref)
     print("golden fixtures written to", HERE)

@@ -323,3 +323,33 @@ def test_oracle_token_refiner_ends_in_its_weighted_rms_norm():
     assert not torch.allclose(y, O.rms(x, 1e-6) * w["refiner_norm"], atol=1e-3)  # the blocks did something
     w0 = O.make_weights(dict(cfg, refiner=0), 5)
     assert O.refine(cfg, w0, x, lambda t: t, 1e-6) is x
+
+
+def test_oracle_curve_lookup_matches_reference_c_of():
+    """Pruned checkpoints: the oracle's curve lookup (fp32) against tools/check_pruned_curve.py's own `c_of` (run on a
+    seeded table by tests/golden/make_golden.py) at t * 1024 and past both ends of the table."""
+    g = np.load(os.path.join(GOLDEN, "curve.npz"))
+    got = O.curve_points([float(t) for t in g["t"]], g["table"]).numpy()
+    np.testing.assert_allclose(got, g["c"], rtol=2e-6, atol=2e-6)
+    out = O.curve_points([float(p) / 1024.0 for p in g["outside_pos"]], g["table"]).numpy()
+    np.testing.assert_allclose(out, g["outside"], rtol=2e-6, atol=2e-6)
+
+
+def test_oracle_pruned_checkpoint_has_no_time_embedder():
+    """A pruned checkpoint's weights: adaln_t_table [1025][8], [18 d][8] and [2 d][8] fp32 projections, no time MLP; block
+    0's modulation is the curve point projected without SiLU."""
+    import torch
+
+    cfg = dict(dim=256, heads=2, ffn=512, blocks=2, time_dim=128, text_dim=256, curve=8)
+    w = O.make_weights(cfg, 2)
+    assert "t_in_w" not in w and w["curve_table"].shape == (1025, 8)
+    assert w["blocks"][0]["ada_w"].shape == (18 * 256, 8) and w["fada_w"].shape == (512, 8)
+    seen = {}
+    L = dict(text=3, frames=1, h=4, w=4, audio=0)
+    text = np.zeros((3, 256), np.float32)
+    video = O.synthetic(4 * 96, 1, 2, 0.0, 1.0).reshape(4, 96)
+    O.step(cfg, w, L, text, video, np.zeros((0, 32), np.float32), 0.6, 0.6, probes=lambda n, l, a: seen.__setitem__(n, a))
+    assert "temb" not in seen
+    c = O.curve_points([0.6], w["curve_table"])
+    want = (c @ w["blocks"][0]["ada_w"].T + w["blocks"][0]["ada_b"]).numpy()
+    np.testing.assert_allclose(seen["mod0"], want, rtol=1e-6, atol=1e-6)
