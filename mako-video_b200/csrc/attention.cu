@@ -725,14 +725,11 @@ void attention(const AttnParams& p, cudaStream_t s)
     maps.q = rows_map(p.q, p.heads, p.rows, p.row_stride);
     maps.k = rows_map(p.k, p.heads, p.rows, p.row_stride);
     maps.v = rows_map(p.v, p.heads, p.rows, p.row_stride);
-    static bool attr[2] = {false, false};
-    if (!attr[sparse]) {
-        if (sparse)
-            H3_CUDA(cudaFuncSetAttribute(attn3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, A3_SMEM));
-        else
-            H3_CUDA(cudaFuncSetAttribute(attn2_kernel<A2_SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize, A2_SMEM));
-        attr[sparse] = true;
-    }
+    static std::atomic<uint64_t> opt_in[2];
+    if (sparse)
+        smem_opt_in(attn3_kernel, A3_SMEM, opt_in[1]);
+    else
+        smem_opt_in(attn2_kernel<A2_SPLIT>, A2_SMEM, opt_in[0]);
     // Dense: two query tiles per CTA share every K/V tile (half the shared-memory traffic per FLOP). Sparse: query
     // tiles have their own key lists, so one tile per CTA with double-buffered scores.
     if (sparse)

@@ -77,6 +77,15 @@ bool device_accessible(const void* p)
     return a.type != cudaMemoryTypeUnregistered && a.devicePointer != nullptr;
 }
 
+uint64_t device_bit()
+{
+    int dev = 0;
+    H3_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev > 63)
+        throw CudaError("device index past 63");
+    return uint64_t(1) << dev;
+}
+
 int num_sms()
 {
     int dev = 0, n = 0;

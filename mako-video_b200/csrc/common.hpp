@@ -3,6 +3,7 @@
 #pragma once
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <atomic>
 #include <cstdint>
 #include <stdexcept>
 #include <string>
@@ -29,6 +30,22 @@ CUtensorMap make_tmap(CUtensorMapDataType type, int rank, const void* base, cons
 uint32_t take_device_error(cudaStream_t s);
 
 int num_sms();
+
+// One bit for the current device (devices 0-63), for per-device one-time set-up.
+uint64_t device_bit();
+
+// Raises a kernel's dynamic shared-memory limit to `bytes` once per device: the opt-in belongs to the kernel in each
+// device's context, so a process that drives several GPUs needs it on every one. Setting it twice is harmless, so
+// the flag is only marked after the call.
+template <class Kernel>
+void smem_opt_in(Kernel* kernel, int bytes, std::atomic<uint64_t>& done)
+{
+    const uint64_t bit = device_bit();
+    if (done.load(std::memory_order_acquire) & bit)
+        return;
+    cuda_check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes), "cudaFuncSetAttribute");
+    done.fetch_or(bit, std::memory_order_release);
+}
 
 // True when a kernel may dereference p: device or managed memory, or pinned host memory mapped into the device's
 // address space (null counts as accessible; callers check their own required arguments).

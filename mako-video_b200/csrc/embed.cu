@@ -205,11 +205,8 @@ void gemv_f32(const float* W, const float* b, const float* x, int U, int N, int 
     if (U < 1 || U > MAXU)
         throw CudaError("gemv_f32: 1 to 4 vectors");
     const size_t smem = size_t(U) * K * sizeof(float);
-    static bool attr = false;
-    if (!attr) {
-        H3_CUDA(cudaFuncSetAttribute(gemv_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-        attr = true;
-    }
+    static std::atomic<uint64_t> opt_in;
+    smem_opt_in(gemv_f32_kernel, 200 * 1024, opt_in);
     const int grid = std::min((N + 7) / 8, num_sms() * 4);
     gemv_f32_kernel<<<grid, 256, smem, s>>>(W, b, x, U, N, K, int(act), out, out2);
     H3_CUDA(cudaGetLastError());
@@ -220,11 +217,8 @@ void adaln_gemv(const void* W, const float* b, const float* x, int U, int groups
     if (U < 1 || U > MAXU || K % 8)
         throw CudaError("adaln_gemv: 1 to 4 vectors and K a multiple of 8");
     const size_t smem = size_t(U) * K * sizeof(float);
-    static bool attr = false;
-    if (!attr) {
-        H3_CUDA(cudaFuncSetAttribute(adaln_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-        attr = true;
-    }
+    static std::atomic<uint64_t> opt_in;
+    smem_opt_in(adaln_kernel, 200 * 1024, opt_in);
     const size_t rows = size_t(groups) * G;
     const int grid = int(std::min<size_t>((rows + 7) / 8, size_t(num_sms()) * 8));
     adaln_kernel<<<grid, 256, smem, s>>>(static_cast<const __nv_bfloat16*>(W), b, x, U, groups, G, K, out);

@@ -419,12 +419,9 @@ void launch(const void* A, const void* B, const GemmParams& p, cudaStream_t s)
     const uint64_t bstr[1] = {ldb * esz};
     const uint32_t bbox[2] = {uint32_t(kelems), uint32_t(BN)};
     const CUtensorMap tb = make_tmap(dt, 2, B, bdims, bstr, bbox);
-    static bool attr_set = false;
+    static std::atomic<uint64_t> opt_in;
     const int smem = Smem<BN, EPI>::TOTAL;
-    if (!attr_set) {
-        H3_CUDA(cudaFuncSetAttribute(gemm_kernel<BN, EPI, IS_I8>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-        attr_set = true;
-    }
+    smem_opt_in(gemm_kernel<BN, EPI, IS_I8>, smem, opt_in);
     const int tiles = ((p.M + BM - 1) / BM) * (p.N / BN);
     const int grid = std::min(tiles, num_sms());
     OutMaps om{};

@@ -297,11 +297,8 @@ void cube_scores(const float* mq, const float* mk, int heads, int cubes, float* 
 {
     const dim3 grid((cubes + CS_T - 1) / CS_T, (cubes + CS_T - 1) / CS_T, heads);
     const size_t smem = size_t(2) * 128 * CS_P * sizeof(float);
-    static bool attr = false;
-    if (!attr) {
-        H3_CUDA(cudaFuncSetAttribute(cube_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-        attr = true;
-    }
+    static std::atomic<uint64_t> opt_in;
+    smem_opt_in(cube_scores_kernel, int(smem), opt_in);
     cube_scores_kernel<<<grid, 256, smem, s>>>(mq, mk, cubes, scores);
     H3_CUDA(cudaGetLastError());
 }
@@ -311,11 +308,8 @@ void cube_topk(const float* scores, int heads, const CubeGrid& g, int k, int loc
     const size_t smem = size_t(g.cubes()) * 4;
     if (smem > 160 * 1024)
         throw CudaError("cube_topk: too many cubes");
-    static bool attr = false;
-    if (!attr) {
-        H3_CUDA(cudaFuncSetAttribute(cube_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
-        attr = true;
-    }
+    static std::atomic<uint64_t> opt_in;
+    smem_opt_in(cube_topk_kernel, 160 * 1024, opt_in);
     cube_topk_kernel<<<dim3(g.cubes(), heads), TK_NT, smem, s>>>(scores, g, k, local, sel, nsel, kcap);
     H3_CUDA(cudaGetLastError());
 }

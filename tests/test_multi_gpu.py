@@ -11,7 +11,7 @@ import torch.multiprocessing as mp
 
 pytestmark = pytest.mark.gpu
 
-CFG = dict(dim=512, heads=4, ffn=1280, blocks=2, time_dim=256, text_dim=512)
+CFG = dict(dim=512, heads=4, ffn=1280, blocks=2, time_dim=256, text_dim=512, refiner=2)
 LAYOUT = dict(text=40, frames=6, h=12, w=14, audio=24, cond_frames=1, cond_last=[1])
 
 
@@ -26,11 +26,11 @@ def _inputs():
     return H, lay, text, video, audio
 
 
-def _rank(rank, world, nccl_id, sparse, q, exchange="fused", int8_mask=0):
+def _rank(rank, world, nccl_id, sparse, q, exchange="fused", int8_mask=0, cfg=None):
     os.environ["H3_EXCHANGE"] = exchange
     H, lay, text, video, audio = _inputs()
     torch.cuda.set_device(rank)
-    m = H.Model(CFG, seed=1, rank=rank, world=world, nccl_id=nccl_id, device=rank, sparse_ratio=sparse, sparse_local=1,
+    m = H.Model(cfg or CFG, seed=1, rank=rank, world=world, nccl_id=nccl_id, device=rank, sparse_ratio=sparse, sparse_local=1,
                 int8_mask=int8_mask)
     m.begin(text, lay)
     v, a = m.step(video, audio, 0.7, 0.4)
@@ -39,14 +39,14 @@ def _rank(rank, world, nccl_id, sparse, q, exchange="fused", int8_mask=0):
     q.put((rank, v, a, v2, a2))
 
 
-def _compare_two_ranks_with_one(sparse, exchange, int8_mask=0):
+def _compare_two_ranks_with_one(sparse, exchange, int8_mask=0, cfg=None):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     ctx = mp.get_context("spawn")
     H, *_ = _inputs()
     nccl_id = H.nccl_unique_id()
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, 2, nccl_id, sparse, q, exchange, int8_mask)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, 2, nccl_id, sparse, q, exchange, int8_mask, cfg)) for r in range(2)]
     for p in procs:
         p.start()
     res = {}
@@ -56,7 +56,7 @@ def _compare_two_ranks_with_one(sparse, exchange, int8_mask=0):
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    one = ctx.Process(target=_rank, args=(0, 1, None, sparse, q, exchange, int8_mask))
+    one = ctx.Process(target=_rank, args=(0, 1, None, sparse, q, exchange, int8_mask, cfg))
     one.start()
     ref = q.get(timeout=300)[1:]
     one.join(timeout=120)
@@ -79,3 +79,35 @@ def test_two_rank_int8_step_matches_one_rank(cuda, exchange):
     row across them, so the int8 rows (and the step) equal the single-rank ones."""
     H, *_ = _inputs()
     _compare_two_ranks_with_one(0.0, exchange, int8_mask=H.INT8_QKV | H.INT8_OUT | H.INT8_FC1 | H.INT8_FC2)
+
+
+def test_two_rank_pruned_checkpoint_step_matches_one_rank(cuda):
+    """A pruned checkpoint: every rank projects the curve point for all blocks itself (no AdaLN all-gather)."""
+    _compare_two_ranks_with_one(0.0, "fused", cfg=dict(CFG, curve=8))
+
+
+def _two_devices_one_process(q):
+    H, lay, text, video, audio = _inputs()
+    out = []
+    for dev in (0, 1):
+        m = H.Model(dict(CFG, blocks=1), seed=1, device=dev, sparse_ratio=0.5, sparse_local=1)
+        m.begin(text, lay)
+        out.append(m.step(video, audio, 0.7, 0.4))
+        m.close()
+    q.put(out)
+
+
+def test_models_on_two_devices_in_one_process(cuda):
+    """One process driving two GPUs (a model on each, one after the other): every kernel's per-device set-up (the
+    dynamic shared-memory opt-in) must happen on each device, and both give the same velocities."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_two_devices_one_process, args=(q,))
+    p.start()
+    (v0, a0), (v1, a1) = q.get(timeout=300)
+    p.join(timeout=120)
+    assert p.exitcode == 0
+    np.testing.assert_array_equal(v0, v1)
+    np.testing.assert_array_equal(a0, a1)
