@@ -246,27 +246,6 @@ __device__ __forceinline__ float ex2_approx(float x)
     return y;
 }
 
-// 2^x on the FMA and integer pipes (for x >= -125; smaller x gives 2^-125): split x = r + f with r = round(x) by
-// adding 1.5 * 2^23 (the sum's low mantissa bits then hold r), approximate 2^f on [-0.5, 0.5] by a cubic, and add r
-// to the exponent field. The cubic's coefficients are a reweighted least-squares fit of 2^f on Chebyshev nodes of
-// [-0.5, 0.5] (max relative error 7.5e-5 in fp32, below bf16's 3.9e-3 resolution). Used for part of the softmax's
-// exponentials so that they do not all queue on the MUFU pipe.
-__device__ __forceinline__ float ex2_poly(float x)
-{
-    x = fmaxf(x, -125.0f);
-    const float t = x + 12582912.0f;
-    const float j = t - 12582912.0f;
-    const float f = x - j;
-    const float p = fmaf(fmaf(fmaf(0.05517161f, f, 0.24261111f), f, 0.69326097f), f, 0.99992806f);
-    const int r = __float_as_int(t) - 0x4B400000;
-    return __int_as_float(__float_as_int(p) + (r << 23));
-}
-
-// ex2_poly on a pair, in packed fp32 arithmetic: the range reduction by the 1.5 * 2^23 rounding constant and the
-// cubic on the FMA pipe (two lanes of work per instruction), the exponent added as an integer. The rounding constant's
-// own bits vanish from (t << 23) modulo 2^32, so the exponent add is one shift-and-add per element.
-__device__ __forceinline__ float2 ex2_poly2(float2 x);
-
 // Three-input maximum (one instruction on sm_100).
 __device__ __forceinline__ float max3f(float a, float b, float c)
 {
@@ -296,18 +275,6 @@ __device__ __forceinline__ float2 add2(float2 a, float2 b)
         : "=f"(d.x), "=f"(d.y)
         : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
     return d;
-}
-
-__device__ __forceinline__ float2 ex2_poly2(float2 x)
-{
-    x = make_float2(fmaxf(x.x, -125.0f), fmaxf(x.y, -125.0f));
-    const float2 t = add2(x, make_float2(12582912.0f, 12582912.0f));
-    const float2 f = fma2(add2(t, make_float2(-12582912.0f, -12582912.0f)), make_float2(-1.0f, -1.0f), x);
-    float2 p = fma2(make_float2(0.05517161f, 0.05517161f), f, make_float2(0.24261111f, 0.24261111f));
-    p = fma2(p, f, make_float2(0.69326097f, 0.69326097f));
-    p = fma2(p, f, make_float2(0.99992806f, 0.99992806f));
-    return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
-                       __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi)
