@@ -377,6 +377,9 @@ __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid
 // TMEM: S buffer 0 | S buffer 1 | O (128 columns each). S(j+2) overwrites P(j) only after PV(j) read it (one thread
 // issues both, and the tensor core runs them in order). The softmax of step j may rescale O only once PV(j-1) is
 // done (it waits for that only when a rescale is needed).
+// A tile of dense rows (text, conditioning, audio) sees every key, the same for both of its units: it runs as one
+// M = 128 tile (unit a in lanes 0-63, unit b in 64-127, the tensor core's full rate) over 128-key blocks loaded
+// once, the ring holding one item per step instead of one per unit.
 constexpr int A3_KST = 3, A3_VST = 2;
 constexpr int NT3 = 64 + 256;
 constexpr int A3_OFF_Q = 0;
@@ -420,7 +423,7 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
             head = (id - p.heads * dt) / vt, tile = (id - p.heads * dt) % vt;
     }
     int nkv = p.nblocks[head * p.q_tiles + tile];
-    const bool every = nkv < 0;
+    const bool every = nkv < 0; // a dense-row tile: one M = 128 tile over every key
     if (every)
         nkv = (p.rows + 127) / 128;
     const int4 qr = p.q_rows[tile]; // (first row of unit a, of unit b or -1, rows of a, rows of b)
@@ -463,15 +466,15 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
         mbar_arrive_expect_tx(q_full, TILE);
         load_rows(smem + A3_OFF_Q, 0, qr.x, head, &maps.q, q_full);
         load_rows(smem + A3_OFF_Q, 1, qr.y < 0 ? qr.x : qr.y, head, &maps.q, q_full);
-        // Ring items i = 2 j + x (step j, query unit x): K runs ahead of V by up to the depth of its ring. A padding
-        // entry (no key unit) loads row 0: the keys are masked.
-        const int items = 2 * nkv;
+        // Ring items i = 2 j + x (step j, query unit x), or i = j for a dense-row tile: K runs ahead of V by up to the
+        // depth of its ring. A padding entry (no key unit) loads row 0: the keys are masked.
+        const int items = every ? nkv : 2 * nkv;
         int ik = 0, iv = 0;
         bool ok = true;
         while (ok && iv < items) {
             const bool k_turn = ik < items && ik < iv + A3_KST;
             const int i = k_turn ? ik : iv;
-            const int4 e = entry(i >> 1, i & 1);
+            const int4 e = every ? every_row_block(i, p.rows) : entry(i >> 1, i & 1);
             const int r0 = e.x < 0 ? 0 : e.x, r1 = e.y < 0 ? r0 : e.y;
             if (k_turn) {
                 const int s = ik % A3_KST;
@@ -493,11 +496,27 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
         }
     } else if (nkv > 0 && warp == 1 && elect_one_lane()) {
         // ------------------------------------------------------------------------------------------ MMA
-        const uint32_t id_s = idesc_bf16(64, 128);
-        const uint32_t id_pv = idesc_bf16(64, 128, false, true);
+        const uint32_t id_s = idesc_bf16(64, 128), id_s128 = idesc_bf16(128, 128);
+        const uint32_t id_pv = idesc_bf16(64, 128, false, true), id_pv128 = idesc_bf16(128, 128, false, true);
         const uint32_t sq = smem_u32(smem + A3_OFF_Q);
-        // S(j) for both query units (unit x: query rows at 8192 x within each dim half, lanes at 16 x)
+        // S(j) for both query units (unit x: query rows at 8192 x within each dim half, lanes at 16 x), or for the
+        // whole 128-row tile of a dense-row tile
         auto issue_s = [&](int j) -> bool {
+            if (every) {
+                const int s = j % A3_KST;
+                if (!mbar_wait(&k_full[s], (j / A3_KST) & 1))
+                    return false;
+                tc_fence_after();
+                const uint32_t sk = smem_u32(smem + A3_OFF_K + s * TILE);
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk) {
+                    const uint32_t off = (kk >> 2) * HALF + (kk & 3) * 32;
+                    mma_bf16_ss(tmem + (j & 1) * 128, sdesc_sw128(sq + off, 16, 1024), sdesc_sw128(sk + off, 16, 1024), id_s128, kk > 0);
+                }
+                mma_commit(&k_empty[s]);
+                mma_commit(&s_full[j & 1]);
+                return true;
+            }
             for (int x = 0; x < 2; ++x) {
                 const int i = 2 * j + x, s = i % A3_KST;
                 if (!mbar_wait(&k_full[s], (i / A3_KST) & 1))
@@ -521,7 +540,18 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
         for (int j = 0; j < nkv && ok; ++j) {
             if (!(ok = mbar_wait(&p_full[j & 1], (j >> 1) & 1)))
                 break;
-            for (int x = 0; x < 2 && ok; ++x) {
+            if (every) {
+                const int sv = j % A3_VST;
+                if (!(ok = mbar_wait(&v_full[sv], (j / A3_VST) & 1)))
+                    break;
+                tc_fence_after();
+                const uint32_t vb = smem_u32(smem + A3_OFF_V + sv * TILE);
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk)
+                    mma_bf16_ts(tmem + T_O, tmem + (j & 1) * 128 + kk * 8, sdesc_sw128(vb + kk * 2048, HALF, 1024), id_pv128, (j | kk) != 0);
+                mma_commit(&v_empty[sv]);
+            }
+            for (int x = 0; x < 2 && ok && !every; ++x) {
                 const int i = 2 * j + x, sv = i % A3_VST;
                 if (!(ok = mbar_wait(&v_full[sv], (i / A3_VST) & 1)))
                     break;
@@ -547,8 +577,10 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
         const int hc = (warp - 2) >> 2; // 64-key half of the step this warp handles
         const int quarter = warp & 3;
         const int row = quarter * 32 + lane_id(); // TMEM lane
-        const int x = (lane_id() >> 4) & 1;       // query unit of this lane's row
-        const int m = quarter * 16 + (lane_id() & 15); // the row's index inside its unit
+        // query unit of this lane's row and the row's index inside it (M = 64 layout: 16 lanes of each quarter per
+        // unit; M = 128 layout of a dense-row tile: lane = row of the tile)
+        const int x = every ? quarter >> 1 : (lane_id() >> 4) & 1;
+        const int m = every ? (quarter & 1) * 32 + lane_id() : quarter * 16 + (lane_id() & 15);
         const uint32_t lane_base = uint32_t(quarter * 32) << 16;
         const uint32_t tO = tmem + lane_base + T_O + hc * 64;
         float* red = reinterpret_cast<float*>(smem + A3_OFF_RED); // [3 slots][2 slices][128 rows]
