@@ -101,7 +101,10 @@ __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid
 
     const int warp = warp_id();
     const int pair = blockIdx.x, head = blockIdx.y;
-    const int nkv = (p.rows + 127) / 128;
+    // keys: 128-row blocks [kv0, kv0 + nkv), all of them or this CTA's part of a split launch (gridDim.z parts)
+    const int nkv_all = (p.rows + 127) / 128, per = (nkv_all + gridDim.z - 1) / gridDim.z;
+    const int kv0 = blockIdx.z * per;
+    const int nkv = min(nkv_all, kv0 + per) - kv0;
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
@@ -144,16 +147,16 @@ __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid
                 if (!mbar_wait(&k_empty[s], ((jk / A2_KST) & 1) ^ 1))
                     break;
                 mbar_arrive_expect_tx(&k_full[s], TILE);
-                load_rows(smem + A2_OFF_K + s * TILE, 0, 128 * jk, head, &maps.k, &k_full[s]);
-                load_rows(smem + A2_OFF_K + s * TILE, 1, 128 * jk + 64, head, &maps.k, &k_full[s]);
+                load_rows(smem + A2_OFF_K + s * TILE, 0, 128 * (kv0 + jk), head, &maps.k, &k_full[s]);
+                load_rows(smem + A2_OFF_K + s * TILE, 1, 128 * (kv0 + jk) + 64, head, &maps.k, &k_full[s]);
                 ++jk;
             } else {
                 const int s = jv % A2_VST;
                 if (!mbar_wait(&v_empty[s], ((jv / A2_VST) & 1) ^ 1))
                     break;
                 mbar_arrive_expect_tx(&v_full[s], TILE);
-                load_rows(smem + A2_OFF_V + s * TILE, 0, 128 * jv, head, &maps.v, &v_full[s]);
-                load_rows(smem + A2_OFF_V + s * TILE, 1, 128 * jv + 64, head, &maps.v, &v_full[s]);
+                load_rows(smem + A2_OFF_V + s * TILE, 0, 128 * (kv0 + jv), head, &maps.v, &v_full[s]);
+                load_rows(smem + A2_OFF_V + s * TILE, 1, 128 * (kv0 + jv) + 64, head, &maps.v, &v_full[s]);
                 ++jv;
             }
         }
@@ -244,7 +247,7 @@ __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid
                     for (int i = 0; i < 32; ++i)
                         s[c * 32 + i] = __uint_as_float(r[c][i]);
             }
-            const int left = p.rows - j * 128 - hc * NC;
+            const int left = p.rows - (kv0 + j) * 128 - hc * NC;
             if (left < NC) {
 #pragma unroll
                 for (int c = 0; c < NC; ++c)
@@ -332,7 +335,28 @@ __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid
                     l += slot[o * 128 + row];
             }
         }
-        if (ok && mbar_wait(&pv_done[t], (nkv - 1) & 1)) {
+        const bool done = ok && mbar_wait(&pv_done[t], (nkv - 1) & 1);
+        if (done && gridDim.z > 1) {
+            // a split launch: this part's unnormalised output, row maximum and sum, for the combine kernel
+            tc_fence_after();
+            const int out_row = pair * 256 + t * 128 + row;
+            const size_t item = (size_t(blockIdx.z) * p.rows + out_row) * p.heads + head;
+#pragma unroll 1
+            for (int c = 0; c < NC / 32; ++c) {
+                uint32_t o[32];
+                tmem_ld32(tO + c * 32, o);
+                tmem_wait_ld();
+                if (out_row < p.rows) {
+                    float4* d4 = reinterpret_cast<float4*>(p.part_o + item * 128 + hc * NC + c * 32);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        d4[i] = make_float4(__uint_as_float(o[4 * i]), __uint_as_float(o[4 * i + 1]), __uint_as_float(o[4 * i + 2]),
+                                            __uint_as_float(o[4 * i + 3]));
+                }
+            }
+            if (out_row < p.rows && hc == 0)
+                *reinterpret_cast<float2*>(p.part_ml + item * 2) = make_float2(m, l);
+        } else if (done) {
             tc_fence_after();
             const int out_row = pair * 256 + t * 128 + row;
             const float inv = l > 0.f ? 1.f / l : 0.f;
@@ -734,6 +758,35 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
     }
 }
 
+// Merges the two halves of a split dense launch: per (row, head) one warp, four dims a lane; the halves' outputs
+// weighted by 2^(m_s - max(m_0, m_1)), divided by the weighted sum, bf16 into the output (this rank's or its owner's).
+__global__ void __launch_bounds__(256) attn_combine_kernel(const AttnParams p)
+{
+    const size_t item = size_t(blockIdx.x) * 8 + warp_id();
+    if (item >= size_t(p.rows) * p.heads)
+        return;
+    const int row = int(item / p.heads), head = int(item % p.heads);
+    const size_t i1 = size_t(p.rows) * p.heads + item;
+    const float2 a = *reinterpret_cast<const float2*>(p.part_ml + item * 2);
+    const float2 b = *reinterpret_cast<const float2*>(p.part_ml + i1 * 2);
+    const float mx = fmaxf(a.x, b.x);
+    const float wa = mx == -INFINITY ? 0.f : ex2_approx(a.x - mx), wb = mx == -INFINITY ? 0.f : ex2_approx(b.x - mx);
+    const float sum = wa * a.y + wb * b.y;
+    const float inv = sum > 0.f ? 1.f / sum : 0.f;
+    const float4 oa = *reinterpret_cast<const float4*>(p.part_o + item * 128 + lane_id() * 4);
+    const float4 ob = *reinterpret_cast<const float4*>(p.part_o + i1 * 128 + lane_id() * 4);
+    __nv_bfloat16* dst = out_ptr(p, row, head, lane_id() * 4);
+    *reinterpret_cast<uint2*>(dst) = make_uint2(pack_bf16x2((oa.x * wa + ob.x * wb) * inv, (oa.y * wa + ob.y * wb) * inv),
+                                                pack_bf16x2((oa.z * wa + ob.z * wb) * inv, (oa.w * wa + ob.w * wb) * inv));
+}
+
+// A dense launch of this many rows and heads splits its keys in two when its CTAs fill fewer than six waves.
+bool split_dense(int rows, int heads)
+{
+    const long long ctas = (long long)((rows + 255) / 256) * heads;
+    return (rows + 127) / 128 >= 4 && ctas < 6LL * num_sms();
+}
+
 CUtensorMap rows_map(const void* base, int heads, int rows, int64_t row_stride)
 {
     const uint64_t dims[3] = {128, uint64_t(heads), uint64_t(rows > 0 ? rows : 1)};
@@ -744,7 +797,14 @@ CUtensorMap rows_map(const void* base, int heads, int rows, int64_t row_stride)
 
 } // namespace
 
-void attention(const AttnParams& p, cudaStream_t s)
+size_t attention_split_bytes(int rows, int heads)
+{
+    if (rows <= 0 || heads <= 0 || !split_dense(rows, heads))
+        return 0;
+    return size_t(2) * rows * heads * (128 + 2) * sizeof(float);
+}
+
+int attention(const AttnParams& p, cudaStream_t s)
 {
     if (p.heads <= 0 || !p.q || !p.k || !p.v || !p.out || (p.row_stride * 2) % 16 || (p.out_row_stride * 2) % 16)
         throw CudaError("attention: bad arguments");
@@ -752,7 +812,7 @@ void attention(const AttnParams& p, cudaStream_t s)
     if (sparse && (p.grid.cubes() <= 0 || !p.nblocks || !p.q_rows || p.q_tiles <= 0 || p.rows != p.grid.rows()))
         throw CudaError("attention: bad sparse arguments");
     if (p.rows <= 0)
-        return;
+        return 0;
     Maps maps;
     maps.q = rows_map(p.q, p.heads, p.rows, p.row_stride);
     maps.k = rows_map(p.k, p.heads, p.rows, p.row_stride);
@@ -764,11 +824,22 @@ void attention(const AttnParams& p, cudaStream_t s)
         smem_opt_in(attn2_kernel<A2_SPLIT>, A2_SMEM, opt_in[0]);
     // Dense: two query tiles per CTA share every K/V tile (half the shared-memory traffic per FLOP). Sparse: query
     // tiles have their own key lists, so one tile per CTA with double-buffered scores.
-    if (sparse)
+    if (sparse) {
         attn3_kernel<<<p.q_tiles * p.heads, NT3, A3_SMEM, s>>>(maps, p);
-    else
-        attn2_kernel<A2_SPLIT><<<dim3((p.rows + 255) / 256, p.heads), NT2, A2_SMEM, s>>>(maps, p);
+        H3_CUDA(cudaGetLastError());
+        return 1;
+    }
+    // A launch of few waves (several ranks leave each a few heads) loses much of its last wave; splitting every CTA's
+    // keys in two, given scratch for the halves, doubles the CTAs, and a combine kernel merges them.
+    const int parts = p.part_o && p.part_ml && split_dense(p.rows, p.heads) ? 2 : 1;
+    attn2_kernel<A2_SPLIT><<<dim3((p.rows + 255) / 256, p.heads, parts), NT2, A2_SMEM, s>>>(maps, p);
     H3_CUDA(cudaGetLastError());
+    if (parts == 1)
+        return 1;
+    const size_t items = size_t(p.rows) * p.heads;
+    attn_combine_kernel<<<unsigned((items + 7) / 8), 256, 0, s>>>(p);
+    H3_CUDA(cudaGetLastError());
+    return 2;
 }
 
 } // namespace h3

@@ -72,6 +72,11 @@ struct AttnParams {
     void* peer_out[8] = {};
     int rows_per_rank = 0, my_rank = 0;
     float scale = 0.08838834764831845f; // 1 / sqrt(128)
+    // Dense mode, launches of few waves: scratch for a key range split in two (null: never split). part_o
+    // [2][rows][heads][128] fp32 receives each half's unnormalised output and part_ml [2][rows][heads][2] its row
+    // maximum (log2 units) and sum; a combine kernel merges the halves into `out`. Sized by attention_split_bytes.
+    float* part_o = nullptr;
+    float* part_ml = nullptr;
 
     // Sparse mode (blocks != null; rows in the packed order above). Query tile t is two units (two cubes, or two
     // chunks of dense rows), q_rows[t] = (first row a, first row b or -1, rows of a, rows of b); each unit has its
@@ -87,6 +92,12 @@ struct AttnParams {
     CubeGrid grid;
 };
 
-void attention(const AttnParams& p, cudaStream_t s);
+// Launches the attention; returns the number of kernels launched.
+int attention(const AttnParams& p, cudaStream_t s);
+
+// Bytes of split scratch (part_o + part_ml) a dense launch of `rows` rows and `heads` heads uses, 0 when it runs in
+// enough waves not to split (under six waves of CTAs on this device's SMs: the partial last wave costs more than
+// writing and merging the two halves).
+size_t attention_split_bytes(int rows, int heads);
 
 } // namespace h3

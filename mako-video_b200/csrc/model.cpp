@@ -284,6 +284,8 @@ struct Model::Impl {
     DevBuf in_video, in_audio, pk_video, pk_audio, rows_out, rows_all;
     SparseBuffers sp;
     DevBuf sp_mq, sp_mk, sp_scores, sp_sel, sp_nsel, sp_blocks, sp_nblocks, sp_qrows;
+    DevBuf attn_part; // dense attention split scratch: [2][S][H/P][128] fp32 outputs, then [2][S][H/P][2] (max, sum)
+    size_t attn_split_bytes = 0;
     ncclComm_t comm = nullptr;
     std::vector<cudaEvent_t> ev;
     // Sequence parallel with the exchange fused into the kernels: every rank's qkv_recv and o_recv mapped here.
@@ -497,6 +499,10 @@ void Model::alloc_activations()
     }
     d_->rows_out.ensure(M * 128 * 4);
     d_->rows_all.ensure(Spad * 128 * 4);
+    // scratch for the dense attention's key-split halves (only layouts whose attention launch fills few waves)
+    d_->attn_split_bytes = attention_split_bytes(S_, Hp);
+    if (d_->attn_split_bytes)
+        d_->attn_part.ensure(d_->attn_split_bytes);
     if (P > 1 && d_->fused)
         map_peers();
 }
@@ -1023,11 +1029,13 @@ void Model::step(const float* video, const float* audio, float t_video, float t_
             mark("select");
             ap.blocks = b.blocks, ap.nblocks = b.nblocks, ap.q_rows = b.q_rows, ap.q_tiles = b.q_tiles;
             ap.max_blocks = b.max_blocks, ap.grid = grid;
-            attention(ap, s);
-            launches_ += 5;
+            launches_ += 4 + attention(ap, s);
         } else {
-            attention(ap, s);
-            launches_ += 1;
+            if (d_->attn_split_bytes) {
+                ap.part_o = d_->attn_part.as<float>();
+                ap.part_ml = ap.part_o + size_t(2) * S_ * Hp * 128;
+            }
+            launches_ += attention(ap, s);
         }
         mark("attn");
         const void* oin = d_->o.p;
