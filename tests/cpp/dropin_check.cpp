@@ -2,6 +2,7 @@
 // host-side members, which need no GPU: parse_int8, rows, and the refusal of a checkpoint path.
 #include "models/h3.hpp"
 
+#include <cstddef>
 #include <cstdio>
 
 namespace mako::mtl {
@@ -46,5 +47,12 @@ int main()
         threw = std::string(e.what()).find("synthetic") != std::string::npos;
     }
     check(threw, "a checkpoint path is refused with a message");
+    // The C ABI's struct layouts, for the bindings' own declarations to be checked against (tests/test_cpp_dropin.py).
+    std::printf("abi h3_config %zu %zu %zu\n", sizeof(h3_config), offsetof(h3_config, refiner_blocks), offsetof(h3_config, curve_dims));
+    std::printf("abi h3_layout %zu %zu %zu\n", sizeof(h3_layout), offsetof(h3_layout, refs), offsetof(h3_layout, n_refs));
+    std::printf("abi h3_layout_ref %zu\n", sizeof(h3_layout_ref));
+    std::printf("abi h3_world %zu %zu\n", sizeof(h3_world), offsetof(h3_world, nccl_id));
+    std::printf("abi h3k_gemm_args %zu %zu\n", sizeof(h3k_gemm_args), offsetof(h3k_gemm_args, b_scale));
+    std::printf("abi h3k_cube_grid %zu\n", sizeof(h3k_cube_grid));
     return failures ? 1 : 0;
 }

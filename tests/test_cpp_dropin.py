@@ -1,5 +1,6 @@
 """The C++ drop-in header (include/models/h3.hpp) compiles against the reference's usage and its host-side members
 work through libh3b200.so (no GPU needed)."""
+import ctypes
 import os
 import subprocess
 
@@ -17,3 +18,15 @@ def test_dropin_header_compiles_and_runs(tmp_path):
     r = subprocess.run([str(exe)], capture_output=True, text=True)
     assert r.returncode == 0, r.stdout + r.stderr
     assert "FAIL" not in r.stdout
+    # the ctypes declarations of the Python binding match the header's struct layouts
+    abi = {line.split()[1]: [int(v) for v in line.split()[2:]] for line in r.stdout.splitlines() if line.startswith("abi ")}
+    H = h3b200
+    want = {
+        "h3_config": [ctypes.sizeof(H.h3_config), H.h3_config.refiner_blocks.offset, H.h3_config.curve_dims.offset],
+        "h3_layout": [ctypes.sizeof(H.h3_layout), H.h3_layout.refs.offset, H.h3_layout.n_refs.offset],
+        "h3_layout_ref": [ctypes.sizeof(H.h3_layout_ref)],
+        "h3_world": [ctypes.sizeof(H.h3_world), H.h3_world.nccl_id.offset],
+        "h3k_gemm_args": [ctypes.sizeof(H.h3k_gemm_args), H.h3k_gemm_args.b_scale.offset],
+        "h3k_cube_grid": [ctypes.sizeof(H.h3k_cube_grid)],
+    }
+    assert abi == want, (abi, want)
