@@ -87,9 +87,15 @@ const char* h3_last_error(void);
 int h3_nccl_unique_id(uint8_t out[128]);
 
 /* H3::H3(path, ctx, telemetry, int8) and Engine::transformer (src/video/engine.cpp:105-117).
- * weights: "synthetic:SEED" for random-init weights (every value a hash of SEED, tensor and index); loading a
- * checkpoint directory is not built and returns H3_ERR_ARG. int8_mask: bits 1 qkv, 2 out, 4 fc1, 8 fc2
- * (H3::Int8). sparse_ratio / sparse_local as h3_set_sparse. world: NULL for one rank. device: the CUDA device. */
+ * weights: "synthetic:SEED" for random-init weights (every value a hash of SEED, tensor and index), or a checkpoint:
+ * a safetensors file or a directory of them holding every tensor h3_check_weights lists, under this build's names
+ * (the reference's own where its files or prose give them: time_embedder.*, blocks.N.adaln_proj.linear.*,
+ * adaln_t_table, condition_proj, video_patch_proj, audio_patch_proj, proj_out), in the logical layout: fc1
+ * [gate; value], q/k/v stacked q, k, v (or, with file metadata qkv_layout = interleaved, each head's q, k and v rows
+ * together, stacked at load as the reference's upload_qkv does, docs/architecture.md:62-63). BF16, F16 and F32
+ * tensors are converted to the model's element types. A missing tensor or a shape that disagrees returns H3_ERR_ARG
+ * before any device work. int8_mask: bits 1 qkv, 2 out, 4 fc1, 8 fc2 (H3::Int8), quantised per row at load.
+ * sparse_ratio / sparse_local as h3_set_sparse. world: NULL for one rank. device: the CUDA device. */
 int h3_create(const h3_config* cfg, const char* weights, uint32_t int8_mask, float sparse_ratio, uint32_t sparse_local,
               const h3_world* world, int32_t device, h3_model** out);
 
@@ -128,6 +134,23 @@ int h3_add_lora(h3_model* m, const char* path, float scale, int32_t strict, uint
  * stripped), '\n'-separated, NUL-terminated, truncated to cap bytes; *count the adapters, *rank the first one's
  * rank, *alpha the file's "alpha" metadata (0 when absent). Any pointer may be NULL. No counterpart in the reference. */
 int h3_lora_inspect(const char* path, char* names, uint64_t cap, uint32_t* count, uint32_t* rank, float* alpha);
+
+/* Every tensor a checkpoint for this model shape holds, one line each: "name dtype shape" (dtype BF16 or F32, the
+ * element type the model keeps; shape as d0xd1), in set-up order; NUL-terminated, truncated to cap bytes; *count the
+ * tensors. For converters from other layouts. Host only. No counterpart in the reference. */
+int h3_weight_specs(const h3_config* cfg, char* out, uint64_t cap, uint32_t* count);
+
+/* Writes the model's weights to a safetensors file in the layout h3_create reads (qkv_layout = stacked), so that a
+ * model created from the file computes what this one does. bf16 models only (an int8 model holds no bf16 rows of its
+ * quantised projections: H3_ERR_ARG). The file holding the weights is the reference's model directory's role
+ * (src/video/engine.cpp:105-117); the writer itself has no counterpart in the reference. */
+int h3_save_weights(h3_model* m, const char* path);
+
+/* Checks a checkpoint (file or directory) against a model shape without touching a GPU: H3_OK when every tensor
+ * h3_create needs is there with its shape, else H3_ERR_ARG with the first problem (a missing tensor, a shape that
+ * disagrees) in message (NUL-terminated, truncated to cap bytes; may be NULL) and h3_last_error(). Host only. No
+ * counterpart in the reference. */
+int h3_check_weights(const h3_config* cfg, const char* path, char* message, uint64_t cap);
 
 /* Engine::sigmas(steps, shift) (src/video/engine.cpp:71-88): the schedule from 1 to 0, torch.linspace's float
  * spacing, shifted by s x / (1 + (s - 1) x), consecutive repeats dropped. Writes up to `steps` points to out and

@@ -83,9 +83,9 @@ public:
 
     using ProbeFn = std::function<void(const std::string& name, int layer, const float* data, size_t n)>;
 
-    // H3(path, ctx, telemetry, int8) (src/video/engine.cpp:109-110). `path` is "synthetic:SEED" (random-init weights);
-    // a checkpoint directory is refused (the safetensors loader is not built). The context and telemetry arguments
-    // of mako-common's runtime are accepted and unused: the GPU is the current CUDA device.
+    // H3(path, ctx, telemetry, int8) (src/video/engine.cpp:109-110). `path` is a checkpoint (a safetensors file or a
+    // directory of them, see h3_create) or "synthetic:SEED" (random-init weights). The context and telemetry
+    // arguments of mako-common's runtime are accepted and unused: the GPU is the current CUDA device.
     template <class Context, class Telemetry>
     H3(const std::string& path, Context&, Telemetry, uint32_t int8, h3_config cfg = h3_mini_h3(), const h3_world* world = nullptr,
        int device = 0)
@@ -102,6 +102,9 @@ public:
 
     // MiniMax-H3's shape.
     static h3_config h3_mini_h3() { return h3_config{kDim, 56, 14336, 50, kTimeDim, kText, kVideoPatch, kAudioChannels, 1e-6f, 2, 0}; }
+
+    // Writes the weights to a safetensors file a later H3(path, ...) reads back (h3_save_weights; bf16 models).
+    void save_weights(const std::string& path) { check(h3_save_weights(m_, path.c_str())); }
 
     // set_sparse(ratio, local) (src/video/engine.cpp:112).
     void set_sparse(float ratio, uint32_t local) { check(h3_set_sparse(m_, ratio, local)); }

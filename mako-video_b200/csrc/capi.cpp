@@ -55,6 +55,9 @@ int guarded(F&& f)
     } catch (const DeviceError& e) {
         g_error = e.what();
         return H3_ERR_DEVICE;
+    } catch (const std::invalid_argument& e) {
+        g_error = e.what();
+        return H3_ERR_ARG;
     } catch (const h3::CudaError& e) {
         g_error = e.what();
         const std::string w = e.what();
@@ -112,6 +115,22 @@ h3::Layout to_layout(const h3_layout* l)
     if (o.h % 2 || o.w % 2)
         throw ArgError("layout: the latent height and width must be even");
     return o;
+}
+
+h3::Config to_config(const h3_config* cfg)
+{
+    h3::Config c;
+    c.dim = int(cfg->dim), c.heads = int(cfg->heads), c.ffn = int(cfg->ffn), c.blocks = int(cfg->blocks);
+    c.time_dim = int(cfg->time_dim), c.text_dim = int(cfg->text_dim), c.video_patch = int(cfg->video_patch);
+    c.audio_channels = int(cfg->audio_channels), c.eps = cfg->eps, c.refiner = int(cfg->refiner_blocks);
+    if (c.video_patch != 96 || c.audio_channels != 32)
+        throw ArgError("h3_create: video_patch must be 96 and audio_channels 32");
+    if (cfg->refiner_blocks > 2)
+        throw ArgError("h3_create: at most 2 token refiner blocks (MiniMax-H3 has 2)");
+    if (cfg->curve_dims != 0 && cfg->curve_dims != 8)
+        throw ArgError("h3_create: curve_dims is 0 (full model) or 8 (pruned checkpoint)");
+    c.curve = int(cfg->curve_dims);
+    return c;
 }
 
 h3::CubeGrid to_grid(const h3k_cube_grid* g)
@@ -189,22 +208,20 @@ int h3_create(const h3_config* cfg, const char* weights, uint32_t int8_mask, flo
             throw ArgError("h3_create: null argument");
         *out = nullptr;
         const std::string w = weights;
-        if (w.rfind("synthetic:", 0) != 0)
-            throw ArgError("h3_create: only synthetic weights (\"synthetic:SEED\") are built; loading " + w + " is not");
-        const uint64_t seed = std::stoull(w.substr(10));
         if (int8_mask & ~15u)
             throw ArgError("h3_create: int8 mask bits are 1 qkv, 2 out, 4 fc1, 8 fc2");
-        h3::Config c;
-        c.dim = int(cfg->dim), c.heads = int(cfg->heads), c.ffn = int(cfg->ffn), c.blocks = int(cfg->blocks);
-        c.time_dim = int(cfg->time_dim), c.text_dim = int(cfg->text_dim), c.video_patch = int(cfg->video_patch);
-        c.audio_channels = int(cfg->audio_channels), c.eps = cfg->eps, c.refiner = int(cfg->refiner_blocks);
-        if (c.video_patch != 96 || c.audio_channels != 32)
-            throw ArgError("h3_create: video_patch must be 96 and audio_channels 32");
-        if (cfg->refiner_blocks > 2)
-            throw ArgError("h3_create: at most 2 token refiner blocks (MiniMax-H3 has 2)");
-        if (cfg->curve_dims != 0 && cfg->curve_dims != 8)
-            throw ArgError("h3_create: curve_dims is 0 (full model) or 8 (pruned checkpoint)");
-        c.curve = int(cfg->curve_dims);
+        const h3::Config c = to_config(cfg);
+        // the weights: synthetic, or a checkpoint whose names and shapes are checked before any device work
+        std::unique_ptr<h3::WeightSource> src;
+        if (w.rfind("synthetic:", 0) == 0) {
+            src = std::make_unique<h3::SyntheticWeights>(std::stoull(w.substr(10)));
+        } else {
+            auto ck = std::make_unique<h3::CheckpointWeights>(w);
+            const std::string problem = ck->check(c);
+            if (!problem.empty())
+                throw ArgError("h3_create: " + w + ": " + problem);
+            src = std::move(ck);
+        }
         h3::World wd;
         if (world) {
             wd.rank = world->rank, wd.size = world->size;
@@ -213,7 +230,7 @@ int h3_create(const h3_config* cfg, const char* weights, uint32_t int8_mask, flo
         H3_CUDA(cudaSetDevice(device));
         auto m = std::make_unique<h3_model>();
         m->device = device;
-        m->m = std::make_unique<h3::Model>(c, seed, int8_mask, wd);
+        m->m = std::make_unique<h3::Model>(c, *src, int8_mask, wd);
         m->m->set_sparse(sparse_ratio, int(sparse_local));
         *out = m.release();
     });
@@ -287,6 +304,55 @@ int h3_add_lora(h3_model* m, const char* path, float scale, int32_t strict, uint
             *merged = uint32_t(r.merged);
         if (skipped)
             *skipped = uint32_t(r.skipped);
+    });
+}
+
+int h3_weight_specs(const h3_config* cfg, char* out, uint64_t cap, uint32_t* count)
+{
+    return guarded([&] {
+        if (!cfg)
+            throw ArgError("h3_weight_specs: null config");
+        const std::vector<h3::WeightSpec> specs = h3::weight_specs(to_config(cfg));
+        std::string text;
+        for (const h3::WeightSpec& sp : specs) {
+            text += sp.name + (sp.bf16 ? " BF16 " : " F32 ");
+            for (size_t k = 0; k < sp.shape.size(); ++k)
+                text += (k ? "x" : "") + std::to_string(sp.shape[k]);
+            text += "\n";
+        }
+        if (out && cap) {
+            const size_t n = std::min<size_t>(text.size(), cap - 1);
+            std::memcpy(out, text.data(), n);
+            out[n] = '\0';
+        }
+        if (count)
+            *count = uint32_t(specs.size());
+    });
+}
+
+int h3_save_weights(h3_model* m, const char* path)
+{
+    return guarded([&] {
+        check_model(m);
+        if (!path)
+            throw ArgError("h3_save_weights: null path");
+        m->m->save(path);
+    });
+}
+
+int h3_check_weights(const h3_config* cfg, const char* path, char* message, uint64_t cap)
+{
+    return guarded([&] {
+        if (!cfg || !path)
+            throw ArgError("h3_check_weights: null argument");
+        const std::string problem = h3::CheckpointWeights(path).check(to_config(cfg));
+        if (message && cap) {
+            const size_t n = std::min<size_t>(problem.size(), cap - 1);
+            std::memcpy(message, problem.data(), n);
+            message[n] = '\0';
+        }
+        if (!problem.empty())
+            throw ArgError("h3_check_weights: " + std::string(path) + ": " + problem);
     });
 }
 

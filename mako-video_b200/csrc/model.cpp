@@ -14,8 +14,10 @@
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <filesystem>
 #include <map>
 #include <sstream>
+#include <stdexcept>
 
 namespace h3 {
 
@@ -312,13 +314,253 @@ struct Model::Impl {
             throw CudaError(std::string("NCCL: ") + #x + ": " + ncclGetErrorString(r_));                                  \
     } while (0)
 
+// ------------------------------------------------------------------------------------------------ weights
+
+std::vector<WeightSpec> weight_specs(const Config& c)
+{
+    const int64_t d = c.dim, inner = c.inner(), F = c.ffn, td = c.time_dim;
+    const bool pruned = c.curve > 0;
+    const int64_t ka = pruned ? c.curve : td; // the AdaLN projections' input width
+    std::vector<WeightSpec> w;
+    auto add = [&](std::string name, std::vector<int64_t> shape, bool bf16, uint32_t id, float mean, float stdev, int owner = 0,
+                   int index = -1) {
+        WeightSpec sp;
+        sp.name = std::move(name), sp.shape = std::move(shape), sp.bf16 = bf16, sp.id = id, sp.mean = mean, sp.stdev = stdev;
+        sp.owner = owner, sp.index = index;
+        w.push_back(std::move(sp));
+    };
+    // model-level weights: the names the reference's own files and prose use where they give one (time_embedder.*,
+    // blocks.N.adaln_proj.linear.*, adaln_t_table: tools/check_pruned_curve.py:43-56; condition_proj, video_patch_proj,
+    // audio_patch_proj, proj_out: docs/architecture.md:26-31,115), this build's names elsewhere
+    if (!pruned) {
+        add("time_embedder.proj_in.weight", {d, 256}, false, kTInW, 0.f, kStd);
+        add("time_embedder.proj_in.bias", {d}, false, kTInB, 0.f, kStd);
+        add("time_embedder.proj_out.weight", {td, d}, false, kTOutW, 0.f, kStd);
+        add("time_embedder.proj_out.bias", {td}, false, kTOutB, 0.f, kStd);
+    } else {
+        add("adaln_t_table", {1025, int64_t(c.curve)}, false, kCurveTable, 0.f, kCurveStd);
+    }
+    add("video_patch_proj.weight", {d, int64_t(c.video_patch)}, true, kVpW, 0.f, kStd);
+    add("video_patch_proj.bias", {d}, false, kVpB, 0.f, kStd);
+    add("audio_patch_proj.weight", {d, int64_t(c.audio_channels)}, true, kApW, 0.f, kStd);
+    add("audio_patch_proj.bias", {d}, false, kApB, 0.f, kStd);
+    add("condition_proj.weight", {d, int64_t(c.text_dim)}, true, kCondW, 0.f, kStd);
+    add("condition_proj.bias", {d}, false, kCondB, 0.f, kStd);
+    add("norm_out.adaln_proj.weight", {2 * d, ka}, !pruned, kFadaW, 0.f, kStd);
+    add("norm_out.adaln_proj.bias", {2 * d}, false, kFadaB, 0.f, kStd);
+    add("proj_out.weight", {int64_t(c.video_patch), d}, false, kHvW, 0.f, kStd);
+    add("proj_out.bias", {int64_t(c.video_patch)}, false, kHvB, 0.f, kStd);
+    add("audio_proj_out.weight", {int64_t(c.audio_channels), d}, false, kHaW, 0.f, kStd);
+    add("audio_proj_out.bias", {int64_t(c.audio_channels)}, false, kHaB, 0.f, kStd);
+    auto block = [&](int owner, int index, uint32_t base) {
+        const std::string p = (owner == 1 ? "blocks." : "token_refiner.blocks.") + std::to_string(index) + ".";
+        if (owner == 1) {
+            add(p + "adaln_proj.linear.weight", {18 * d, ka}, !pruned, base + kAdaW, 0.f, kStd, owner, index);
+            add(p + "adaln_proj.linear.bias", {18 * d}, false, base + kAdaB, 0.f, kStd, owner, index);
+        }
+        add(p + "norm1.weight", {d}, false, base + kNorm1, 1.f, kStd, owner, index);
+        add(p + "attn.qkv.weight", {3 * inner, d}, true, base + kQkvW, 0.f, kStd, owner, index);
+        add(p + "attn.qkv.bias", {3 * inner}, false, base + kQkvB, 0.f, kStd, owner, index);
+        add(p + "attn.norm_q.weight", {128}, false, base + kQn, 1.f, kStd, owner, index);
+        add(p + "attn.norm_k.weight", {128}, false, base + kKn, 1.f, kStd, owner, index);
+        add(p + "attn.to_out.weight", {d, inner}, true, base + kOutW, 0.f, kStd, owner, index);
+        add(p + "attn.to_out.bias", {d}, false, base + kOutB, 0.f, kStd, owner, index);
+        add(p + "norm2.weight", {d}, false, base + kNorm2, 1.f, kStd, owner, index);
+        add(p + "ff.fc1.weight", {2 * F, d}, true, base + kFc1W, 0.f, kStd, owner, index);
+        add(p + "ff.fc1.bias", {2 * F}, false, base + kFc1B, 0.f, kStd, owner, index);
+        add(p + "ff.fc2.weight", {d, F}, true, base + kFc2W, 0.f, kStd, owner, index);
+        add(p + "ff.fc2.bias", {d}, false, base + kFc2B, 0.f, kStd, owner, index);
+    };
+    for (int l = 0; l < c.blocks; ++l)
+        block(1, l, kBlockBase + kBlockStride * l);
+    for (int r = 0; r < c.refiner; ++r)
+        block(2, r, kRefinerBase + kBlockStride * r);
+    if (c.refiner > 0)
+        add("token_refiner.norm.weight", {d}, false, kRefinerNorm, 1.f, kStd);
+    return w;
+}
+
+void SyntheticWeights::get(const WeightSpec& spec, void* dst, cudaStream_t s)
+{
+    fill_synthetic(dst, spec.bf16, spec.count(), seed_, spec.id, spec.mean, spec.stdev, s);
+}
+
+struct CheckpointWeights::Files {
+    std::vector<std::unique_ptr<SafeTensors>> files;
+    std::vector<bool> interleaved;       // per file: metadata qkv_layout = interleaved
+    std::map<std::string, size_t> where; // tensor name -> file
+};
+
+CheckpointWeights::CheckpointWeights(const std::string& path) : f_(new Files)
+{
+    std::vector<std::string> paths;
+    std::error_code ec;
+    if (std::filesystem::is_directory(path, ec)) {
+        for (const auto& e : std::filesystem::directory_iterator(path, ec))
+            if (e.is_regular_file(ec) && e.path().extension() == ".safetensors")
+                paths.push_back(e.path().string());
+        std::sort(paths.begin(), paths.end());
+        if (paths.empty())
+            throw std::invalid_argument("checkpoint: no .safetensors file in " + path);
+    } else {
+        paths.push_back(path);
+    }
+    for (const std::string& p : paths) {
+        std::unique_ptr<SafeTensors> st;
+        try {
+            st = std::make_unique<SafeTensors>(p);
+        } catch (const std::runtime_error& e) {
+            throw std::invalid_argument(std::string("checkpoint: ") + e.what());
+        }
+        const auto it = st->metadata().find("qkv_layout");
+        f_->interleaved.push_back(it != st->metadata().end() && it->second == "interleaved");
+        for (const auto& [name, t] : st->tensors())
+            if (!f_->where.emplace(name, f_->files.size()).second)
+                throw std::invalid_argument("checkpoint: tensor " + name + " appears in two files");
+        f_->files.push_back(std::move(st));
+    }
+}
+
+CheckpointWeights::~CheckpointWeights() = default;
+
+std::string CheckpointWeights::check(const Config& c) const
+{
+    for (const WeightSpec& sp : weight_specs(c)) {
+        const auto it = f_->where.find(sp.name);
+        if (it == f_->where.end())
+            return "no tensor " + sp.name;
+        const SafeTensor& t = f_->files[it->second]->tensors().at(sp.name);
+        if (t.shape != sp.shape) {
+            std::string got, want;
+            for (int64_t v : t.shape)
+                got += (got.empty() ? "" : "x") + std::to_string(v);
+            for (int64_t v : sp.shape)
+                want += (want.empty() ? "" : "x") + std::to_string(v);
+            return sp.name + " is " + got + ", this model needs " + want;
+        }
+        if (t.dtype != "BF16" && t.dtype != "F16" && t.dtype != "F32")
+            return sp.name + " has dtype " + t.dtype + " (BF16, F16 or F32 expected)";
+    }
+    return "";
+}
+
+void CheckpointWeights::get(const WeightSpec& spec, void* dst, cudaStream_t s)
+{
+    const auto it = f_->where.find(spec.name);
+    if (it == f_->where.end())
+        throw std::invalid_argument("checkpoint: no tensor " + spec.name);
+    const SafeTensors& st = *f_->files[it->second];
+    if (st.tensors().at(spec.name).shape != spec.shape)
+        throw std::invalid_argument("checkpoint: " + spec.name + " has another shape than this model's");
+    const size_t esz = spec.bf16 ? 2 : 4;
+    std::vector<unsigned char> host(spec.count() * esz);
+    if (spec.bf16) {
+        const std::vector<uint16_t> v = st.read_bf16(spec.name);
+        std::memcpy(host.data(), v.data(), host.size());
+    } else {
+        const std::vector<float> v = st.read_f32(spec.name);
+        std::memcpy(host.data(), v.data(), host.size());
+    }
+    const bool qkv = spec.name.size() > 15 && (spec.name.compare(spec.name.size() - 15, 15, "attn.qkv.weight") == 0 ||
+                                                spec.name.compare(spec.name.size() - 13, 13, "attn.qkv.bias") == 0);
+    if (qkv && f_->interleaved[it->second]) {
+        // [q_h; k_h; v_h] for every head h -> [q (all heads); k; v]
+        const int64_t rows = spec.shape[0], cols = spec.shape.size() > 1 ? spec.shape[1] : 1, inner = rows / 3;
+        const size_t row_bytes = size_t(cols) * esz;
+        std::vector<unsigned char> stacked(host.size());
+        for (int64_t h = 0; h < inner / 128; ++h)
+            for (int p = 0; p < 3; ++p)
+                for (int r = 0; r < 128; ++r)
+                    std::memcpy(&stacked[size_t(p * inner + h * 128 + r) * row_bytes], &host[size_t(h * 384 + p * 128 + r) * row_bytes], row_bytes);
+        host.swap(stacked);
+    }
+    H3_CUDA(cudaMemcpyAsync(dst, host.data(), host.size(), cudaMemcpyHostToDevice, s));
+    H3_CUDA(cudaStreamSynchronize(s)); // the host copy goes out of scope
+}
+
 Model::Model(const Config& c, uint64_t seed, uint32_t int8_mask, const World& world)
     : d_(new Impl), c_(c), world_(world), int8_(int8_mask)
 {
+    SyntheticWeights src(seed);
+    init(src);
+}
+
+Model::Model(const Config& c, WeightSource& src, uint32_t int8_mask, const World& world)
+    : d_(new Impl), c_(c), world_(world), int8_(int8_mask)
+{
+    init(src);
+}
+
+// Where a weight lives on the device and how its logical layout maps onto the stored one.
+struct Model::Target {
+    enum Mode { plain, audio_padded, fc1_rows, fc1_bias, curve } mode = plain;
+    DevBuf* buf = nullptr;
+    size_t offset = 0; // bytes into buf (plain: the AdaLN projections of all blocks share one buffer)
+};
+
+Model::Target Model::locate(const WeightSpec& sp)
+{
+    const int d = c_.dim;
+    const size_t ka = c_.curve ? size_t(c_.curve) : size_t(c_.time_dim);
+    Target t;
+    if (sp.owner == 0) {
+        switch (sp.id) {
+        case kTInW: t.buf = &d_->t_in_w; break;
+        case kTInB: t.buf = &d_->t_in_b; break;
+        case kTOutW: t.buf = &d_->t_out_w; break;
+        case kTOutB: t.buf = &d_->t_out_b; break;
+        case kCurveTable: t.mode = Target::curve; break;
+        case kVpW: t.buf = &d_->vp_w; break;
+        case kVpB: t.buf = &d_->vp_b; break;
+        case kApW: t.buf = &d_->ap_w, t.mode = Target::audio_padded; break;
+        case kApB: t.buf = &d_->ap_b; break;
+        case kCondW: t.buf = &d_->cond_w; break;
+        case kCondB: t.buf = &d_->cond_b; break;
+        case kFadaW: t.buf = &d_->fada_w; break;
+        case kFadaB: t.buf = &d_->fada_b; break;
+        case kHvW: t.buf = &d_->hv_w; break;
+        case kHvB: t.buf = &d_->hv_b; break;
+        case kHaW: t.buf = &d_->ha_w; break;
+        case kHaB: t.buf = &d_->ha_b; break;
+        case kRefinerNorm: t.buf = &d_->refiner_norm; break;
+        default: throw CudaError("weights: unknown tensor " + sp.name);
+        }
+        return t;
+    }
+    Impl::Block& B = sp.owner == 1 ? d_->blocks.at(sp.index) : d_->refiner.at(sp.index);
+    const uint32_t local = sp.id - (sp.owner == 1 ? kBlockBase : kRefinerBase) - kBlockStride * uint32_t(sp.index);
+    switch (local) {
+    case kAdaW: t.buf = &d_->ada_w, t.offset = size_t(sp.index) * 18 * d * ka * (c_.curve ? 4 : 2); break;
+    case kAdaB: t.buf = &d_->ada_b, t.offset = size_t(sp.index) * 18 * d * 4; break;
+    case kNorm1: t.buf = &B.norm1; break;
+    case kQkvW: t.buf = &B.qkv_w; break;
+    case kQkvB: t.buf = &B.qkv_b; break;
+    case kQn: t.buf = &B.qn; break;
+    case kKn: t.buf = &B.kn; break;
+    case kOutW: t.buf = &B.out_w; break;
+    case kOutB: t.buf = &B.out_b; break;
+    case kNorm2: t.buf = &B.norm2; break;
+    case kFc1W: t.buf = &B.fc1_w, t.mode = Target::fc1_rows; break;
+    case kFc1B: t.buf = &B.fc1_b, t.mode = Target::fc1_bias; break;
+    case kFc2W: t.buf = &B.fc2_w; break;
+    case kFc2B: t.buf = &B.fc2_b; break;
+    default: throw CudaError("weights: unknown tensor " + sp.name);
+    }
+    return t;
+}
+
+void Model::init(WeightSource& src)
+{
+    const Config& c = c_;
+    const World& world = world_;
     if (c.dim % 256 || c.inner() % 256 || c.ffn % 128 || (2 * c.ffn) % 256 || c.time_dim % 8 || c.text_dim % 8 || c.dim > 8192)
         throw CudaError("config: dim and heads*128 multiples of 256, ffn of 128, time_dim and text_dim of 8, dim <= 8192");
     if (world.size < 1 || world.rank < 0 || world.rank >= world.size || c.heads % world.size)
         throw CudaError("world: heads must divide evenly over the ranks");
+    if (c.curve != 0 && c.curve != 8)
+        throw CudaError("config: curve_dims is 0 or 8");
+    if (c.refiner < 0 || c.refiner > 2)
+        throw CudaError("config: at most 2 token refiner blocks");
     H3_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
     if (world.size > 1) {
         if (world.size > 8)
@@ -330,84 +572,67 @@ Model::Model(const Config& c, uint64_t seed, uint32_t int8_mask, const World& wo
         const char* ex = std::getenv("H3_EXCHANGE");
         d_->fused = !(ex && std::string(ex) == "nccl");
     }
-    const int d = c.dim, L = c.blocks, inner = c.inner(), F = c.ffn, td = c.time_dim;
+    const int d = c.dim, L = c.blocks, inner = c.inner(), F = c.ffn;
+    const size_t ka = c.curve ? size_t(c.curve) : size_t(c.time_dim);
     cudaStream_t s = stream_;
-    auto fill = [&](DevBuf& b, size_t n, bool bf16, uint32_t id, float mean, float stdev) {
-        b.ensure(n * (bf16 ? 2 : 4));
-        fill_synthetic(b.p, bf16, n, seed, id, mean, stdev, s);
-    };
-    const bool pruned = c.curve > 0;
-    if (c.curve != 0 && c.curve != 8)
-        throw CudaError("config: curve_dims is 0 or 8");
-    const int ka = pruned ? c.curve : td; // the AdaLN projections' input width
-    if (!pruned) {
-        fill(d_->t_in_w, size_t(d) * 256, false, kTInW, 0.f, kStd);
-        fill(d_->t_in_b, d, false, kTInB, 0.f, kStd);
-        fill(d_->t_out_w, size_t(td) * d, false, kTOutW, 0.f, kStd);
-        fill(d_->t_out_b, td, false, kTOutB, 0.f, kStd);
-    } else {
-        // adaln_t_table [1025][8]: generated on the device like every weight, kept on the host for the per-step lookup
-        DevBuf tab;
-        fill(tab, size_t(1025) * c.curve, false, kCurveTable, 0.f, kCurveStd);
-        d_->curve_table.resize(size_t(1025) * c.curve);
-        H3_CUDA(cudaMemcpyAsync(d_->curve_table.data(), tab.p, d_->curve_table.size() * 4, cudaMemcpyDeviceToHost, s));
-        H3_CUDA(cudaStreamSynchronize(s));
-    }
-    fill(d_->vp_w, size_t(d) * c.video_patch, true, kVpW, 0.f, kStd);
-    fill(d_->vp_b, d, false, kVpB, 0.f, kStd);
-    fill(d_->ap_w, size_t(d) * 64, true, kApW, 0.f, 0.f); // padded to 64 inputs; the first 32 columns filled below
-    {
-        DevBuf tmp;
-        fill(tmp, size_t(d) * c.audio_channels, true, kApW, 0.f, kStd);
-        H3_CUDA(cudaMemcpy2DAsync(d_->ap_w.p, 64 * 2, tmp.p, c.audio_channels * 2, c.audio_channels * 2, d, cudaMemcpyDeviceToDevice, s));
-        H3_CUDA(cudaStreamSynchronize(s));
-    }
-    fill(d_->ap_b, d, false, kApB, 0.f, kStd);
-    fill(d_->cond_w, size_t(d) * c.text_dim, true, kCondW, 0.f, kStd);
-    fill(d_->cond_b, d, false, kCondB, 0.f, kStd);
-    fill(d_->fada_w, size_t(2) * d * ka, !pruned, kFadaW, 0.f, kStd);
-    fill(d_->fada_b, size_t(2) * d, false, kFadaB, 0.f, kStd);
-    fill(d_->hv_w, size_t(c.video_patch) * d, false, kHvW, 0.f, kStd);
-    fill(d_->hv_b, c.video_patch, false, kHvB, 0.f, kStd);
-    fill(d_->ha_w, size_t(c.audio_channels) * d, false, kHaW, 0.f, kStd);
-    fill(d_->ha_b, c.audio_channels, false, kHaB, 0.f, kStd);
-    // AdaLN projections of every block in one tensor (one GEMV reads them all): block l at offset l * 18 d * td.
-    d_->ada_w.ensure(size_t(L) * 18 * d * ka * (pruned ? 4 : 2));
-    d_->ada_b.ensure(size_t(L) * 18 * d * 4);
     d_->blocks.resize(L);
-    for (int l = 0; l < L; ++l) {
-        const uint32_t base = kBlockBase + kBlockStride * l;
-        fill_synthetic(d_->ada_w.as<uint8_t>() + size_t(l) * 18 * d * ka * (pruned ? 4 : 2), !pruned, size_t(18) * d * ka, seed, base + kAdaW,
-                       0.f, kStd, s);
-        fill_synthetic(d_->ada_b.as<float>() + size_t(l) * 18 * d, 0, size_t(18) * d, seed, base + kAdaB, 0.f, kStd, s);
-        Impl::Block& b = d_->blocks[l];
-        fill(b.norm1, d, false, base + kNorm1, 1.f, kStd);
-        fill(b.qkv_w, size_t(3) * inner * d, true, base + kQkvW, 0.f, kStd);
-        fill(b.qkv_b, size_t(3) * inner, false, base + kQkvB, 0.f, kStd);
-        fill(b.qn, 128, false, base + kQn, 1.f, kStd);
-        fill(b.kn, 128, false, base + kKn, 1.f, kStd);
-        fill(b.out_w, size_t(d) * inner, true, base + kOutW, 0.f, kStd);
-        fill(b.out_b, d, false, base + kOutB, 0.f, kStd);
-        fill(b.norm2, d, false, base + kNorm2, 1.f, kStd);
-        {
-            // fc1 as stored ([gate; value] rows), then regrouped for the fused SwiGLU epilogue.
-            DevBuf w, bias;
-            fill(w, size_t(2) * F * d, true, base + kFc1W, 0.f, kStd);
-            fill(bias, size_t(2) * F, false, base + kFc1B, 0.f, kStd);
-            b.fc1_w.ensure(size_t(2) * F * d * 2);
-            b.fc1_b.ensure(size_t(2) * F * 4);
-            interleave_gate_value(w.p, F, d, b.fc1_w.p, s);
-            interleave_gate_value_f32(bias.as<float>(), F, b.fc1_b.as<float>(), s);
+    d_->refiner.resize(c.refiner);
+    // the AdaLN projections of every block in one tensor (one GEMV reads them all): block l at offset l * 18 d ka
+    d_->ada_w.ensure(size_t(L) * 18 * d * ka * (c.curve ? 4 : 2));
+    d_->ada_b.ensure(size_t(L) * 18 * d * 4);
+    d_->ap_w.ensure(size_t(d) * 64 * 2); // zeroed: padded to 64 inputs, the first 32 columns set below
+    for (const WeightSpec& sp : weight_specs(c)) {
+        const Target t = locate(sp);
+        const size_t bytes = sp.count() * (sp.bf16 ? 2 : 4);
+        switch (t.mode) {
+        case Target::plain:
+            if (t.buf != &d_->ada_w && t.buf != &d_->ada_b)
+                t.buf->ensure(bytes);
+            src.get(sp, t.buf->as<uint8_t>() + t.offset, s);
+            break;
+        case Target::audio_padded: {
+            DevBuf tmp;
+            tmp.ensure(bytes);
+            src.get(sp, tmp.p, s);
+            H3_CUDA(cudaMemcpy2DAsync(t.buf->p, 64 * 2, tmp.p, size_t(c.audio_channels) * 2, size_t(c.audio_channels) * 2, d,
+                                      cudaMemcpyDeviceToDevice, s));
             H3_CUDA(cudaStreamSynchronize(s));
+            break;
         }
-        fill(b.fc2_w, size_t(d) * F, true, base + kFc2W, 0.f, kStd);
-        fill(b.fc2_b, d, false, base + kFc2B, 0.f, kStd);
+        case Target::fc1_rows:
+        case Target::fc1_bias: {
+            // stored as [gate; value]; regrouped into 128-row [gate g; value g] pairs for the fused SwiGLU epilogue
+            DevBuf tmp;
+            tmp.ensure(bytes);
+            src.get(sp, tmp.p, s);
+            t.buf->ensure(bytes);
+            if (t.mode == Target::fc1_rows)
+                interleave_gate_value(tmp.p, F, d, t.buf->p, s);
+            else
+                interleave_gate_value_f32(tmp.as<float>(), F, t.buf->as<float>(), s);
+            H3_CUDA(cudaStreamSynchronize(s));
+            break;
+        }
+        case Target::curve: {
+            // adaln_t_table: kept on the host for the per-step lookup
+            DevBuf tab;
+            tab.ensure(bytes);
+            src.get(sp, tab.p, s);
+            d_->curve_table.resize(sp.count());
+            H3_CUDA(cudaMemcpyAsync(d_->curve_table.data(), tab.p, bytes, cudaMemcpyDeviceToHost, s));
+            H3_CUDA(cudaStreamSynchronize(s));
+            break;
+        }
+        }
+    }
+    // int8 at load: the chosen projections' rows quantised per row; their bf16 rows released
+    for (Impl::Block& b : d_->blocks) {
         auto quant = [&](DevBuf& w, DevBuf& q, DevBuf& sc, int rows, int K) {
             q.ensure(size_t(rows) * K);
             sc.ensure(size_t(rows) * 4);
             quant_weight_rows(w.p, rows, K, q.as<int8_t>(), sc.as<float>(), s);
             H3_CUDA(cudaStreamSynchronize(s));
-            w.release(); // the int8 rows replace the bf16 ones
+            w.release();
         };
         if (int8_ & kInt8Qkv)
             quant(b.qkv_w, b.qkv_q, b.qkv_s, 3 * inner, d);
@@ -418,36 +643,55 @@ Model::Model(const Config& c, uint64_t seed, uint32_t int8_mask, const World& wo
         if (int8_ & kInt8Fc2)
             quant(b.fc2_w, b.fc2_q, b.fc2_s, d, F);
     }
-    if (c.refiner < 0 || c.refiner > 2)
-        throw CudaError("config: at most 2 token refiner blocks");
-    d_->refiner.resize(c.refiner);
-    for (int r = 0; r < c.refiner; ++r) {
-        const uint32_t base = kRefinerBase + kBlockStride * r;
-        Impl::Block& b = d_->refiner[r];
-        fill(b.norm1, d, false, base + kNorm1, 1.f, kStd);
-        fill(b.qkv_w, size_t(3) * inner * d, true, base + kQkvW, 0.f, kStd);
-        fill(b.qkv_b, size_t(3) * inner, false, base + kQkvB, 0.f, kStd);
-        fill(b.qn, 128, false, base + kQn, 1.f, kStd);
-        fill(b.kn, 128, false, base + kKn, 1.f, kStd);
-        fill(b.out_w, size_t(d) * inner, true, base + kOutW, 0.f, kStd);
-        fill(b.out_b, d, false, base + kOutB, 0.f, kStd);
-        fill(b.norm2, d, false, base + kNorm2, 1.f, kStd);
-        DevBuf w, bias;
-        fill(w, size_t(2) * F * d, true, base + kFc1W, 0.f, kStd);
-        fill(bias, size_t(2) * F, false, base + kFc1B, 0.f, kStd);
-        b.fc1_w.ensure(size_t(2) * F * d * 2);
-        b.fc1_b.ensure(size_t(2) * F * 4);
-        interleave_gate_value(w.p, F, d, b.fc1_w.p, s);
-        interleave_gate_value_f32(bias.as<float>(), F, b.fc1_b.as<float>(), s);
-        H3_CUDA(cudaStreamSynchronize(s));
-        fill(b.fc2_w, size_t(d) * F, true, base + kFc2W, 0.f, kStd);
-        fill(b.fc2_b, d, false, base + kFc2B, 0.f, kStd);
-    }
-    if (c.refiner > 0)
-        fill(d_->refiner_norm, d, false, kRefinerNorm, 1.f, kStd);
     H3_CUDA(cudaStreamSynchronize(s));
     if (take_device_error(s))
         throw CudaError("device error during weight set-up");
+}
+
+void Model::save(const std::string& path)
+{
+    if (int8_)
+        throw std::invalid_argument("save: an int8 model no longer holds the bf16 rows of its quantised projections; save a bf16 model");
+    const std::vector<WeightSpec> specs = weight_specs(c_);
+    std::vector<SafeTensorOut> outs;
+    for (const WeightSpec& sp : specs) {
+        SafeTensorOut o;
+        o.name = sp.name, o.dtype = sp.bf16 ? "BF16" : "F32", o.shape = sp.shape, o.bytes = sp.count() * (sp.bf16 ? 2 : 4);
+        outs.push_back(std::move(o));
+    }
+    cudaStream_t s = stream_;
+    const int d = c_.dim, F = c_.ffn;
+    const std::map<std::string, std::string> meta = {{"format", "pt"}, {"qkv_layout", "stacked"}, {"writer", "libh3b200"}};
+    write_safetensors(path, outs, meta, [&](size_t i, std::vector<unsigned char>& buf) {
+        const WeightSpec& sp = specs[i];
+        const Target t = locate(sp);
+        switch (t.mode) {
+        case Target::plain:
+            H3_CUDA(cudaMemcpyAsync(buf.data(), t.buf->as<uint8_t>() + t.offset, buf.size(), cudaMemcpyDeviceToHost, s));
+            break;
+        case Target::audio_padded:
+            H3_CUDA(cudaMemcpy2DAsync(buf.data(), size_t(c_.audio_channels) * 2, t.buf->p, 64 * 2, size_t(c_.audio_channels) * 2, d,
+                                      cudaMemcpyDeviceToHost, s));
+            break;
+        case Target::fc1_rows:
+        case Target::fc1_bias: {
+            // back from the 128-row [gate g; value g] pairs to [gate; value]
+            std::vector<unsigned char> stored(buf.size());
+            H3_CUDA(cudaMemcpyAsync(stored.data(), t.buf->p, stored.size(), cudaMemcpyDeviceToHost, s));
+            H3_CUDA(cudaStreamSynchronize(s));
+            const size_t row = t.mode == Target::fc1_rows ? size_t(d) * 2 : 4;
+            for (int i = 0; i < 2 * F; ++i) {
+                const int r = i < F ? (i / 128) * 256 + i % 128 : ((i - F) / 128) * 256 + 128 + (i - F) % 128;
+                std::memcpy(&buf[size_t(i) * row], &stored[size_t(r) * row], row);
+            }
+            break;
+        }
+        case Target::curve:
+            std::memcpy(buf.data(), d_->curve_table.data(), buf.size());
+            break;
+        }
+        H3_CUDA(cudaStreamSynchronize(s));
+    });
 }
 
 Model::~Model()

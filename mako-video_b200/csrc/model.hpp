@@ -103,8 +103,68 @@ enum Int8Mask : uint32_t { kInt8Qkv = 1, kInt8Out = 2, kInt8Fc1 = 4, kInt8Fc2 = 
 // "none", "all" or a comma list of qkv, out, fc1, fc2; false when the text is not one of these.
 bool parse_int8(const std::string& s, uint32_t& mask);
 
+// One named weight of the model in its logical layout (as a checkpoint stores it): fc1 [gate; value] rows, q/k/v
+// stacked q, k, v, the audio projection 32 inputs wide. Its name in a checkpoint, shape, element type, and the tensor
+// id and distribution of the synthetic generator.
+struct WeightSpec {
+    std::string name;
+    std::vector<int64_t> shape;
+    bool bf16 = false;
+    uint32_t id = 0;
+    float mean = 0.f, stdev = 0.02f;
+    int owner = 0;  // 0 the model, 1 a block, 2 a token refiner block
+    int index = -1; // the block or refiner block
+    uint64_t count() const
+    {
+        uint64_t n = 1;
+        for (int64_t v : shape)
+            n *= uint64_t(v);
+        return n;
+    }
+};
+
+// Every weight of a model of this shape, in the order they are set up and saved.
+std::vector<WeightSpec> weight_specs(const Config& c);
+
+// Where a model's weights come from: spec's values, in its logical layout and element type, written to device memory.
+class WeightSource {
+public:
+    virtual ~WeightSource() = default;
+    virtual void get(const WeightSpec& spec, void* dst, cudaStream_t s) = 0;
+};
+
+// Random-init weights: value i of a tensor = mean + stdev * a hash of (seed, tensor id, i) (fill_synthetic).
+class SyntheticWeights : public WeightSource {
+public:
+    explicit SyntheticWeights(uint64_t seed) : seed_(seed) {}
+    void get(const WeightSpec& spec, void* dst, cudaStream_t s) override;
+
+private:
+    uint64_t seed_;
+};
+
+// A checkpoint: one safetensors file, or a directory of them. Tensors are found by the names weight_specs gives,
+// checked against the expected shape, and converted to the weight's element type (BF16, F16 or F32 sources). A file
+// whose metadata says qkv_layout = interleaved stores each head's q, k and v rows together ([q_h; k_h; v_h] for head
+// h), as the reference's shards do (docs/architecture.md:62-63); they are stacked q, k, v at load (its upload_qkv).
+class CheckpointWeights : public WeightSource {
+public:
+    explicit CheckpointWeights(const std::string& path);
+    ~CheckpointWeights() override;
+    void get(const WeightSpec& spec, void* dst, cudaStream_t s) override;
+    // The first problem a model of shape c would meet loading this checkpoint ("" if none): a missing tensor or a
+    // shape that disagrees. Host only.
+    std::string check(const Config& c) const;
+
+private:
+    struct Files;
+    std::unique_ptr<Files> f_;
+};
+
 class Model {
 public:
+    // Weights from `src` (synthetic or a checkpoint); the int8_mask's projections are quantised per row at load.
+    Model(const Config& c, WeightSource& src, uint32_t int8_mask, const World& world);
     // Synthetic weights from `seed` (every value a hash of seed, tensor and index; see fill_synthetic).
     Model(const Config& c, uint64_t seed, uint32_t int8_mask, const World& world);
     ~Model();
@@ -143,6 +203,11 @@ public:
     };
     LoraResult add_lora(const std::string& path, float scale, bool strict);
 
+    // Writes every weight to a safetensors file under the names of weight_specs, in the logical layout (metadata
+    // qkv_layout = stacked), such that a model created from it is this one. bf16 models only (the int8 rows replace
+    // the bf16 ones).
+    void save(const std::string& path);
+
     const Config& config() const { return c_; }
     const Layout& layout() const { return layout_; }
     int rows() const { return S_; }
@@ -171,6 +236,9 @@ private:
     bool begun_ = false;
     void alloc_activations();
     void refine_text(int T); // the token refiner over x_text (begin)
+    void init(WeightSource& src); // the constructors' body: checks, stream, communicator, weights
+    struct Target;
+    Target locate(const WeightSpec& sp); // where a weight lives on the device
     void map_peers(); // the ranks' receive buffers, mapped into every rank (sequence-parallel, fused exchange)
     // Copies a device tensor to the host and hands it to the probe; with `rows` set it is [S][n / S] in the packed row
     // order and is handed over in the layout's row order.

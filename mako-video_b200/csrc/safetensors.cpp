@@ -243,12 +243,13 @@ SafeTensors::SafeTensors(const std::string& path) : path_(path)
     }
 }
 
-std::vector<float> SafeTensors::read_f32(const std::string& name) const
+std::vector<unsigned char> SafeTensors::read_raw(const std::string& name, const SafeTensor*& tp) const
 {
     const auto it = tensors_.find(name);
     if (it == tensors_.end())
         throw std::runtime_error("safetensors: " + path_ + " has no tensor " + name);
     const SafeTensor& t = it->second;
+    tp = &t;
     uint64_t count = 1;
     for (int64_t d : t.shape)
         count *= uint64_t(d);
@@ -262,6 +263,96 @@ std::vector<float> SafeTensors::read_f32(const std::string& name) const
     f.seekg(std::streamoff(data_offset_ + t.begin));
     if (!f.read(reinterpret_cast<char*>(raw.data()), std::streamsize(raw.size())))
         throw std::runtime_error("safetensors: " + path_ + ": cannot read tensor " + name);
+    return raw;
+}
+
+uint16_t bf16_bits(float f)
+{
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    if ((u & 0x7F800000u) == 0x7F800000u && (u & 0x007FFFFFu))
+        return uint16_t((u >> 16) | 0x40); // NaN stays a (quiet) NaN
+    u += 0x7FFFu + ((u >> 16) & 1u);
+    return uint16_t(u >> 16);
+}
+
+std::vector<uint16_t> SafeTensors::read_bf16(const std::string& name) const
+{
+    const SafeTensor* t = nullptr;
+    const std::vector<unsigned char> raw = read_raw(name, t);
+    if (t->dtype == "BF16") {
+        std::vector<uint16_t> out(raw.size() / 2);
+        std::memcpy(out.data(), raw.data(), raw.size());
+        return out;
+    }
+    const std::vector<float> f = read_f32(name);
+    std::vector<uint16_t> out(f.size());
+    for (size_t i = 0; i < f.size(); ++i)
+        out[i] = bf16_bits(f[i]);
+    return out;
+}
+
+void write_safetensors(const std::string& path, const std::vector<SafeTensorOut>& tensors,
+                       const std::map<std::string, std::string>& metadata,
+                       const std::function<void(size_t, std::vector<unsigned char>&)>& data)
+{
+    auto quote = [](const std::string& v) {
+        std::string q = "\"";
+        for (char ch : v) {
+            if (ch == '"' || ch == '\\')
+                q += '\\';
+            q += ch;
+        }
+        return q + "\"";
+    };
+    std::string h = "{";
+    if (!metadata.empty()) {
+        h += "\"__metadata__\":{";
+        bool first = true;
+        for (const auto& [k, v] : metadata) {
+            h += (first ? "" : ",") + quote(k) + ":" + quote(v);
+            first = false;
+        }
+        h += "}";
+    }
+    uint64_t off = 0;
+    for (size_t i = 0; i < tensors.size(); ++i) {
+        const SafeTensorOut& t = tensors[i];
+        h += (i || !metadata.empty() ? "," : "") + quote(t.name) + ":{\"dtype\":" + quote(t.dtype) + ",\"shape\":[";
+        for (size_t k = 0; k < t.shape.size(); ++k)
+            h += (k ? "," : "") + std::to_string(t.shape[k]);
+        h += "],\"data_offsets\":[" + std::to_string(off) + "," + std::to_string(off + t.bytes) + "]}";
+        off += t.bytes;
+    }
+    h += "}";
+    while (h.size() % 8)
+        h += ' ';
+    std::ofstream f(path, std::ios::binary | std::ios::trunc);
+    if (!f)
+        throw std::runtime_error("safetensors: cannot create " + path);
+    unsigned char len8[8];
+    uint64_t n = h.size();
+    for (int i = 0; i < 8; ++i, n >>= 8)
+        len8[i] = static_cast<unsigned char>(n & 0xFF);
+    f.write(reinterpret_cast<const char*>(len8), 8);
+    f.write(h.data(), std::streamsize(h.size()));
+    std::vector<unsigned char> buf;
+    for (size_t i = 0; i < tensors.size(); ++i) {
+        buf.assign(tensors[i].bytes, 0);
+        data(i, buf);
+        f.write(reinterpret_cast<const char*>(buf.data()), std::streamsize(buf.size()));
+    }
+    if (!f)
+        throw std::runtime_error("safetensors: writing " + path + " failed");
+}
+
+std::vector<float> SafeTensors::read_f32(const std::string& name) const
+{
+    const SafeTensor* tp = nullptr;
+    const std::vector<unsigned char> raw = read_raw(name, tp);
+    const SafeTensor& t = *tp;
+    const uint64_t esz = t.dtype == "F32" ? 4 : 2;
+    const uint64_t count = raw.size() / esz;
     std::vector<float> out(count);
     for (uint64_t i = 0; i < count; ++i) {
         if (esz == 4)

@@ -101,6 +101,9 @@ SIGNATURES = {
     "h3_sigmas": (ctypes.c_int, [_U32, _F, _P, _P]),
     "h3_add_lora": (ctypes.c_int, [_P, ctypes.c_char_p, _F, _I32, _P, _P]),
     "h3_lora_inspect": (ctypes.c_int, [ctypes.c_char_p, _P, _U64, _P, _P, _P]),
+    "h3_weight_specs": (ctypes.c_int, [ctypes.POINTER(h3_config), _P, _U64, _P]),
+    "h3_save_weights": (ctypes.c_int, [_P, ctypes.c_char_p]),
+    "h3_check_weights": (ctypes.c_int, [ctypes.POINTER(h3_config), ctypes.c_char_p, _P, _U64]),
     "h3k_wait_selftest": (ctypes.c_int, [_U64, _P]),
     "h3_denoise": (ctypes.c_int, [_P, _P, _U64, _P, _U64, _P, _P, _U32, PROGRESS_FN, _P, _P]),
     "h3_stream": (_P, [_P]),
@@ -272,14 +275,16 @@ class Model:
     """The transformer (h3_create / h3_begin / h3_step)."""
 
     def __init__(self, config="c1", seed=0, int8_mask=0, sparse_ratio=0.0, sparse_local=1, rank=0, world=1, nccl_id=None,
-                 device=0, eps=1e-6):
+                 device=0, eps=1e-6, weights=None):
+        """weights: a checkpoint path (safetensors file or directory); None for synthetic weights from `seed`."""
         self.cfg = make_config(config, eps)
         w = None
         if world > 1:
             w = h3_world(rank, world)
             ctypes.memmove(w.nccl_id, nccl_id, 128)
         self.h = ctypes.c_void_p()
-        check(lib().h3_create(ctypes.byref(self.cfg), f"synthetic:{seed}".encode(), int8_mask, sparse_ratio, sparse_local,
+        src = str(weights).encode() if weights is not None else f"synthetic:{seed}".encode()
+        check(lib().h3_create(ctypes.byref(self.cfg), src, int8_mask, sparse_ratio, sparse_local,
                               None if w is None else ctypes.byref(w), device, ctypes.byref(self.h)))
         self._probe_cb = None
         self.layout = None
@@ -294,6 +299,10 @@ class Model:
             self.close()
         except Exception:
             pass
+
+    def save_weights(self, path):
+        """h3_save_weights: every weight to a safetensors file that h3_create reads back."""
+        check(lib().h3_save_weights(self.h, str(path).encode()))
 
     def add_lora(self, path, scale=1.0, strict=True):
         """h3_add_lora: returns (merged, skipped) adapter counts."""
@@ -381,3 +390,26 @@ class Model:
 
         self._probe_cb = PROBE_FN(cb)
         check(lib().h3_set_probe(self.h, self._probe_cb, None))
+
+
+def weight_specs(config, eps=1e-6):
+    """h3_weight_specs: [(name, dtype, shape)] of every tensor a checkpoint for this shape holds (host only)."""
+    cfg = make_config(config, eps)
+    n = ctypes.c_uint32()
+    check(lib().h3_weight_specs(ctypes.byref(cfg), None, 0, ctypes.byref(n)))
+    buf = ctypes.create_string_buffer(1 << 22)
+    check(lib().h3_weight_specs(ctypes.byref(cfg), buf, len(buf), ctypes.byref(n)))
+    out = []
+    for line in buf.value.decode().splitlines():
+        name, dtype, shape = line.split()
+        out.append((name, dtype, tuple(int(v) for v in shape.split("x"))))
+    assert len(out) == n.value
+    return out
+
+
+def check_weights(config, path, eps=1e-6):
+    """h3_check_weights: "" when the checkpoint fits the shape, else its first problem (host only)."""
+    cfg = make_config(config, eps)
+    msg = ctypes.create_string_buffer(4096)
+    rc = lib().h3_check_weights(ctypes.byref(cfg), str(path).encode(), msg, len(msg))
+    return "" if rc == H3_OK else (msg.value.decode() or lib().h3_last_error().decode())

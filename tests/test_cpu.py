@@ -298,13 +298,49 @@ def test_packed_order_puts_each_cube_in_one_run(dims):
     assert order.tolist() == want
 
 
-def test_create_refuses_checkpoint_paths_without_touching_the_gpu():
+def test_create_refuses_a_missing_checkpoint_without_touching_the_gpu():
     L = h3b200.lib()
     cfg = h3b200.make_config("c1")
     h = ctypes.c_void_p()
     rc = L.h3_create(ctypes.byref(cfg), b"/models/minimax-h3/FL2VA/transformer", 0, 0.0, 1, None, 0, ctypes.byref(h))
     assert rc == h3b200.H3_ERR_ARG and not h.value
-    assert b"synthetic" in L.h3_last_error()
+    assert b"cannot open" in L.h3_last_error()
+
+
+def test_weight_specs_and_checkpoint_checks(tmp_path):
+    """The tensors a checkpoint holds (h3_weight_specs), and h3_check_weights on a file with all of them, on a
+    directory of two shards, and with one missing, one of the wrong shape or one in a second shard twice."""
+    from tests import safetensors_util as ST
+
+    cfg = dict(dim=256, heads=2, ffn=512, blocks=2, time_dim=128, text_dim=256, refiner=1)
+    specs = h3b200.weight_specs(cfg)
+    shape = {n: s for n, _, s in specs}
+    dtypes = {n: d for n, d, _ in specs}
+    assert specs[0][0] == "time_embedder.proj_in.weight"
+    assert shape["blocks.0.attn.qkv.weight"] == (768, 256) and dtypes["blocks.0.attn.qkv.weight"] == "BF16"
+    assert shape["blocks.1.ff.fc1.weight"] == (1024, 256) and shape["blocks.1.adaln_proj.linear.weight"] == (18 * 256, 128)
+    assert "token_refiner.blocks.0.attn.to_out.weight" in shape and "token_refiner.norm.weight" in shape
+    assert "token_refiner.blocks.0.adaln_proj.linear.weight" not in shape
+    tensors = {n: np.zeros(s, np.float32) for n, s in shape.items()}
+    ST.write(tmp_path / "all.safetensors", tensors, dtype=dtypes)
+    assert h3b200.check_weights(cfg, tmp_path / "all.safetensors") == ""
+    names = list(tensors)
+    shards = tmp_path / "shards"
+    shards.mkdir()
+    ST.write(shards / "a.safetensors", {n: tensors[n] for n in names[:20]}, dtype="F32")
+    ST.write(shards / "b.safetensors", {n: tensors[n] for n in names[20:]}, dtype="BF16")
+    assert h3b200.check_weights(cfg, shards) == ""
+    ST.write(tmp_path / "missing.safetensors", {n: a for n, a in tensors.items() if n != "blocks.1.attn.norm_k.weight"})
+    assert h3b200.check_weights(cfg, tmp_path / "missing.safetensors") == "no tensor blocks.1.attn.norm_k.weight"
+    bad = dict(tensors, **{"proj_out.weight": np.zeros((95, 256), np.float32)})
+    ST.write(tmp_path / "bad.safetensors", bad)
+    assert h3b200.check_weights(cfg, tmp_path / "bad.safetensors") == "proj_out.weight is 95x256, this model needs 96x256"
+    ST.write(shards / "c.safetensors", {names[0]: tensors[names[0]]})
+    assert "two files" in h3b200.check_weights(cfg, shards)
+    pruned = h3b200.weight_specs(dict(cfg, curve=8))
+    pn = {n: s for n, _, s in pruned}
+    assert pn["adaln_t_table"] == (1025, 8) and "time_embedder.proj_in.weight" not in pn
+    assert pn["blocks.0.adaln_proj.linear.weight"] == (18 * 256, 8)
 
 
 def test_oracle_token_refiner_ends_in_its_weighted_rms_norm():
