@@ -140,6 +140,15 @@ int h3_lora_inspect(const char* path, char* names, uint64_t cap, uint32_t* count
  * tensors. For converters from other layouts. Host only. No counterpart in the reference. */
 int h3_weight_specs(const h3_config* cfg, char* out, uint64_t cap, uint32_t* count);
 
+/* Rewrites the checkpoint at src (a safetensors file or a directory of them) as a file at dst in the layout h3_create
+ * reads, for a model of shape cfg: every tensor under this library's name, the model's element type, q/k/v stacked.
+ * renames (may be NULL): lines "this_name source_name" for tensors the source names otherwise, '#' lines ignored,
+ * and "qkv_layout interleaved" when the source keeps each head's q, k and v rows together without saying so in its
+ * metadata (the reference's shards, docs/architecture.md:62-63). The source is checked first (a missing tensor or a
+ * shape that disagrees: H3_ERR_ARG). Host only. No counterpart in the reference: the path from its FL2VA files (whose
+ * block-internal tensor names are not in the reference tree) to this library. */
+int h3_convert_weights(const h3_config* cfg, const char* src, const char* dst, const char* renames);
+
 /* Writes the model's weights to a safetensors file in the layout h3_create reads (qkv_layout = stacked), so that a
  * model created from the file computes what this one does. bf16 models only (an int8 model holds no bf16 rows of its
  * quantised projections: H3_ERR_ARG). The file holding the weights is the reference's model directory's role

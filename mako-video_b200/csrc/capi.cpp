@@ -15,7 +15,9 @@
 #include <cstring>
 #include <functional>
 #include <initializer_list>
+#include <map>
 #include <memory>
+#include <sstream>
 #include <string>
 
 struct h3_model {
@@ -327,6 +329,36 @@ int h3_weight_specs(const h3_config* cfg, char* out, uint64_t cap, uint32_t* cou
         }
         if (count)
             *count = uint32_t(specs.size());
+    });
+}
+
+int h3_convert_weights(const h3_config* cfg, const char* src, const char* dst, const char* renames)
+{
+    return guarded([&] {
+        if (!cfg || !src || !dst)
+            throw ArgError("h3_convert_weights: null argument");
+        std::map<std::string, std::string> table;
+        bool interleaved = false;
+        if (renames) {
+            std::istringstream in(renames);
+            std::string line;
+            while (std::getline(in, line)) {
+                std::istringstream ls(line);
+                std::string a, b, extra;
+                if (!(ls >> a) || a[0] == '#')
+                    continue;
+                if (!(ls >> b) || (ls >> extra))
+                    throw ArgError("h3_convert_weights: a rename line is \"this_name source_name\", not \"" + line + "\"");
+                if (a == "qkv_layout") {
+                    if (b != "interleaved" && b != "stacked")
+                        throw ArgError("h3_convert_weights: qkv_layout is interleaved or stacked");
+                    interleaved = b == "interleaved";
+                    continue;
+                }
+                table[a] = b;
+            }
+        }
+        h3::convert_checkpoint(to_config(cfg), src, dst, std::move(table), interleaved);
     });
 }
 

@@ -389,10 +389,19 @@ struct CheckpointWeights::Files {
     std::vector<std::unique_ptr<SafeTensors>> files;
     std::vector<bool> interleaved;       // per file: metadata qkv_layout = interleaved
     std::map<std::string, size_t> where; // tensor name -> file
+    std::map<std::string, std::string> renames;
+    // the checkpoint's name of a weight
+    const std::string& source(const std::string& name) const
+    {
+        const auto it = renames.find(name);
+        return it == renames.end() ? name : it->second;
+    }
 };
 
-CheckpointWeights::CheckpointWeights(const std::string& path) : f_(new Files)
+CheckpointWeights::CheckpointWeights(const std::string& path, std::map<std::string, std::string> renames, bool interleaved)
+    : f_(new Files)
 {
+    f_->renames = std::move(renames);
     std::vector<std::string> paths;
     std::error_code ec;
     if (std::filesystem::is_directory(path, ec)) {
@@ -413,7 +422,7 @@ CheckpointWeights::CheckpointWeights(const std::string& path) : f_(new Files)
             throw std::invalid_argument(std::string("checkpoint: ") + e.what());
         }
         const auto it = st->metadata().find("qkv_layout");
-        f_->interleaved.push_back(it != st->metadata().end() && it->second == "interleaved");
+        f_->interleaved.push_back(interleaved || (it != st->metadata().end() && it->second == "interleaved"));
         for (const auto& [name, t] : st->tensors())
             if (!f_->where.emplace(name, f_->files.size()).second)
                 throw std::invalid_argument("checkpoint: tensor " + name + " appears in two files");
@@ -426,10 +435,11 @@ CheckpointWeights::~CheckpointWeights() = default;
 std::string CheckpointWeights::check(const Config& c) const
 {
     for (const WeightSpec& sp : weight_specs(c)) {
-        const auto it = f_->where.find(sp.name);
+        const std::string& src = f_->source(sp.name);
+        const auto it = f_->where.find(src);
         if (it == f_->where.end())
-            return "no tensor " + sp.name;
-        const SafeTensor& t = f_->files[it->second]->tensors().at(sp.name);
+            return "no tensor " + src + (src == sp.name ? "" : " (for " + sp.name + ")");
+        const SafeTensor& t = f_->files[it->second]->tensors().at(src);
         if (t.shape != sp.shape) {
             std::string got, want;
             for (int64_t v : t.shape)
@@ -446,19 +456,27 @@ std::string CheckpointWeights::check(const Config& c) const
 
 void CheckpointWeights::get(const WeightSpec& spec, void* dst, cudaStream_t s)
 {
-    const auto it = f_->where.find(spec.name);
+    const std::vector<unsigned char> h = host(spec);
+    H3_CUDA(cudaMemcpyAsync(dst, h.data(), h.size(), cudaMemcpyHostToDevice, s));
+    H3_CUDA(cudaStreamSynchronize(s)); // the host copy goes out of scope
+}
+
+std::vector<unsigned char> CheckpointWeights::host(const WeightSpec& spec) const
+{
+    const std::string& src = f_->source(spec.name);
+    const auto it = f_->where.find(src);
     if (it == f_->where.end())
-        throw std::invalid_argument("checkpoint: no tensor " + spec.name);
+        throw std::invalid_argument("checkpoint: no tensor " + src);
     const SafeTensors& st = *f_->files[it->second];
-    if (st.tensors().at(spec.name).shape != spec.shape)
-        throw std::invalid_argument("checkpoint: " + spec.name + " has another shape than this model's");
+    if (st.tensors().at(src).shape != spec.shape)
+        throw std::invalid_argument("checkpoint: " + src + " has another shape than this model's " + spec.name);
     const size_t esz = spec.bf16 ? 2 : 4;
     std::vector<unsigned char> host(spec.count() * esz);
     if (spec.bf16) {
-        const std::vector<uint16_t> v = st.read_bf16(spec.name);
+        const std::vector<uint16_t> v = st.read_bf16(src);
         std::memcpy(host.data(), v.data(), host.size());
     } else {
-        const std::vector<float> v = st.read_f32(spec.name);
+        const std::vector<float> v = st.read_f32(src);
         std::memcpy(host.data(), v.data(), host.size());
     }
     const bool qkv = spec.name.size() > 15 && (spec.name.compare(spec.name.size() - 15, 15, "attn.qkv.weight") == 0 ||
@@ -474,8 +492,25 @@ void CheckpointWeights::get(const WeightSpec& spec, void* dst, cudaStream_t s)
                     std::memcpy(&stacked[size_t(p * inner + h * 128 + r) * row_bytes], &host[size_t(h * 384 + p * 128 + r) * row_bytes], row_bytes);
         host.swap(stacked);
     }
-    H3_CUDA(cudaMemcpyAsync(dst, host.data(), host.size(), cudaMemcpyHostToDevice, s));
-    H3_CUDA(cudaStreamSynchronize(s)); // the host copy goes out of scope
+    return host;
+}
+
+void convert_checkpoint(const Config& c, const std::string& src, const std::string& dst, std::map<std::string, std::string> renames,
+                        bool interleaved)
+{
+    const CheckpointWeights ck(src, std::move(renames), interleaved);
+    const std::string problem = ck.check(c);
+    if (!problem.empty())
+        throw std::invalid_argument("convert: " + src + ": " + problem);
+    const std::vector<WeightSpec> specs = weight_specs(c);
+    std::vector<SafeTensorOut> outs;
+    for (const WeightSpec& sp : specs) {
+        SafeTensorOut o;
+        o.name = sp.name, o.dtype = sp.bf16 ? "BF16" : "F32", o.shape = sp.shape, o.bytes = sp.count() * (sp.bf16 ? 2 : 4);
+        outs.push_back(std::move(o));
+    }
+    write_safetensors(dst, outs, {{"format", "pt"}, {"qkv_layout", "stacked"}, {"writer", "libh3b200"}},
+                      [&](size_t i, std::vector<unsigned char>& buf) { buf = ck.host(specs[i]); });
 }
 
 Model::Model(const Config& c, uint64_t seed, uint32_t int8_mask, const World& world)

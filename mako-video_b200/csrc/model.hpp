@@ -5,6 +5,7 @@
 
 #include <cstdint>
 #include <functional>
+#include <map>
 #include <memory>
 #include <string>
 #include <vector>
@@ -126,6 +127,11 @@ struct WeightSpec {
 // Every weight of a model of this shape, in the order they are set up and saved.
 std::vector<WeightSpec> weight_specs(const Config& c);
 
+// Writes a checkpoint for a model of shape c in this build's layout (its names, stacked q/k/v, the model's element
+// types) from the checkpoint at `src` read through `renames` / `interleaved` as CheckpointWeights reads it. Host only.
+void convert_checkpoint(const Config& c, const std::string& src, const std::string& dst, std::map<std::string, std::string> renames,
+                        bool interleaved);
+
 // Where a model's weights come from: spec's values, in its logical layout and element type, written to device memory.
 class WeightSource {
 public:
@@ -149,9 +155,13 @@ private:
 // h), as the reference's shards do (docs/architecture.md:62-63); they are stacked q, k, v at load (its upload_qkv).
 class CheckpointWeights : public WeightSource {
 public:
-    explicit CheckpointWeights(const std::string& path);
+    // renames: this build's name -> the checkpoint's, for checkpoints that name tensors otherwise (a name not in the
+    // map is looked up as it is); interleaved: treat every file's q/k/v as interleaved, whatever its metadata says.
+    explicit CheckpointWeights(const std::string& path, std::map<std::string, std::string> renames = {}, bool interleaved = false);
     ~CheckpointWeights() override;
     void get(const WeightSpec& spec, void* dst, cudaStream_t s) override;
+    // spec's values in its logical layout and element type, in host memory (what get uploads).
+    std::vector<unsigned char> host(const WeightSpec& spec) const;
     // The first problem a model of shape c would meet loading this checkpoint ("" if none): a missing tensor or a
     // shape that disagrees. Host only.
     std::string check(const Config& c) const;

@@ -103,6 +103,7 @@ SIGNATURES = {
     "h3_lora_inspect": (ctypes.c_int, [ctypes.c_char_p, _P, _U64, _P, _P, _P]),
     "h3_weight_specs": (ctypes.c_int, [ctypes.POINTER(h3_config), _P, _U64, _P]),
     "h3_save_weights": (ctypes.c_int, [_P, ctypes.c_char_p]),
+    "h3_convert_weights": (ctypes.c_int, [ctypes.POINTER(h3_config), ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p]),
     "h3_check_weights": (ctypes.c_int, [ctypes.POINTER(h3_config), ctypes.c_char_p, _P, _U64]),
     "h3k_wait_selftest": (ctypes.c_int, [_U64, _P]),
     "h3_denoise": (ctypes.c_int, [_P, _P, _U64, _P, _U64, _P, _P, _U32, PROGRESS_FN, _P, _P]),
@@ -413,3 +414,13 @@ def check_weights(config, path, eps=1e-6):
     msg = ctypes.create_string_buffer(4096)
     rc = lib().h3_check_weights(ctypes.byref(cfg), str(path).encode(), msg, len(msg))
     return "" if rc == H3_OK else (msg.value.decode() or lib().h3_last_error().decode())
+
+
+def convert_weights(config, src, dst, renames=None, interleaved=False, eps=1e-6):
+    """h3_convert_weights: src (file or directory) rewritten at dst in this library's layout; renames {this library's
+    name: the source's}; interleaved: the source keeps each head's q, k, v rows together (host only)."""
+    cfg = make_config(config, eps)
+    lines = [f"{a} {b}" for a, b in (renames or {}).items()]
+    if interleaved:
+        lines.append("qkv_layout interleaved")
+    check(lib().h3_convert_weights(ctypes.byref(cfg), str(src).encode(), str(dst).encode(), "\n".join(lines).encode()))

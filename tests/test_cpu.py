@@ -389,3 +389,34 @@ def test_oracle_pruned_checkpoint_has_no_time_embedder():
     c = O.curve_points([0.6], w["curve_table"])
     want = (c @ w["blocks"][0]["ada_w"].T + w["blocks"][0]["ada_b"]).numpy()
     np.testing.assert_allclose(seen["mod0"], want, rtol=1e-6, atol=1e-6)
+
+
+def test_convert_renames_and_stacks_a_foreign_checkpoint(tmp_path):
+    """h3_convert_weights: a checkpoint that names two tensors otherwise, keeps each head's q, k and v rows together
+    and stores everything as F32 becomes one that h3_create reads: this library's names, q/k/v stacked, bf16 matrices
+    rounded to nearest even, fp32 vectors as they were."""
+    from tests import safetensors_util as ST
+
+    cfg = dict(dim=256, heads=2, ffn=512, blocks=1, time_dim=128, text_dim=256, refiner=1)
+    specs = h3b200.weight_specs(cfg)
+    rng = np.random.default_rng(0)
+    ours = {n: rng.standard_normal(s).astype(np.float32) for n, _, s in specs}
+    renames = {"blocks.0.attn.qkv.weight": "model.layers.0.attention.wqkv.weight", "blocks.0.norm1.weight": "model.layers.0.ln1.weight"}
+    src = {}
+    for n, a in ours.items():
+        if n.endswith("attn.qkv.weight") or n.endswith("attn.qkv.bias"):
+            parts = a.reshape((3, 2, 128) + a.shape[1:])
+            a = np.ascontiguousarray(parts.transpose((1, 0, 2) + tuple(range(3, parts.ndim)))).reshape(a.shape)
+        src[renames.get(n, n)] = a
+    ST.write(tmp_path / "src.safetensors", src, dtype="F32")
+    assert h3b200.check_weights(cfg, tmp_path / "src.safetensors") == "no tensor blocks.0.norm1.weight"
+    h3b200.convert_weights(cfg, tmp_path / "src.safetensors", tmp_path / "dst.safetensors", renames=renames, interleaved=True)
+    assert h3b200.check_weights(cfg, tmp_path / "dst.safetensors") == ""
+    got, dtypes, meta = ST.read(tmp_path / "dst.safetensors")
+    assert meta["qkv_layout"] == "stacked" and set(got) == set(ours)
+    for n, d, _ in specs:
+        want = ST.bf16_values(ours[n]).numpy() if d == "BF16" else ours[n]
+        assert dtypes[n] == d
+        np.testing.assert_array_equal(got[n], want)
+    with pytest.raises(h3b200.H3Error):
+        h3b200.convert_weights(cfg, tmp_path / "src.safetensors", tmp_path / "x.safetensors")  # the renames are needed
