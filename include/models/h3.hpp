@@ -182,6 +182,20 @@ public:
         return r;
     }
 
+    // Checkpoints (no counterpart in the reference; host only). check_weights: "" when the checkpoint at `path` fits
+    // the shape, else its first problem. convert_weights: the checkpoint at `src` rewritten at `dst` in this library's
+    // layout through `renames` lines ("this_name source_name", "qkv_layout interleaved"); see h3_convert_weights.
+    static std::string check_weights(const std::string& path, h3_config cfg = h3_mini_h3())
+    {
+        char msg[4096] = {};
+        return h3_check_weights(&cfg, path.c_str(), msg, sizeof msg) == H3_OK ? std::string() : std::string(msg);
+    }
+    static void convert_weights(const std::string& src, const std::string& dst, const std::string& renames = {},
+                                h3_config cfg = h3_mini_h3())
+    {
+        check(h3_convert_weights(&cfg, src.c_str(), dst.c_str(), renames.c_str()));
+    }
+
     // parse_int8 (tools/mako_video.cpp:108-114).
     static std::optional<uint32_t> parse_int8(std::string_view s)
     {

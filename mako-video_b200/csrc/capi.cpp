@@ -377,7 +377,12 @@ int h3_check_weights(const h3_config* cfg, const char* path, char* message, uint
     return guarded([&] {
         if (!cfg || !path)
             throw ArgError("h3_check_weights: null argument");
-        const std::string problem = h3::CheckpointWeights(path).check(to_config(cfg));
+        std::string problem;
+        try {
+            problem = h3::CheckpointWeights(path).check(to_config(cfg));
+        } catch (const std::exception& e) {
+            problem = e.what(); // a file that cannot be read is the problem to report
+        }
         if (message && cap) {
             const size_t n = std::min<size_t>(problem.size(), cap - 1);
             std::memcpy(message, problem.data(), n);

@@ -47,6 +47,8 @@ int main()
         threw = std::string(e.what()).find("cannot open") != std::string::npos;
     }
     check(threw, "a missing checkpoint is refused with a message");
+    check(H3::check_weights("/models/minimax-h3/FL2VA/transformer").find("cannot open") != std::string::npos,
+          "check_weights reports a missing checkpoint");
     // The C ABI's struct layouts, for the bindings' own declarations to be checked against (tests/test_cpp_dropin.py).
     std::printf("abi h3_config %zu %zu %zu\n", sizeof(h3_config), offsetof(h3_config, refiner_blocks), offsetof(h3_config, curve_dims));
     std::printf("abi h3_layout %zu %zu %zu\n", sizeof(h3_layout), offsetof(h3_layout, refs), offsetof(h3_layout, n_refs));
