@@ -420,3 +420,19 @@ def test_convert_renames_and_stacks_a_foreign_checkpoint(tmp_path):
         np.testing.assert_array_equal(got[n], want)
     with pytest.raises(h3b200.H3Error):
         h3b200.convert_weights(cfg, tmp_path / "src.safetensors", tmp_path / "x.safetensors")  # the renames are needed
+
+
+def test_h3_shape_holds_the_reference_parameter_counts():
+    """MiniMax-H3's shape in this build (dim 5376, 56 heads of 128, SwiGLU 14336, 50 blocks, time 2688, the two-block
+    token refiner) holds the sizes the reference documents: 20 B parameters without the AdaLN projections and 33 B with
+    (docs/architecture.md:11-12); the AdaLN projections 26 GB of the 66, and 47 GB once q/k/v, out, fc1 and fc2 are
+    int8 rows (docs/architecture.md:53-56)."""
+    specs = h3b200.weight_specs("h3")
+    count = lambda pick: sum(math.prod(s) for n, _, s in specs if pick(n))
+    total, adaln = count(lambda n: True), count(lambda n: "adaln_proj" in n)
+    assert round(total / 1e9) == 33 and round((total - adaln) / 1e9) == 20
+    nbytes = sum(math.prod(s) * (2 if d == "BF16" else 4) for _, d, s in specs)
+    assert round(nbytes / 1e9) == 66 and round(2 * adaln / 1e9) == 26
+    projections = count(lambda n: n.startswith("blocks.") and any(k in n for k in ("attn.qkv.weight", "attn.to_out.weight",
+                                                                                  "ff.fc1.weight", "ff.fc2.weight")))
+    assert round((nbytes - projections) / 1e9) == 47  # int8 rows: one byte instead of two
