@@ -436,3 +436,25 @@ def test_h3_shape_holds_the_reference_parameter_counts():
     projections = count(lambda n: n.startswith("blocks.") and any(k in n for k in ("attn.qkv.weight", "attn.to_out.weight",
                                                                                   "ff.fc1.weight", "ff.fc2.weight")))
     assert round((nbytes - projections) / 1e9) == 47  # int8 rows: one byte instead of two
+
+
+def test_h3_tensor_shapes_and_768p_rows_match_the_reference_prose():
+    """Shapes the reference states for MiniMax-H3: AdaLN 2688 -> 96768 = 3 x 6 x 5376 and the final layer's 2688 ->
+    2 x 5376 (docs/architecture.md:49-53), q/k/v 5376 -> 21504 and out 7168 -> 5376, fc1 28672 rows [gate; value], fc2
+    from 14336 (docs/architecture.md:61-65; docs/performance.md:41-43), condition_proj 5120 -> 5376, the patch
+    projections 96 and 32 -> 5376 (docs/architecture.md:25-31), a pruned checkpoint's [96768][8] and [10752][8]
+    projections (docs/architecture.md:57-60); and the 768p x 124-frame layout's 37 x 24 x 42 = 37296 video rows and
+    414 audio rows (docs/architecture.md:31-33; tests/geometry_test.cpp:24-26)."""
+    shape = {n: s for n, _, s in h3b200.weight_specs("h3")}
+    assert shape["blocks.0.adaln_proj.linear.weight"] == (96768, 2688)
+    assert shape["norm_out.adaln_proj.weight"] == (10752, 2688)
+    assert shape["blocks.49.attn.qkv.weight"] == (21504, 5376) and shape["blocks.49.attn.to_out.weight"] == (5376, 7168)
+    assert shape["blocks.0.ff.fc1.weight"] == (28672, 5376) and shape["blocks.0.ff.fc2.weight"] == (5376, 14336)
+    assert shape["condition_proj.weight"] == (5376, 5120)
+    assert shape["video_patch_proj.weight"] == (5376, 96) and shape["audio_patch_proj.weight"] == (5376, 32)
+    assert "blocks.50.norm1.weight" not in shape
+    pruned = {n: s for n, _, s in h3b200.weight_specs(dict(h3b200.CONFIGS["h3"], curve=8))}
+    assert pruned["blocks.0.adaln_proj.linear.weight"] == (96768, 8) and pruned["norm_out.adaln_proj.weight"] == (10752, 8)
+    lay = h3b200.Layout(text=300, frames=37, h=48, w=84, audio=207, cond_frames=0)
+    assert lay.video_rows == 37296 and lay.audio_rows == 414
+    assert h3b200.lib().h3_layout_rows(ctypes.byref(lay.c)) == 300 + 414 + 37296
