@@ -72,7 +72,7 @@ def load_peaks():
 # ---------------------------------------------------------------------------------------------- FLOP counts
 
 def step_flops(cfg, S, layout, sparse_ratio=0.0):
-    """Algorithmic FLOPs of one step: the block GEMMs and attention (the SURVEY's per-unit figures)."""
+    """Algorithmic FLOPs of one step: the block GEMMs (2 M N K each) and attention (4 S^2 inner dense)."""
     d, inner, F, L = cfg["dim"], cfg["heads"] * 128, cfg["ffn"], cfg["blocks"]
     gemm = L * 2 * S * (d * 3 * inner + inner * d + d * 2 * F + F * d)
     attn_launch = attention_flops(cfg, S, layout, sparse_ratio)
@@ -144,83 +144,231 @@ class ClockSampler:
 
 # ----------------------------------------------------------------------------------------------- CPU sample
 
-def cpu_sample(cfg, S, n_q=4096, n_k=16384, threads=None):
-    """The CPU restatement (the oracle's block arithmetic, fp32 with bf16-valued weights) on one full-width block:
-    q/k/v for n_k rows, attention of n_q queries over those n_k keys, the out projection and the FFN for n_q rows;
-    each part scaled to all S rows (work per row is uniform) and to every block. Returns (s per step, description)."""
+def _inputs(layout, cfg, seed=0):
+    rng = np.random.default_rng(seed)
+    text = rng.standard_normal((layout.d["text"], cfg["text_dim"]), dtype=np.float32)
+    video = rng.standard_normal((layout.video_rows, 96), dtype=np.float32)
+    audio = rng.standard_normal((layout.audio_rows, 32), dtype=np.float32)
+    return text, video, audio
+
+
+def cpu_step_sample(cfg, layout, threads=None, weights=None):
+    """The oracle's own step (oracle/h3_oracle.py: step, torch fp32 with bf16-valued weights) with ONE block of the
+    configuration's width over ALL of the workload's rows, on `threads` host threads. The probes time the block (from
+    the packed input to block 0's output); the rest of the step (text projection and token refiner, time embedding,
+    patch projections, final norm and heads) runs once. Returns (extrapolated s per step = rest + blocks x block,
+    block s, rest s, description, weights)."""
     import torch
     from oracle import h3_oracle as O
 
     threads = threads or os.cpu_count() or 1
     torch.set_num_threads(threads)
-    d, H, F, L = cfg["dim"], cfg["heads"], cfg["ffn"], cfg["blocks"]
-    inner = H * 128
-    g = torch.Generator().manual_seed(0)
-    w = lambda *s: (torch.randn(*s, generator=g) * 0.02).bfloat16().float()
-    Wqkv, Wout, W1, W2 = w(3 * inner, d), w(d, inner), w(2 * F, d), w(d, F)
-    Wada = w(18 * d, cfg["time_dim"])
-    n_k, n_q = min(n_k, S), min(n_q, S)
-    x = torch.randn(n_k, d, generator=g)
-    mod = torch.randn(6, d, generator=g) * 0.1
-    pos = np.stack([np.arange(n_k, dtype=np.float64)] * 3, 1)
-    cs = torch.from_numpy(O.rope_table(pos))
+    one = dict(cfg, blocks=1)
+    w = weights if weights is not None else O.make_weights(one, 0)
+    text, video, audio = _inputs(layout, cfg)
+    marks = {}
+
+    def probe(name, layer, _a):
+        marks[name if layer < 0 else f"{name}{layer}"] = time.perf_counter()
+
     t0 = time.perf_counter()
-    s = torch.randn(1, cfg["time_dim"], generator=g)
-    _ = s @ Wada.T
-    t_ada = time.perf_counter() - t0
-    t0 = time.perf_counter()
-    h = O.rms(x, 1e-6) * (1 + mod[1]) + mod[0]
-    qkv = (h @ Wqkv.T).reshape(n_k, 3, H, 128)
-    q = O.rope(O.rms(qkv[:n_q, 0], 1e-6), cs[:n_q])
-    k = O.rope(O.rms(qkv[:, 1], 1e-6), cs)
-    v = qkv[:, 2]
-    t_qkv = time.perf_counter() - t0
-    t0 = time.perf_counter()
-    qh, kh, vh = q.permute(1, 0, 2), k.permute(1, 0, 2), v.permute(1, 0, 2)
-    o = torch.empty_like(qh)
-    for hh in range(H):  # one head at a time keeps the score matrix to n_q x n_k
-        o[hh] = torch.softmax(qh[hh] @ kh[hh].T / math.sqrt(128.0), -1) @ vh[hh]
-    t_attn = time.perf_counter() - t0
-    t0 = time.perf_counter()
-    xr = x[:n_q] + mod[2] * (o.permute(1, 0, 2).reshape(n_q, inner) @ Wout.T)
-    h2 = O.rms(xr, 1e-6) * (1 + mod[4]) + mod[3]
-    gv = h2 @ W1.T
-    a = torch.nn.functional.silu(gv[:, :F]) * gv[:, F:]
-    xr = xr + mod[5] * (a @ W2.T)
-    t_rest = time.perf_counter() - t0
-    block = t_qkv * (S / n_k) + t_attn * (S / n_q) * (S / n_k) + t_rest * (S / n_q) + t_ada
-    desc = (f"one full-width block (d {d}, {H} heads, SwiGLU {F}): q/k/v for {n_k} rows, attention of {n_q} queries over "
-            f"{n_k} keys, out + FFN for {n_q} rows, each part scaled to S = {S} rows and x{L} blocks; torch fp32 on "
-            f"{threads} threads")
-    return block * L, desc, t_qkv + t_attn + t_rest + t_ada
+    O.step(one, w, layout.d, text, video, audio, 0.7, 0.7, probes=probe)
+    t1 = time.perf_counter()
+    block = marks["block0"] - marks["x0"]
+    rest = (t1 - t0) - block
+    L = cfg["blocks"]
+    desc = (f"oracle step (oracle/h3_oracle.py: step, torch fp32) with one full-width block (d {cfg['dim']}, {cfg['heads']} heads, "
+            f"SwiGLU {cfg['ffn']}) over all {layout.rows} rows: the block timed ({block:.1f} s) x{L} blocks + the step's "
+            f"other work once ({rest:.1f} s); {threads} host threads")
+    return rest + L * block, block, rest, desc, w
 
 
 # ---------------------------------------------------------------------------------------------------- arms
 
 def run_reference(args, rank, world):
-    """The reference's host-side path for the step: the CPU restatement (the reference's own step is Metal inside
-    an absent submodule), all host threads, a bounded sample per step scaled to the full step."""
+    """The reference's host-side path for the step. The reference's own step is Metal code inside an absent
+    submodule, so the CPU arm is the oracle's restatement of it: one full step of the oracle with one full-width
+    block over all of the workload's rows per timed sample, the block scaled to the stack's block count. Samples run
+    until K are timed or ~2 minutes have passed (at least one), so the run stays within a few minutes."""
     if rank != 0:
         return
     import h3b200 as H
     cfg_name, lay_name, ratio, local, int8, wdesc = WORKLOADS[args.workload]
-    cfg = H.CONFIGS[cfg_name]
-    S = H.Layout.named(lay_name).rows
-    vals = []
-    desc = ""
-    for i in range(args.warmup + args.steps):
-        v, desc, _ = cpu_sample(cfg, S)
-        if i >= args.warmup:
-            vals.append(v)
+    cfg = dict(H.CONFIGS[cfg_name])
+    layout = H.Layout.named(lay_name)
+    threads = os.cpu_count() or 1
+    # warm-up: the same step on an eighth of the frames (threads and allocator spun up; weights generated)
+    small = dict(layout.d)
+    small["frames"] = max(1, small["frames"] // 8)
+    w = None
+    for _ in range(min(args.warmup, 1)):
+        _, _, _, _, w = cpu_step_sample(cfg, H.Layout(**small), threads, w)
+    vals, blocks, rests, desc = [], [], [], ""
+    t_start = time.perf_counter()
+    while len(vals) < max(1, args.steps) and (not vals or time.perf_counter() - t_start < 120.0):
+        v, b, r, desc, w = cpu_step_sample(cfg, layout, threads, w)
+        vals.append(v)
+        blocks.append(b)
+        rests.append(r)
     value = statistics.mean(vals)
-    threads = os.cpu_count()
-    line = {"metric": METRIC, "value": value, "unit": "s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": value * 1e3, "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "impl": "reference",
-            "config": {"workload": wdesc, "rows": S, "dim": cfg["dim"], "heads": cfg["heads"], "blocks": cfg["blocks"]},
-            "cpu_baseline": {"value": value, "unit": "s", "cores": threads, "kind": "port", "sample": desc},
+    sample_s = statistics.mean(b + r for b, r in zip(blocks, rests))
+    note = ""
+    if ratio or int8:
+        note = " (dense bf16-valued fp32 attention and projections: the CPU restatement has no sparse or int8 fast path)"
+    line = {"metric": METRIC, "value": value, "unit": "s", "n_gpus": args.gpus, "steps": len(vals), "warmup": min(args.warmup, 1),
+            "steps_requested": args.steps, "warmup_requested": args.warmup,
+            "ms_per_step": sample_s * 1e3,
+            "ms_per_step_is": "one timed sample: the oracle's step with one full-width block over all rows",
+            "extrapolated_from": f"1 full-S block x{cfg['blocks']} + the step's other work once",
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded normal inputs, hash-generated ~N(0, 0.02) weights)", "impl": "reference",
+            "config": {"workload": wdesc, "rows": layout.rows, "dim": cfg["dim"], "heads": cfg["heads"], "ffn": cfg["ffn"],
+                       "blocks": cfg["blocks"]},
+            "cpu_baseline": {"value": value, "unit": "s", "cores": threads, "kind": "port", "sample": desc + note,
+                             "block_s": statistics.mean(blocks), "rest_s": statistics.mean(rests)},
             "e2e": {"value": value, "unit": "s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     emit(line)
+
+
+class Runner:
+    """One model on this rank's GPU and the workload inputs; measures device time (inputs resident) and the end-to-end
+    time through h3_step (host buffers)."""
+
+    def __init__(self, H, torch, dist, model, layout, cfg, rank, world, local_rank):
+        self.H, self.torch, self.dist = H, torch, dist
+        self.model, self.layout, self.cfg = model, layout, cfg
+        self.rank, self.world, self.local_rank = rank, world, local_rank
+        self.dev = torch.device("cuda", local_rank)
+        self.text, video, audio = _inputs(layout, cfg)
+        model.begin(self.text, layout)
+        self.dv, self.da = torch.from_numpy(video).to(self.dev), torch.from_numpy(audio).to(self.dev)
+        self.ov, self.oa = torch.empty_like(self.dv), torch.empty_like(self.da)
+        pin = lambda a: torch.from_numpy(a).pin_memory().numpy()
+        self.pv, self.pa = pin(video), pin(audio)
+        self.hv = torch.empty(video.shape, dtype=torch.float32).pin_memory().numpy()
+        self.ha = torch.empty(audio.shape, dtype=torch.float32).pin_memory().numpy()
+        self.ext = torch.cuda.ExternalStream(model.stream, device=self.dev)
+        self.t = (0.7, 0.7)
+
+    def step_dev(self):
+        L = self.layout
+        self.model.step_device(self.dv.data_ptr(), L.video_rows, self.da.data_ptr() if self.da.numel() else None, L.audio_rows,
+                               *self.t, self.ov.data_ptr(), self.oa.data_ptr() if self.oa.numel() else None)
+
+    def step_host(self):
+        H, pv, pa, hv, ha = self.H, self.pv, self.pa, self.hv, self.ha
+        H.check(H.lib().h3_step(self.model.h, pv.ctypes.data, pv.shape[0], pa.ctypes.data if pa.size else None, pa.shape[0], *self.t,
+                                hv.ctypes.data, ha.ctypes.data if ha.size else None))
+
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+
+    def maxed(self, vals):
+        if self.world == 1:
+            return vals
+        t = self.torch.tensor(vals, device=self.dev, dtype=self.torch.float64)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return [float(x) for x in t]
+
+    def measure(self, steps, warmup, pairs, clocks_gpu=None):
+        torch = self.torch
+        for _ in range(warmup):
+            self.step_dev()
+        self.model.synchronize()
+        # value: K steps back to back with the inputs in HBM, CUDA events on the library's stream
+        self.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        clk = ClockSampler(clocks_gpu) if clocks_gpu is not None else None
+        if clk:
+            clk.__enter__()
+        with torch.cuda.stream(self.ext):
+            e0.record()
+            for _ in range(steps):
+                self.step_dev()
+            e1.record()
+        self.model.synchronize()
+        torch.cuda.synchronize()
+        if clk:
+            clk.__exit__()
+        self.barrier()
+        ms = e0.elapsed_time(e1) / steps
+        launches = self.model.last_launches()
+        # end to end, interleaved with device-resident steps so that both see the same clocks: each pair is one
+        # h3_step (pinned host buffers in and out, wall clock) and one step_device (CUDA events)
+        e2e, dev = [], []
+        for _ in range(pairs):
+            self.barrier()
+            t0 = time.perf_counter()
+            self.step_host()
+            e2e.append(time.perf_counter() - t0)
+            self.barrier()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(self.ext):
+                a.record()
+                self.step_dev()
+                b.record()
+            self.model.synchronize()
+            dev.append(a.elapsed_time(b) * 1e-3)
+        if not np.isfinite(self.hv).all():
+            raise RuntimeError("non-finite velocities")
+        # per-kernel-class device times (events after each class in every block) through h3_step: the copies too
+        self.model.set_timing(True)
+        self.step_host()
+        classes = self.model.timing_by_class()
+        self.model.set_timing(False)
+        ms, e2e_s, dev_s = self.maxed([ms, statistics.mean(e2e), statistics.mean(dev)])
+        return {"ms": ms, "e2e_s": e2e_s, "paired_dev_s": dev_s, "launches": launches, "classes": classes,
+                "clocks": clk.summary() if clk else None}
+
+
+def _line_part(m, cfg, layout, ratio, world, peaks, args_workload_key, int8):
+    """The metric, e2e, the attention roofline and the HBM-bound kernels' bandwidth of one measured workload."""
+    S = layout.rows
+    classes = m["classes"]
+    attn_ms, attn_n = classes.get("attn", (0.0, 0))
+    attn_launch = attention_flops(cfg, S, layout.d, ratio) / world
+    achieved = attn_launch / (attn_ms / max(attn_n, 1) * 1e-3) / 1e12 if attn_ms else None
+    peak = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
+    gemm_flops, attn_flops = step_flops(cfg, S, layout.d, ratio)
+    gemm_ms = sum(classes.get(c, (0.0, 0))[0] for c in ("qkv", "out", "fc1", "fc2"))
+    gemm_tflops = (gemm_flops / world) / (gemm_ms * 1e-3) / 1e12 if gemm_ms else None
+    h2d_ms = classes.get("h2d", (0.0, 0))[0]
+    d2h_ms = classes.get("d2h", (0.0, 0))[0]
+    vb, ab = layout.video_rows * 96 * 4, layout.audio_rows * 32 * 4
+    # HBM-bound kernels: modulated RMS norms (fp32 rows in, bf16 or int8 + row scale out) and the AdaLN GEMV (weights)
+    S_l = -(-S // world)
+    d, td, L = cfg["dim"], cfg["time_dim"], cfg["blocks"]
+    norm_ms, norm_n = classes.get("norm", (0.0, 0))
+    norm_bytes = S_l * d * (4 + (1 if int8 else 2)) + (S_l * 4 if int8 else 0)
+    norm_gbs = norm_bytes / (norm_ms / norm_n * 1e-3) / 1e9 if norm_ms else None
+    ada_ms = classes.get("adaln", (0.0, 0))[0]
+    ada_bytes = (-(-L // world) * 18 * d + 2 * d) * td * 2
+    ada_gbs = ada_bytes / (ada_ms * 1e-3) / 1e9 if ada_ms else None
+    hbm = peaks.get("hbm_gbs")
+    return {
+        "value": m["ms"] / 1e3, "unit": "s", "ms_per_step": m["ms"],
+        "e2e": {"value": m["e2e_s"], "unit": "s", "h2d_bytes_per_step": int(vb + ab), "d2h_bytes_per_step": int(vb + ab),
+                "paired_device_s": m["paired_dev_s"], "h2d_ms": h2d_ms, "d2h_ms": d2h_ms,
+                "note": "each timed h3_step (pinned host buffers, wall clock) is paired with a device-resident step "
+                        "(CUDA events) so both see the same clocks; h2d_ms / d2h_ms are the copy stages' CUDA-event times "
+                        "inside h3_step (d2h includes the gather of the video rows back to the layout's order)"},
+        "roofline": {"bound": "tensor", "kernel": "attention (attn3_kernel, tcgen05)" if ratio else "attention (attn2_kernel, tcgen05)",
+                     "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": (achieved / peak) if achieved else None,
+                     "traffic": load_traffic("attention", args_workload_key) if world == 1 else None,
+                     "peak_kind": "measured bf16 sustained (MEASURED_PEAKS.json)",
+                     "launch_flops": attn_launch, "launch_ms": attn_ms / max(attn_n, 1) if attn_n else None,
+                     "gemm_tflops": gemm_tflops, "gemm_frac": gemm_tflops / peak if gemm_tflops else None},
+        "hbm_kernels": {
+            "rms_mod_kernel": {"achieved_gbs": norm_gbs, "frac": norm_gbs / hbm if norm_gbs and hbm else None,
+                               "bytes_per_launch": norm_bytes, "launch_ms": norm_ms / norm_n if norm_n else None},
+            "adaln_kernel": {"achieved_gbs": ada_gbs, "frac": ada_gbs / hbm if ada_gbs and hbm else None, "bytes_per_step": ada_bytes,
+                             "ms": ada_ms},
+            "peak_gbs": hbm, "peak_kind": "measured copy bandwidth (MEASURED_PEAKS.json)"},
+        "step_tflops": (gemm_flops + attn_flops) / world / (m["ms"] * 1e-3) / 1e12 * world,
+        "stage_ms": {k: round(v[0], 3) for k, v in sorted(classes.items(), key=lambda kv: -kv[1][0])},
+    }
 
 
 def run_ours(args, rank, world, local_rank):
@@ -234,127 +382,75 @@ def run_ours(args, rank, world, local_rank):
     if args.blocks:
         cfg["blocks"] = args.blocks  # a shorter stack of the same blocks (profiling cases)
     layout = H.Layout.named(lay_name)
-    nccl_id = None
-    if world > 1:
-        obj = [H.nccl_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(obj, src=0)
-        nccl_id = obj[0]
-    model = H.Model(cfg, seed=0, int8_mask=int8, sparse_ratio=ratio, sparse_local=local, rank=rank, world=world,
-                    nccl_id=nccl_id, device=local_rank)
-    rng = np.random.default_rng(0)
-    text = rng.standard_normal((layout.d["text"], cfg["text_dim"]), dtype=np.float32)
-    video = rng.standard_normal((layout.video_rows, 96), dtype=np.float32)
-    audio = rng.standard_normal((layout.audio_rows, 32), dtype=np.float32)
-    model.begin(text, layout)
-    dev = torch.device("cuda", local_rank)
-    dv, da = torch.from_numpy(video).to(dev), torch.from_numpy(audio).to(dev)
-    ov, oa = torch.empty_like(dv), torch.empty_like(da)
-    ext = torch.cuda.ExternalStream(model.stream, device=dev)
-    t_v, t_a = 0.7, 0.7
 
-    def step_dev():
-        model.step_device(dv.data_ptr(), layout.video_rows, da.data_ptr() if da.numel() else None, layout.audio_rows, t_v, t_a,
-                          ov.data_ptr(), oa.data_ptr() if oa.numel() else None)
-
-    def barrier():
+    def new_model(int8_mask, sparse_ratio, sparse_local):
+        nccl_id = None
         if world > 1:
-            dist.barrier()
+            obj = [H.nccl_unique_id() if rank == 0 else None]
+            dist.broadcast_object_list(obj, src=0)
+            nccl_id = obj[0]
+        return H.Model(cfg, seed=0, int8_mask=int8_mask, sparse_ratio=sparse_ratio, sparse_local=sparse_local, rank=rank, world=world,
+                       nccl_id=nccl_id, device=local_rank)
 
-    for _ in range(args.warmup):
-        step_dev()
-    model.synchronize()
+    model = new_model(int8, ratio, local)
+    run = Runner(H, torch, dist, model, layout, cfg, rank, world, local_rank)
     if args.profile:
         # profiling runs (ncu): just the steps, no timing extras
-        for _ in range(args.steps):
-            step_dev()
+        for _ in range(args.warmup + args.steps):
+            run.step_dev()
         model.synchronize()
         model.close()
         return
-
-    # ---- value: device time per step, inputs resident
-    barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local_rank) as clk:
-        with torch.cuda.stream(ext):
-            e0.record()
-            for _ in range(args.steps):
-                step_dev()
-            e1.record()
-        model.synchronize()
-    torch.cuda.synchronize()
-    barrier()
-    ms = e0.elapsed_time(e1) / args.steps
-    launches = model.last_launches()
-    clocks = clk.summary()
-
-    # ---- per-kernel-class device times (events after each kernel class of every block), one more step
-    model.set_timing(True)
-    step_dev()
-    model.synchronize()
-    classes = model.timing_by_class()
-    model.set_timing(False)
-
-    # ---- e2e through h3_step with pinned host buffers
-    pin = lambda a: torch.from_numpy(a).pin_memory().numpy()
-    pv, pa = pin(video), pin(audio)
-    hv = torch.empty(video.shape, dtype=torch.float32).pin_memory().numpy()
-    ha = torch.empty(audio.shape, dtype=torch.float32).pin_memory().numpy()
-    barrier()
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        H.check(H.lib().h3_step(model.h, pv.ctypes.data, pv.shape[0], pa.ctypes.data if pa.size else None, pa.shape[0], t_v, t_a,
-                                hv.ctypes.data, ha.ctypes.data if ha.size else None))
-    e2e_s = (time.perf_counter() - t0) / args.steps
-    barrier()
-
-    # ---- max over ranks
+    peaks, _ = load_peaks()
+    m = run.measure(args.steps, args.warmup, min(args.steps, 10), clocks_gpu=local_rank)
+    head = _line_part(m, cfg, layout, ratio, world, peaks, args.workload, int8)
+    line = {
+        "metric": METRIC, "value": head["value"], "unit": "s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": head["ms_per_step"], "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+        "dtype": "int8" if int8 else "bf16", "data": "synthetic (seeded normal inputs, hash-generated ~N(0, 0.02) weights)",
+        "config": {"workload": wdesc, "rows": layout.rows, "dim": cfg["dim"], "heads": cfg["heads"], "ffn": cfg["ffn"],
+                   "blocks": cfg["blocks"], "parallelism": f"ulysses-sp{world}" if world > 1 else "single-gpu",
+                   "l2": "no flush: each step streams ~54 GB of weights, far past the 126 MB L2"},
+        "roofline": head["roofline"], "hbm_kernels": head["hbm_kernels"], "step_tflops": head["step_tflops"],
+        "stage_ms": head["stage_ms"], "e2e": head["e2e"], "gpu_launches": m["launches"] * args.steps, "clocks": m["clocks"],
+    }
     if world > 1:
-        t = torch.tensor([ms, e2e_s], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, e2e_s = float(t[0]), float(t[1])
-    if not np.isfinite(hv).all():
-        raise RuntimeError("non-finite velocities")
+        line["exchange"] = ("Ulysses all-to-all fused into the q/k/v GEMM and attention epilogues as NVLink peer stores "
+                            "(CUDA IPC mappings); NCCL carries a 4-byte barrier per exchange, the AdaLN all-gather and the heads' "
+                            "all-gather")
+    # the other BASELINE configurations, on the same weights where the workload allows, fewer steps
+    ks, kw = min(args.steps, 5), 3
+    # int8 last: it needs its own model (int8 weights); the others run on the dense model's weights
+    extras = [] if args.extras == "none" or args.workload != "dense" else (
+        ["sparse"] + (["long", "long-sparse"] if world > 1 else []) + ["int8"])
+    run_layout = lay_name
+    for name in extras:
+        _, lname, r2, l2, i2, d2 = WORKLOADS[name]
+        lay2 = H.Layout.named(lname)
+        if i2:
+            model.close()
+            model = new_model(i2, r2, l2)
+            run = Runner(H, torch, dist, model, lay2, cfg, rank, world, local_rank)
+        else:
+            model.set_sparse(r2, l2)
+            if lname != run_layout:
+                run = Runner(H, torch, dist, model, lay2, cfg, rank, world, local_rank)
+        run_layout = lname
+        m2 = run.measure(ks, kw, ks)
+        part = _line_part(m2, cfg, lay2, r2, world, peaks, name, i2)
+        part.update({"workload": d2, "rows": lay2.rows, "steps": ks, "warmup": kw, "gpu_launches": m2["launches"] * ks})
+        line[name.replace("-", "_")] = part
+    if "sparse" in line:
+        line["sparse"]["dense_over_sparse"] = line["value"] / line["sparse"]["value"]
+    if "long" in line and "long_sparse" in line:
+        line["long_sparse"]["dense_over_sparse"] = line["long"]["value"] / line["long_sparse"]["value"]
     model.close()
     if rank != 0:
         return
-
-    S = layout.rows
-    gemm_flops, attn_flops = step_flops(cfg, S, layout.d, ratio)
-    peaks, peak_kind = load_peaks()
-    L = cfg["blocks"]
-    attn_ms, attn_n = classes.get("attn", (0.0, 0))
-    attn_launch = attention_flops(cfg, S, layout.d, ratio) / world
-    achieved = attn_launch / (attn_ms / max(attn_n, 1) * 1e-3) / 1e12 if attn_ms else None
-    peak = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
-    gemm_ms = sum(classes.get(c, (0.0, 0))[0] for c in ("qkv", "out", "fc1", "fc2"))
-    gemm_tflops = (gemm_flops / world) / (gemm_ms * 1e-3) / 1e12 if gemm_ms else None
-    breakdown = {k: round(v[0], 3) for k, v in sorted(classes.items(), key=lambda kv: -kv[1][0])}
-    line = {
-        "metric": METRIC, "value": ms / 1e3, "unit": "s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms, "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
-        "dtype": "int8" if int8 else "bf16", "data": "synthetic (seeded normal inputs, hash-generated ~N(0, 0.02) weights)",
-        "config": {"workload": wdesc, "rows": S, "dim": cfg["dim"], "heads": cfg["heads"], "ffn": cfg["ffn"], "blocks": L,
-                   "parallelism": f"ulysses-sp{world}" if world > 1 else "single-gpu",
-                   "l2": "no flush: each step streams ~54 GB of weights, far past the 126 MB L2"},
-        "roofline": {"bound": "tensor", "kernel": "attention (flash_attn, tcgen05)", "achieved": achieved, "peak": peak,
-                     "unit": "TFLOP/s", "frac": (achieved / peak) if achieved else None,
-                     "traffic": load_traffic("attention", args.workload) if world == 1 else None,
-                     "peak_kind": f"{peak_kind} bf16 sustained",
-                     "launch_flops": attn_launch, "launch_ms": attn_ms / max(attn_n, 1) if attn_n else None,
-                     "gemm_tflops": gemm_tflops, "gemm_frac": gemm_tflops / peak if gemm_tflops else None},
-        "step_tflops": (gemm_flops + attn_flops) / (ms * 1e-3) / 1e12,
-        "stage_ms": breakdown,
-        "e2e": {"value": e2e_s, "unit": "s", "h2d_bytes_per_step": int(video.nbytes + audio.nbytes),
-                "d2h_bytes_per_step": int(hv.nbytes + ha.nbytes)},
-        "gpu_launches": launches * args.steps,
-        "clocks": clocks,
-    }
-    if world == 1 and not args.no_cpu_baseline:
-        v, desc, spent = cpu_sample(cfg, S)
+    if world == 1 and not args.no_cpu_baseline and cfg_name == "c2":
+        v, b, r, desc, _ = cpu_step_sample(cfg, layout)
         line["cpu_baseline"] = {"value": v, "unit": "s", "cores": os.cpu_count(), "kind": "port", "sample": desc,
-                                "sample_seconds": spent}
+                                "block_s": b, "rest_s": r}
     emit(line)
 
 
@@ -368,6 +464,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--blocks", type=int, default=0, help="override the block count (profiling cases only)")
     ap.add_argument("--profile", action="store_true", help="run warmup + steps and exit (for ncu captures)")
+    ap.add_argument("--extras", default="all", choices=["all", "none"],
+                    help="with the dense workload: also measure sparse (C3), int8 (C4) and, on 2+ GPUs, the long clip (C5)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))

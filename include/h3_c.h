@@ -289,8 +289,10 @@ int h3k_sparse_attention(const void* q, const void* k, const void* v, int64_t ro
  * reserved nearly all device memory for its own pool, or one whose other streams must not stall on the device-wide
  * synchronisation of cudaMalloc / cudaFree. The scratch is a fixed 16 MiB array inside the library, held by every GPU
  * that loads it until the process exits; a grid and head count that need more return H3_ERR_ARG with the sizes.
- * Every call shares that array: calls whose work overlaps on the GPU race. The first call on a device looks up the
- * array's device address; make it before any stream capture. Queued on `stream`, not waited for (h3k_check). */
+ * Every call shares that array: calls whose work overlaps on the GPU race. The first call in each CUDA context (the
+ * device's primary context, normally) looks up the array's device address; make it before any stream capture. A
+ * context torn down and re-created (cudaDeviceReset) is recognised by its id and looked up afresh. Queued on
+ * `stream`, not waited for (h3k_check). */
 int h3k_sparse_attention_noalloc(const void* q, const void* k, const void* v, int64_t row_stride, int32_t heads,
                                  const h3k_cube_grid* g, float ratio, int32_t local, void* out, int64_t out_row_stride, void* stream);
 

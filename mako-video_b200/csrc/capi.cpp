@@ -174,8 +174,9 @@ struct Scratch {
 } // namespace
 
 namespace h3 {
-// For entry points defined in other translation units (noalloc.cu): sets what h3_last_error() returns.
-void set_last_error(const std::string& msg) { g_error = msg; }
+// For entry points defined in other translation units (noalloc.cu): runs f with the status mapping and error message
+// every other entry point uses.
+int run_guarded(const std::function<void()>& f) { return guarded(f); }
 } // namespace h3
 
 extern "C" {

@@ -1113,21 +1113,8 @@ void Model::step(const float* video, const float* audio, float t_video, float t_
         H3_CUDA(cudaEventRecord(d_->upload_done, s));
     }
 
-    // ---- inputs
-    const float* dv = video;
-    const float* da = audio;
-    if (!device_io) {
-        d_->in_video.ensure(size_t(std::max(V, 1)) * c_.video_patch * 4);
-        d_->in_audio.ensure(size_t(std::max(A, 1)) * c_.audio_channels * 4);
-        if (V)
-            H3_CUDA(cudaMemcpyAsync(d_->in_video.p, video, size_t(V) * c_.video_patch * 4, cudaMemcpyHostToDevice, s));
-        if (A)
-            H3_CUDA(cudaMemcpyAsync(d_->in_audio.p, audio, size_t(A) * c_.audio_channels * 4, cudaMemcpyHostToDevice, s));
-        dv = d_->in_video.as<float>();
-        da = d_->in_audio.as<float>();
-    }
     // Timing: an event after each kernel class (from a pool reused across steps); stage i is the time between
-    // events i - 1 and i, named by what ran in between.
+    // events i - 1 and i, named by what ran in between ("h2d" and "d2h": the host copies of a step with host I/O).
     size_t ev_used = 0;
     auto mark = [&](const char* name) {
         if (!timing_)
@@ -1141,6 +1128,21 @@ void Model::step(const float* video, const float* audio, float t_video, float t_
         stage_ms_.push_back({name, 0.f});
     };
     mark("start");
+
+    // ---- inputs
+    const float* dv = video;
+    const float* da = audio;
+    if (!device_io) {
+        d_->in_video.ensure(size_t(std::max(V, 1)) * c_.video_patch * 4);
+        d_->in_audio.ensure(size_t(std::max(A, 1)) * c_.audio_channels * 4);
+        if (V)
+            H3_CUDA(cudaMemcpyAsync(d_->in_video.p, video, size_t(V) * c_.video_patch * 4, cudaMemcpyHostToDevice, s));
+        if (A)
+            H3_CUDA(cudaMemcpyAsync(d_->in_audio.p, audio, size_t(A) * c_.audio_channels * 4, cudaMemcpyHostToDevice, s));
+        dv = d_->in_video.as<float>();
+        da = d_->in_audio.as<float>();
+        mark("h2d");
+    }
 
     // ---- time embedding and modulation
     d_->th.ensure(size_t(U) * d * 4);
@@ -1436,6 +1438,7 @@ void Model::step(const float* video, const float* audio, float t_video, float t_
             H3_CUDA(cudaMemcpyAsync(out_video + size_t(C) * c_.video_patch, vo, size_t(V - C) * c_.video_patch * 4,
                                     cudaMemcpyDeviceToHost, s));
     }
+    mark(device_io ? "output" : "d2h");
     if (timing_) {
         H3_CUDA(cudaStreamSynchronize(s));
         for (size_t i = 1; i < ev_used; ++i)

@@ -7,19 +7,22 @@
 //
 // The array below is held by every GPU that loads the library until the process exits. Every call shares it and it
 // keeps the last call's contents: calls whose work overlaps on the GPU (two streams, or two host threads) race on it.
-// Its device address is looked up once per device, on the first call made with that device current; make that first
-// call before any stream capture.
+// Its device address is looked up on the first call made in each CUDA context (normally once per device: the
+// device's primary context); make that first call before any stream capture. The lookup is keyed by the context's
+// process-unique id, so a context torn down and created again (cudaDeviceReset) gets a fresh lookup instead of the
+// old context's address.
 #include "h3_c.h"
 
 #include "attention.cuh"
 #include "common.hpp"
 #include "sparse.cuh"
 
+#include <functional>
 #include <mutex>
 #include <string>
 
 namespace h3 {
-void set_last_error(const std::string& msg); // capi.cpp: the message h3_last_error() returns
+int run_guarded(const std::function<void()>& f); // capi.cpp: the status codes and message of every entry point
 } // namespace h3
 
 namespace {
@@ -30,25 +33,60 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 
 constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mutex;
-void* g_scratch_addr[kMaxDevices] = {};
+struct ScratchAddr {
+    unsigned long long context_id = 0; // the context the address belongs to (0: none looked up yet)
+    void* addr = nullptr;
+};
+ScratchAddr g_scratch[kMaxDevices];
 
-// The scratch's device address for the current device (cudaGetSymbolAddress once per device). In host code the
+using CtxGetCurrent = CUresult (*)(CUcontext*);
+using CtxGetId = CUresult (*)(CUcontext, unsigned long long*);
+
+template <class Fn>
+Fn driver_fn(const char* name)
+{
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    H3_CUDA(cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q));
+    if (q != cudaDriverEntryPointSuccess || !p)
+        throw h3::CudaError(std::string(name) + " is not available from the driver");
+    return reinterpret_cast<Fn>(p);
+}
+
+// The process-unique id of the current context (the driver never hands the same id to two contexts, unlike the
+// context handle, which a re-created context may reuse).
+unsigned long long current_context_id()
+{
+    static const CtxGetCurrent get_current = driver_fn<CtxGetCurrent>("cuCtxGetCurrent");
+    static const CtxGetId get_id = driver_fn<CtxGetId>("cuCtxGetId");
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (get_current(&ctx) != CUDA_SUCCESS || !ctx || get_id(ctx, &id) != CUDA_SUCCESS)
+        throw h3::CudaError("no-allocation scratch: no current CUDA context");
+    return id;
+}
+
+// The scratch's device address in the current context (cudaGetSymbolAddress once per context). In host code the
 // array's name is only a stand-in, so kernels are always given this address.
 void* scratch_for_current_device()
 {
     int dev = 0;
     H3_CUDA(cudaGetDevice(&dev));
     if (dev < 0 || dev >= kMaxDevices)
-        throw h3::CudaError("h3k_sparse_attention_noalloc: device index out of range");
+        throw h3::CudaError("no-allocation scratch: device index out of range");
+    H3_CUDA(cudaSetDevice(dev)); // makes the device's primary context current if nothing has yet
+    const unsigned long long ctx = current_context_id();
     std::lock_guard<std::mutex> lock(g_scratch_mutex);
-    if (!g_scratch_addr[dev]) {
+    ScratchAddr& e = g_scratch[dev];
+    if (e.context_id != ctx || !e.addr) {
         void* p = nullptr;
         const cudaError_t rc = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (rc != cudaSuccess || !p)
-            throw h3::CudaError(std::string("h3k_sparse_attention_noalloc: cudaGetSymbolAddress failed: ") + cudaGetErrorString(rc));
-        g_scratch_addr[dev] = p;
+            throw h3::CudaError(std::string("no-allocation scratch: cudaGetSymbolAddress failed: ") + cudaGetErrorString(rc));
+        e.context_id = ctx;
+        e.addr = p;
     }
-    return g_scratch_addr[dev];
+    return e.addr;
 }
 
 size_t round256(size_t n) { return (n + 255) & ~size_t(255); }
@@ -59,7 +97,7 @@ extern "C" int h3k_sparse_attention_noalloc(const void* q, const void* k, const 
                                             const h3k_cube_grid* g, float ratio, int32_t local, void* out, int64_t out_row_stride,
                                             void* stream)
 {
-    try {
+    return h3::run_guarded([&] {
         if (!q || !k || !v || !out || !g || heads <= 0)
             throw std::invalid_argument("h3k_sparse_attention_noalloc: null argument or no heads");
         if (g->frames <= 0 || g->ph <= 0 || g->pw <= 0 || g->dense_rows < 0)
@@ -105,13 +143,5 @@ extern "C" int h3k_sparse_attention_noalloc(const void* q, const void* k, const 
         a.q = q, a.k = k, a.v = v, a.row_stride = row_stride, a.heads = heads, a.rows = c.dense_rows + c.frames * c.ph * c.pw;
         a.out = out, a.out_row_stride = out_row_stride;
         h3::sparse_attention(a, c, ratio, local, b, s);
-        h3::set_last_error("");
-        return H3_OK;
-    } catch (const std::invalid_argument& e) {
-        h3::set_last_error(e.what());
-        return H3_ERR_ARG;
-    } catch (const std::exception& e) {
-        h3::set_last_error(e.what());
-        return H3_ERR_CUDA;
-    }
+    });
 }

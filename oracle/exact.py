@@ -13,7 +13,7 @@ LIB = os.path.join(HERE, "libh3_exact.so")
 
 def build(force=False):
     if force or not os.path.exists(LIB) or os.path.getmtime(LIB) < os.path.getmtime(SRC):
-        subprocess.run(["gcc", "-O2", "-ffp-contract=off", "-shared", "-fPIC", "-o", LIB, SRC, "-lm"], check=True)
+        subprocess.run(["gcc", "-O2", "-ffp-contract=off", "-fopenmp", "-shared", "-fPIC", "-o", LIB, SRC, "-lm"], check=True)
     return LIB
 
 
@@ -29,8 +29,16 @@ def lib():
         L.h3x_cube_pool.argtypes = [P, P, I64, I, I, I, I, I, P, P]
         L.h3x_cube_scores.argtypes = [P, P, I, I, P]
         L.h3x_cube_topk.argtypes = [P, I, I, I, I, I, I, P, P, I]
+        L.h3x_synthetic.argtypes = [P, I64, ctypes.c_uint64, ctypes.c_float, ctypes.c_float, I]
         _lib = L
     return _lib
+
+
+def synthetic(n, key, mean, k, bf16):
+    """h3x_synthetic: the loop form of oracle/h3_oracle.py:synthetic (key and k as that function derives them)."""
+    out = np.empty(n, np.float32)
+    lib().h3x_synthetic(out.ctypes.data, n, key, float(mean), float(k), 1 if bf16 else 0)
+    return out
 
 
 def grid_cubes(frames, ph, pw):

@@ -10,7 +10,8 @@
  *   mean  = (sum over the cube's valid rows in cube order of float(x)) / count, sequential fp32 adds
  *   score = fmaf chain over the 128 dims in order
  *   pick  = forced cubes, then highest scores (ties to the lower index) until max(k, forced).
- * Build: gcc -O2 -shared -fPIC -o oracle/libh3_exact.so oracle/h3_exact.c -lm (done by __graft_entry__.build()). */
+ * Build: gcc -O2 -ffp-contract=off -fopenmp -shared -fPIC -o oracle/libh3_exact.so oracle/h3_exact.c -lm (done by
+ * __graft_entry__.build()). */
 #include <math.h>
 #include <stdint.h>
 #include <stdlib.h>
@@ -52,6 +53,8 @@ void h3x_cube_pool(const uint16_t* q, const uint16_t* k, int64_t row_stride, int
 
 void h3x_cube_scores(const float* mq, const float* mk, int heads, int cubes, float* scores)
 {
+    /* every score is its own fmaf chain, so splitting the heads over threads changes no result */
+#pragma omp parallel for schedule(static)
     for (int h = 0; h < heads; ++h)
         for (int i = 0; i < cubes; ++i)
             for (int j = 0; j < cubes; ++j) {
@@ -86,9 +89,10 @@ static int cmp_int(const void* a, const void* b) { return *(const int*)a - *(con
 void h3x_cube_topk(const float* scores, int heads, int frames, int ph, int pw, int k, int local, int32_t* sel, int32_t* nsel, int kcap)
 {
     const int nct = (frames + 3) / 4, ncy = (ph + 3) / 4, ncx = (pw + 3) / 4, nc = nct * ncy * ncx, plane = ncx * ncy;
-    cand* cs = (cand*)malloc(sizeof(cand) * (size_t)nc);
-    int* out = (int*)malloc(sizeof(int) * (size_t)nc);
-    for (int h = 0; h < heads; ++h)
+#pragma omp parallel for schedule(static)
+    for (int h = 0; h < heads; ++h) {
+        cand* cs = (cand*)malloc(sizeof(cand) * (size_t)nc);
+        int* out = (int*)malloc(sizeof(int) * (size_t)nc);
         for (int i = 0; i < nc; ++i) {
             const int ct = i / plane;
             int nout = 0, ncand = 0;
@@ -116,6 +120,36 @@ void h3x_cube_topk(const float* scores, int heads, int frames, int ph, int pw, i
                 sel[((int64_t)h * nc + i) * kcap + t] = out[t];
             nsel[(int64_t)h * nc + i] = n;
         }
-    free(cs);
-    free(out);
+        free(cs);
+        free(out);
+    }
+}
+
+/* The synthetic weights of oracle/h3_oracle.py:synthetic, as a loop (the numpy form is the definition; a CPU test
+ * pins the two together): value i = mean + k * s(i), s(i) = the sum of the four 16-bit fields of
+ * splitmix64(key + i) minus 131070, one fp32 multiply and one fp32 add (-ffp-contract=off keeps them apart), then
+ * optional bf16 rounding to nearest even. k = stdev / sqrt((65536^2 - 1) / 3), computed by the caller. */
+static uint64_t splitmix64(uint64_t x)
+{
+    x += 0x9E3779B97F4A7C15ull;
+    x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+    x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+    return x ^ (x >> 31);
+}
+
+void h3x_synthetic(float* out, int64_t n, uint64_t key, float mean, float k, int bf16)
+{
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; ++i) {
+        const uint64_t h = splitmix64(key + (uint64_t)i);
+        const int64_t s = (int64_t)(h & 0xFFFF) + (int64_t)((h >> 16) & 0xFFFF) + (int64_t)((h >> 32) & 0xFFFF) + (int64_t)(h >> 48) - 131070;
+        float v = mean + k * (float)s;
+        if (bf16) {
+            uint32_t u;
+            memcpy(&u, &v, 4);
+            u = (u + 0x7FFFu + ((u >> 16) & 1u)) & 0xFFFF0000u;
+            memcpy(&v, &u, 4);
+        }
+        out[i] = v;
+    }
 }

@@ -66,7 +66,19 @@ def bf16_round(a):
 def synthetic(n, seed, tensor_id, mean=0.0, stdev=0.02, bf16=False):
     """Value i = mean + stdev * IH4(seed, tensor_id, i): the centred sum of four 16-bit fields of a splitmix64 hash
     (an Irwin-Hall approximation of a unit normal), one fp32 multiply and one fp32 add, then optional bf16
-    rounding. Bit-identical to the library's fill_synthetic."""
+    rounding. Bit-identical to the library's fill_synthetic. Large tensors go through the same arithmetic written as
+    a C loop (oracle/h3_exact.c: h3x_synthetic; pinned to synthetic_np by a CPU test): the numpy form takes minutes
+    for a 5120-wide model's weights."""
+    if n >= (1 << 20):
+        from oracle import exact
+        key = _splitmix64_int((seed * 0x632BE59BD9B4E019 + tensor_id) & M64)
+        norm = 1.0 / math.sqrt((65536.0 * 65536.0 - 1.0) / 3.0)
+        return exact.synthetic(n, key, np.float32(mean), np.float32(float(np.float32(stdev)) * norm), bf16)
+    return synthetic_np(n, seed, tensor_id, mean, stdev, bf16)
+
+
+def synthetic_np(n, seed, tensor_id, mean=0.0, stdev=0.02, bf16=False):
+    """The numpy definition of `synthetic`."""
     key = _splitmix64_int((seed * 0x632BE59BD9B4E019 + tensor_id) & M64)
     with np.errstate(over="ignore"):
         h = _splitmix64_np(np.uint64(key) + np.arange(n, dtype=np.uint64))

@@ -96,7 +96,9 @@ def geometry(ref):
 
 
 if __name__ == "__main__":
-    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("MAKO_REFERENCE", "/root/reference")
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("MAKO_REFERENCE")
+    if not ref:
+        sys.exit("usage: make_golden.py REFERENCE_CHECKOUT (or set MAKO_REFERENCE): the mako-video source tree to read")
     time_adaln(ref)
     rope_freq(ref)
     geometry(ref)

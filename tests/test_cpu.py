@@ -65,6 +65,15 @@ def test_synthetic_values_are_deterministic_and_normal_like():
     assert (bf.view(np.uint32) & 0xFFFF).max() == 0
 
 
+@pytest.mark.parametrize("seed,tid,mean,stdev,bf16", [(0, 7, 0.0, 0.02, False), (3, 104, 1.0, 0.02, False),
+                                                      (5, 123, 0.0, 0.02, True), (11, 2, 0.0, 1.0, False), (0, 18, 0.0, 4.0, True)])
+def test_synthetic_c_loop_equals_the_numpy_definition(seed, tid, mean, stdev, bf16):
+    """Large tensors use the C loop form of the generator; it must give the numpy definition's bits."""
+    n = (1 << 20) + 37
+    np.testing.assert_array_equal(O.synthetic(n, seed, tid, mean, stdev, bf16).view(np.uint32),
+                                  O.synthetic_np(n, seed, tid, mean, stdev, bf16).view(np.uint32))
+
+
 def test_bf16_round_half_even():
     x = np.array([1.0, 1.00390625, 1.01171875, -2.5, 3.0e-39], np.float32)  # exact halves at bf16 spacing 2^-7
     r = O.bf16_round(x)
