@@ -143,9 +143,10 @@ int h3_weight_specs(const h3_config* cfg, char* out, uint64_t cap, uint32_t* cou
 /* Rewrites the checkpoint at src (a safetensors file or a directory of them) as a file at dst in the layout h3_create
  * reads, for a model of shape cfg: every tensor under this library's name, the model's element type, q/k/v stacked.
  * renames (may be NULL): lines "this_name source_name" for tensors the source names otherwise, '#' lines ignored,
- * and "qkv_layout interleaved" when the source keeps each head's q, k and v rows together without saying so in its
- * metadata (the reference's shards, docs/architecture.md:62-63). The source is checked first (a missing tensor or a
- * shape that disagrees: H3_ERR_ARG). Host only. No counterpart in the reference: the path from its FL2VA files (whose
+ * and "qkv_layout interleaved" (or "qkv_layout stacked") for a source whose metadata does not say how it keeps each
+ * head's q, k and v rows (the reference's shards keep them together, docs/architecture.md:62-63): the shapes cannot
+ * tell the two apart, so a source file with q/k/v tensors and no qkv_layout metadata is refused (H3_ERR_ARG) unless
+ * that line is given. The source is checked first (a missing tensor or a shape that disagrees: H3_ERR_ARG). Host only. No counterpart in the reference: the path from its FL2VA files (whose
  * block-internal tensor names are not in the reference tree) to this library. */
 int h3_convert_weights(const h3_config* cfg, const char* src, const char* dst, const char* renames);
 

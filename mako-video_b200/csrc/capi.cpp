@@ -339,7 +339,7 @@ int h3_convert_weights(const h3_config* cfg, const char* src, const char* dst, c
         if (!cfg || !src || !dst)
             throw ArgError("h3_convert_weights: null argument");
         std::map<std::string, std::string> table;
-        bool interleaved = false;
+        bool interleaved = false, layout_given = false;
         if (renames) {
             std::istringstream in(renames);
             std::string line;
@@ -354,12 +354,13 @@ int h3_convert_weights(const h3_config* cfg, const char* src, const char* dst, c
                     if (b != "interleaved" && b != "stacked")
                         throw ArgError("h3_convert_weights: qkv_layout is interleaved or stacked");
                     interleaved = b == "interleaved";
+                    layout_given = true;
                     continue;
                 }
                 table[a] = b;
             }
         }
-        h3::convert_checkpoint(to_config(cfg), src, dst, std::move(table), interleaved);
+        h3::convert_checkpoint(to_config(cfg), src, dst, std::move(table), interleaved, layout_given);
     });
 }
 

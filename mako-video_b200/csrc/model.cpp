@@ -388,6 +388,8 @@ void SyntheticWeights::get(const WeightSpec& spec, void* dst, cudaStream_t s)
 struct CheckpointWeights::Files {
     std::vector<std::unique_ptr<SafeTensors>> files;
     std::vector<bool> interleaved;       // per file: metadata qkv_layout = interleaved
+    std::vector<bool> tagged;            // per file: the metadata has a qkv_layout entry
+    std::vector<std::string> paths;
     std::map<std::string, size_t> where; // tensor name -> file
     std::map<std::string, std::string> renames;
     // the checkpoint's name of a weight
@@ -423,6 +425,8 @@ CheckpointWeights::CheckpointWeights(const std::string& path, std::map<std::stri
         }
         const auto it = st->metadata().find("qkv_layout");
         f_->interleaved.push_back(interleaved || (it != st->metadata().end() && it->second == "interleaved"));
+        f_->tagged.push_back(it != st->metadata().end());
+        f_->paths.push_back(p);
         for (const auto& [name, t] : st->tensors())
             if (!f_->where.emplace(name, f_->files.size()).second)
                 throw std::invalid_argument("checkpoint: tensor " + name + " appears in two files");
@@ -454,6 +458,24 @@ std::string CheckpointWeights::check(const Config& c) const
     return "";
 }
 
+static bool is_qkv(const std::string& name)
+{
+    return (name.size() > 15 && name.compare(name.size() - 15, 15, "attn.qkv.weight") == 0) ||
+           (name.size() > 13 && name.compare(name.size() - 13, 13, "attn.qkv.bias") == 0);
+}
+
+std::string CheckpointWeights::untagged_qkv_file(const Config& c) const
+{
+    for (const WeightSpec& sp : weight_specs(c)) {
+        if (!is_qkv(sp.name))
+            continue;
+        const auto it = f_->where.find(f_->source(sp.name));
+        if (it != f_->where.end() && !f_->tagged[it->second])
+            return f_->paths[it->second];
+    }
+    return "";
+}
+
 void CheckpointWeights::get(const WeightSpec& spec, void* dst, cudaStream_t s)
 {
     const std::vector<unsigned char> h = host(spec);
@@ -479,9 +501,7 @@ std::vector<unsigned char> CheckpointWeights::host(const WeightSpec& spec) const
         const std::vector<float> v = st.read_f32(src);
         std::memcpy(host.data(), v.data(), host.size());
     }
-    const bool qkv = spec.name.size() > 15 && (spec.name.compare(spec.name.size() - 15, 15, "attn.qkv.weight") == 0 ||
-                                                spec.name.compare(spec.name.size() - 13, 13, "attn.qkv.bias") == 0);
-    if (qkv && f_->interleaved[it->second]) {
+    if (is_qkv(spec.name) && f_->interleaved[it->second]) {
         // [q_h; k_h; v_h] for every head h -> [q (all heads); k; v]
         const int64_t rows = spec.shape[0], cols = spec.shape.size() > 1 ? spec.shape[1] : 1, inner = rows / 3;
         const size_t row_bytes = size_t(cols) * esz;
@@ -496,12 +516,19 @@ std::vector<unsigned char> CheckpointWeights::host(const WeightSpec& spec) const
 }
 
 void convert_checkpoint(const Config& c, const std::string& src, const std::string& dst, std::map<std::string, std::string> renames,
-                        bool interleaved)
+                        bool interleaved, bool layout_given)
 {
     const CheckpointWeights ck(src, std::move(renames), interleaved);
     const std::string problem = ck.check(c);
     if (!problem.empty())
         throw std::invalid_argument("convert: " + src + ": " + problem);
+    if (!layout_given) {
+        const std::string untagged = ck.untagged_qkv_file(c);
+        if (!untagged.empty())
+            throw std::invalid_argument("convert: " + untagged + " holds q/k/v tensors but its metadata has no qkv_layout: add a "
+                                        "\"qkv_layout interleaved\" or \"qkv_layout stacked\" line (the reference's shards keep "
+                                        "each head's q, k, v rows together)");
+    }
     const std::vector<WeightSpec> specs = weight_specs(c);
     std::vector<SafeTensorOut> outs;
     for (const WeightSpec& sp : specs) {

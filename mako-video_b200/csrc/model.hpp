@@ -129,8 +129,10 @@ std::vector<WeightSpec> weight_specs(const Config& c);
 
 // Writes a checkpoint for a model of shape c in this build's layout (its names, stacked q/k/v, the model's element
 // types) from the checkpoint at `src` read through `renames` / `interleaved` as CheckpointWeights reads it. Host only.
+// layout_given: the caller stated the source's q/k/v layout; without it a source file that holds q/k/v tensors but
+// no qkv_layout metadata is refused (the shapes cannot tell interleaved from stacked rows).
 void convert_checkpoint(const Config& c, const std::string& src, const std::string& dst, std::map<std::string, std::string> renames,
-                        bool interleaved);
+                        bool interleaved, bool layout_given);
 
 // Where a model's weights come from: spec's values, in its logical layout and element type, written to device memory.
 class WeightSource {
@@ -165,6 +167,8 @@ public:
     // The first problem a model of shape c would meet loading this checkpoint ("" if none): a missing tensor or a
     // shape that disagrees. Host only.
     std::string check(const Config& c) const;
+    // A file holding one of c's q/k/v tensors whose metadata does not say its qkv_layout ("" if none).
+    std::string untagged_qkv_file(const Config& c) const;
 
 private:
     struct Files;

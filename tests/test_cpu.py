@@ -431,6 +431,30 @@ def test_convert_renames_and_stacks_a_foreign_checkpoint(tmp_path):
         h3b200.convert_weights(cfg, tmp_path / "src.safetensors", tmp_path / "x.safetensors")  # the renames are needed
 
 
+def test_convert_refuses_an_untagged_qkv_layout_unless_stated(tmp_path):
+    """A source without qkv_layout metadata could hold q/k/v rows per head (the reference's shards) or stacked; the
+    shapes are the same, so h3_convert_weights refuses to guess: it needs a "qkv_layout interleaved|stacked" line."""
+    from tests import safetensors_util as ST
+
+    cfg = dict(dim=256, heads=2, ffn=512, blocks=1, time_dim=128, text_dim=256, refiner=0)
+    rng = np.random.default_rng(1)
+    src = {n: rng.standard_normal(s).astype(np.float32) for n, _, s in h3b200.weight_specs(cfg)}
+    ST.write(tmp_path / "untagged.safetensors", src, dtype="F32")
+    with pytest.raises(h3b200.H3Error) as e:
+        h3b200.convert_weights(cfg, tmp_path / "untagged.safetensors", tmp_path / "out.safetensors")
+    assert e.value.code == h3b200.H3_ERR_ARG and "qkv_layout" in str(e.value)
+    cfgc = h3b200.make_config(cfg)
+    lib = h3b200.lib()
+    assert lib.h3_convert_weights(ctypes.byref(cfgc), str(tmp_path / "untagged.safetensors").encode(),
+                                  str(tmp_path / "out.safetensors").encode(), b"qkv_layout stacked") == h3b200.H3_OK
+    got, _, meta = ST.read(tmp_path / "out.safetensors")
+    assert meta["qkv_layout"] == "stacked"
+    np.testing.assert_array_equal(got["blocks.0.attn.qkv.bias"], src["blocks.0.attn.qkv.bias"])
+    h3b200.convert_weights(cfg, tmp_path / "untagged.safetensors", tmp_path / "out2.safetensors", interleaved=True)
+    got2, _, _ = ST.read(tmp_path / "out2.safetensors")
+    assert not np.array_equal(got2["blocks.0.attn.qkv.bias"], src["blocks.0.attn.qkv.bias"])
+
+
 def test_h3_shape_holds_the_reference_parameter_counts():
     """MiniMax-H3's shape in this build (dim 5376, 56 heads of 128, SwiGLU 14336, 50 blocks, time 2688, the two-block
     token refiner) holds the sizes the reference documents: 20 B parameters without the AdaLN projections and 33 B with
