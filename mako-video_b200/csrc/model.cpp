@@ -782,6 +782,36 @@ void Model::set_sparse(float ratio, int local)
         throw CudaError("sparse-local must be 0, 1 or 3");
     sparse_ratio_ = ratio;
     sparse_local_ = local;
+    if (begun_) {
+        // the layout is known: size the selection and pass-list buffers for the new ratio now (the reference sets
+        // the ratio before begin, engine.cpp:112; a caller may also change it between steps)
+        size_sparse();
+        H3_CUDA(cudaStreamSynchronize(stream_));
+    }
+}
+
+// The sparse attention's buffers for this layout's cube grid and the current ratio (kept, and only grown, while the
+// ratio is zero or the grid has no cubes).
+void Model::size_sparse()
+{
+    const CubeGrid& g = d_->grid;
+    if (!(sparse_ratio_ > 0.f) || g.cubes() <= 0)
+        return;
+    const int Hp = c_.heads / world_.size;
+    SparseBuffers& b = d_->sp;
+    sparse_sizes(g, sparse_ratio_, sparse_local_, b.kcap, b.q_tiles, b.max_blocks);
+    const size_t nc = g.cubes();
+    d_->sp_mq.ensure(size_t(Hp) * nc * 128 * 4);
+    d_->sp_mk.ensure(size_t(Hp) * nc * 128 * 4);
+    d_->sp_scores.ensure(size_t(Hp) * nc * nc * 4);
+    d_->sp_sel.ensure(size_t(Hp) * nc * b.kcap * 4);
+    d_->sp_nsel.ensure(size_t(Hp) * nc * 4);
+    d_->sp_blocks.ensure(size_t(Hp) * b.q_tiles * b.max_blocks * 16);
+    d_->sp_nblocks.ensure(size_t(Hp) * b.q_tiles * 4);
+    d_->sp_qrows.ensure(size_t(b.q_tiles) * 16);
+    b.mq = d_->sp_mq.as<float>(), b.mk = d_->sp_mk.as<float>(), b.scores = d_->sp_scores.as<float>();
+    b.sel = d_->sp_sel.as<int32_t>(), b.nsel = d_->sp_nsel.as<int32_t>();
+    b.blocks = d_->sp_blocks.as<int4>(), b.nblocks = d_->sp_nblocks.as<int32_t>(), b.q_rows = d_->sp_qrows.as<int4>();
 }
 
 void Model::alloc_activations()
@@ -940,26 +970,7 @@ void Model::begin(const float* text, int T, const Layout& l)
     H3_CUDA(cudaMemcpyAsync(d_->rope.p, local.data(), local.size() * 4, cudaMemcpyHostToDevice, s));
     d_->mod_idx.ensure(S_local_);
     d_->lvl_idx.ensure(S_local_);
-    // sparse buffers
-    if (sparse_ratio_ > 0.f) {
-        if (g.cubes() > 0) {
-            const int Hp = c_.heads / P;
-            SparseBuffers& b = d_->sp;
-            sparse_sizes(g, sparse_ratio_, sparse_local_, b.kcap, b.q_tiles, b.max_blocks);
-            const size_t nc = g.cubes();
-            d_->sp_mq.ensure(size_t(Hp) * nc * 128 * 4);
-            d_->sp_mk.ensure(size_t(Hp) * nc * 128 * 4);
-            d_->sp_scores.ensure(size_t(Hp) * nc * nc * 4);
-            d_->sp_sel.ensure(size_t(Hp) * nc * b.kcap * 4);
-            d_->sp_nsel.ensure(size_t(Hp) * nc * 4);
-            d_->sp_blocks.ensure(size_t(Hp) * b.q_tiles * b.max_blocks * 16);
-            d_->sp_nblocks.ensure(size_t(Hp) * b.q_tiles * 4);
-            d_->sp_qrows.ensure(size_t(b.q_tiles) * 16);
-            b.mq = d_->sp_mq.as<float>(), b.mk = d_->sp_mk.as<float>(), b.scores = d_->sp_scores.as<float>();
-            b.sel = d_->sp_sel.as<int32_t>(), b.nsel = d_->sp_nsel.as<int32_t>();
-            b.blocks = d_->sp_blocks.as<int4>(), b.nblocks = d_->sp_nblocks.as<int32_t>(), b.q_rows = d_->sp_qrows.as<int4>();
-        }
-    }
+    size_sparse();
     H3_CUDA(cudaStreamSynchronize(s));
     begun_ = true;
 }

@@ -249,6 +249,7 @@ private:
     std::vector<std::pair<std::string, float>> stage_ms_;
     bool begun_ = false;
     void alloc_activations();
+    void size_sparse(); // the sparse attention's buffers for the layout's grid and the current ratio
     void refine_text(int T); // the token refiner over x_text (begin)
     void init(WeightSource& src); // the constructors' body: checks, stream, communicator, weights
     struct Target;

@@ -3,6 +3,7 @@
 #include "ptx.cuh"
 #include "rows.cuh"
 
+#include <algorithm>
 #include <cmath>
 
 namespace h3 {
@@ -25,22 +26,6 @@ __device__ __forceinline__ float warp_max(float v)
     return v;
 }
 
-// Block-wide sum for a CTA of NT threads (NT a multiple of 32); every thread gets the total.
-template <int NT>
-__device__ __forceinline__ float block_sum(float v, float* red)
-{
-    v = warp_sum(v);
-    if (lane_id() == 0)
-        red[warp_id()] = v;
-    __syncthreads();
-    float t = 0.f;
-#pragma unroll
-    for (int i = 0; i < NT / 32; ++i)
-        t += red[i];
-    __syncthreads();
-    return t;
-}
-
 template <int NT>
 __device__ __forceinline__ float block_max(float v, float* red)
 {
@@ -56,80 +41,117 @@ __device__ __forceinline__ float block_max(float v, float* red)
     return t;
 }
 
-constexpr int RMS_NT = 128;
-constexpr int RMS_VPT = 16; // float4 per thread: rows up to 128 * 16 * 4 = 8192 wide
+constexpr size_t kRmsStreamSmem = 172032; // row slots of the streaming kernel: 4 warps x 2 rows of 5376 floats
 
-// One CTA per row; the row is held in registers between the reduction and the output pass.
-__global__ void __launch_bounds__(RMS_NT) rms_mod_kernel(const RmsModParams p)
+// y = RMSNorm(x) * w * (1 + scale[r]) + shift[r] per row, bf16, fp32 or int8 (+ row scale) out. A persistent kernel
+// that streams rows through shared memory: each warp owns two row slots
+// and keeps the next row's bulk copy in flight while it works on the current one (eight rows of HBM reads in flight
+// per SM with four warps), reads the row twice from shared memory (sum of squares, then the output) and the shift,
+// scale and weight vectors through L1 (consecutive rows share them). Rows r = (CTA x warps + warp) + i x grid x warps.
+// Shared memory: [warps][2] mbarriers (256 bytes), then [warps][2][d] fp32 row slots.
+__global__ void __launch_bounds__(256) rms_mod_stream_kernel(const RmsModParams p)
 {
-    __shared__ float red[RMS_NT / 32];
-    const int r = blockIdx.x;
-    const int n4 = p.d / 4;
-    const float4* x4 = reinterpret_cast<const float4*>(p.x + size_t(r) * p.ldx);
-    float4 v[RMS_VPT];
-    float ss = 0.f;
-#pragma unroll
-    for (int i = 0; i < RMS_VPT; ++i) {
-        const int c = threadIdx.x + i * RMS_NT;
-        if (c < n4) {
-            v[i] = x4[c];
-            ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+    extern __shared__ __align__(128) uint8_t rm_smem[];
+    const int nw = blockDim.x >> 5, w = warp_id(), lane = lane_id();
+    const uint32_t row_bytes = uint32_t(p.d) * 4;
+    uint64_t* bar = reinterpret_cast<uint64_t*>(rm_smem) + 2 * w;
+    float* buf = reinterpret_cast<float*>(rm_smem + 256) + size_t(2 * w) * p.d;
+    const int stride = gridDim.x * nw;
+    const int first = blockIdx.x * nw + w;
+    if (lane == 0) {
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
+        fence_barrier_init();
+        for (int k = 0; k < 2; ++k) {
+            const int r = first + k * stride;
+            if (r < p.rows) {
+                mbar_arrive_expect_tx(&bar[k], row_bytes);
+                bulk_load(buf + size_t(k) * p.d, p.x + size_t(r) * p.ldx, row_bytes, &bar[k]);
+            }
         }
     }
-    ss = block_sum<RMS_NT>(ss, red);
-    const float rinv = rsqrtf(ss / float(p.d) + p.eps);
-    const int m = p.mod_idx ? p.mod_idx[r] : 0;
-    const float4* sh4 = reinterpret_cast<const float4*>(p.mod + (size_t(m) * p.mod_slots + p.shift_slot) * p.d);
-    const float4* sc4 = reinterpret_cast<const float4*>(p.mod + (size_t(m) * p.mod_slots + p.scale_slot) * p.d);
-    const float4* w4 = reinterpret_cast<const float4*>(p.w);
-    float amax = 0.f;
-#pragma unroll
-    for (int i = 0; i < RMS_VPT; ++i) {
-        const int c = threadIdx.x + i * RMS_NT;
+    __syncwarp();
+    const int n4 = p.d >> 2;
+    int it = 0;
+    bool ok = true;
+    for (int r = first; r < p.rows; r += stride, ++it) {
+        const int slot = it & 1;
+        float4* x4 = reinterpret_cast<float4*>(buf + size_t(slot) * p.d);
+        if (!(ok = mbar_wait(&bar[slot], (it >> 1) & 1)))
+            break;
+        float ss0 = 0.f, ss1 = 0.f;
+        int c = lane;
+        for (; c + 32 < n4; c += 64) {
+            const float4 a = x4[c], b = x4[c + 32];
+            ss0 += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w;
+            ss1 += b.x * b.x + b.y * b.y + b.z * b.z + b.w * b.w;
+        }
         if (c < n4) {
-            const float4 sh = __ldg(sh4 + c), sc = __ldg(sc4 + c);
-            float4 w = make_float4(1.f, 1.f, 1.f, 1.f);
-            if (p.w)
-                w = __ldg(w4 + c);
-            v[i].x = v[i].x * rinv * w.x * (1.f + sc.x) + sh.x;
-            v[i].y = v[i].y * rinv * w.y * (1.f + sc.y) + sh.y;
-            v[i].z = v[i].z * rinv * w.z * (1.f + sc.z) + sh.z;
-            v[i].w = v[i].w * rinv * w.w * (1.f + sc.w) + sh.w;
-            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+            const float4 a = x4[c];
+            ss0 += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w;
         }
-    }
-    if (p.out_kind == RowOut::bf16) {
-        uint2* o = reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(p.out) + size_t(r) * p.ldo);
-#pragma unroll
-        for (int i = 0; i < RMS_VPT; ++i) {
-            const int c = threadIdx.x + i * RMS_NT;
-            if (c < n4)
-                o[c] = make_uint2(pack_bf16x2(v[i].x, v[i].y), pack_bf16x2(v[i].z, v[i].w));
-        }
-    } else if (p.out_kind == RowOut::f32) {
-        float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + size_t(r) * p.ldo);
-#pragma unroll
-        for (int i = 0; i < RMS_VPT; ++i) {
-            const int c = threadIdx.x + i * RMS_NT;
-            if (c < n4)
-                o[c] = v[i];
-        }
-    } else {
-        // The GEMM input is the bf16 rounding of y (as in the bf16 path), quantised per row.
-        amax = block_max<RMS_NT>(amax, red);
-        const float inv = amax > 0.f ? 127.0f / __bfloat162float(__float2bfloat16_rn(amax)) : 0.f;
-        if (threadIdx.x == 0)
-            p.out_scale[r] = __bfloat162float(__float2bfloat16_rn(amax)) / 127.0f;
-        char4* o = reinterpret_cast<char4*>(reinterpret_cast<int8_t*>(p.out) + size_t(r) * p.ldo);
-        auto q = [&](float a) {
-            const float b = __bfloat162float(__float2bfloat16_rn(a));
-            return static_cast<signed char>(fminf(fmaxf(rintf(b * inv), -127.f), 127.f));
+        const float rinv = rsqrtf(warp_sum(ss0 + ss1) / float(p.d) + p.eps);
+        const int m = p.mod_idx ? p.mod_idx[r] : 0;
+        const float4* sh4 = reinterpret_cast<const float4*>(p.mod + (size_t(m) * p.mod_slots + p.shift_slot) * p.d);
+        const float4* sc4 = reinterpret_cast<const float4*>(p.mod + (size_t(m) * p.mod_slots + p.scale_slot) * p.d);
+        const float4* w4 = reinterpret_cast<const float4*>(p.w);
+        auto y_of = [&](int c) {
+            const float4 v = x4[c], sh = __ldg(sh4 + c), sc = __ldg(sc4 + c);
+            const float4 wt = p.w ? __ldg(w4 + c) : make_float4(1.f, 1.f, 1.f, 1.f);
+            return make_float4(v.x * rinv * wt.x * (1.f + sc.x) + sh.x, v.y * rinv * wt.y * (1.f + sc.y) + sh.y,
+                               v.z * rinv * wt.z * (1.f + sc.z) + sh.z, v.w * rinv * wt.w * (1.f + sc.w) + sh.w);
         };
-#pragma unroll
-        for (int i = 0; i < RMS_VPT; ++i) {
-            const int c = threadIdx.x + i * RMS_NT;
-            if (c < n4)
-                o[c] = make_char4(q(v[i].x), q(v[i].y), q(v[i].z), q(v[i].w));
+        if (p.out_kind == RowOut::bf16) {
+            uint2* o = reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(p.out) + size_t(r) * p.ldo);
+#pragma unroll 4
+            for (int c = lane; c < n4; c += 32) {
+                const float4 y = y_of(c);
+                o[c] = make_uint2(pack_bf16x2(y.x, y.y), pack_bf16x2(y.z, y.w));
+            }
+        } else if (p.out_kind == RowOut::f32) {
+            float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + size_t(r) * p.ldo);
+#pragma unroll 4
+            for (int c = lane; c < n4; c += 32)
+                o[c] = y_of(c);
+        } else {
+            // the GEMM input is the bf16 rounding of y (as in the bf16 path), quantised per row: y's bf16 values go
+            // back into the slot, then a third pass quantises them by the row's maximum
+            auto r16 = [](float a) { return __bfloat162float(__float2bfloat16_rn(a)); };
+            float amax = 0.f;
+#pragma unroll 4
+            for (int c = lane; c < n4; c += 32) {
+                float4 y = y_of(c);
+                y = make_float4(r16(y.x), r16(y.y), r16(y.z), r16(y.w));
+                amax = fmaxf(amax, fmaxf(fmaxf(fabsf(y.x), fabsf(y.y)), fmaxf(fabsf(y.z), fabsf(y.w))));
+                x4[c] = y;
+            }
+            amax = warp_max(amax);
+            const float inv = amax > 0.f ? 127.0f / amax : 0.f;
+            if (lane == 0)
+                p.out_scale[r] = amax / 127.0f;
+            __syncwarp();
+            auto q = [&](float b) { return static_cast<signed char>(fminf(fmaxf(rintf(b * inv), -127.f), 127.f)); };
+            char4* o = reinterpret_cast<char4*>(reinterpret_cast<int8_t*>(p.out) + size_t(r) * p.ldo);
+            for (int c = lane; c < n4; c += 32) {
+                const float4 y = x4[c];
+                o[c] = make_char4(q(y.x), q(y.y), q(y.z), q(y.w));
+            }
+        }
+        // the slot's reads (and the int8 pass's writes) come before the next bulk copy into it
+        fence_proxy_async_smem();
+        __syncwarp();
+        const int next = r + 2 * stride;
+        if (lane == 0 && next < p.rows) {
+            mbar_arrive_expect_tx(&bar[slot], row_bytes);
+            bulk_load(buf + size_t(slot) * p.d, p.x + size_t(next) * p.ldx, row_bytes, &bar[slot]);
+        }
+    }
+    if (!ok && lane == 0) {
+        // a wait ran out: let this warp's copies still in flight land before the CTA's shared memory is released
+        for (int k = 1; k < 3; ++k) {
+            const int r = first + (it + k - 1) * stride;
+            if (r < p.rows)
+                mbar_wait(&bar[(it + k - 1) & 1], ((it + k - 1) >> 1) & 1, 100000000ll);
         }
     }
 }
@@ -396,11 +418,21 @@ int grid_for(size_t work, int threads)
 
 void rms_mod_rows(const RmsModParams& p, cudaStream_t s)
 {
-    if (p.d % 4 || p.d > RMS_NT * RMS_VPT * 4 || !p.mod || !p.out || (p.out_kind == RowOut::s8 && !p.out_scale))
+    const size_t slot_bytes = size_t(p.d) * 4;
+    const int nw = int(std::min<size_t>(4, kRmsStreamSmem / (2 * std::max<size_t>(slot_bytes, 16))));
+    if (p.d <= 0 || p.d % 4 || nw < 1 || !p.x || !p.mod || !p.out || (p.out_kind == RowOut::s8 && !p.out_scale))
         throw CudaError("rms_mod_rows: bad arguments");
+    // 16-byte aligned rows for the bulk copies and the vector loads and stores
+    if (reinterpret_cast<uintptr_t>(p.x) % 16 || p.ldx % 4 || reinterpret_cast<uintptr_t>(p.out) % 16 || p.ldo % 4 ||
+        (p.w && reinterpret_cast<uintptr_t>(p.w) % 16) || reinterpret_cast<uintptr_t>(p.mod) % 16)
+        throw CudaError("rms_mod_rows: rows and vectors must start on 16-byte boundaries");
     if (p.rows == 0)
         return;
-    rms_mod_kernel<<<p.rows, RMS_NT, 0, s>>>(p);
+    const int smem = 256 + int(nw * 2 * slot_bytes);
+    static std::atomic<uint64_t> opt_in;
+    smem_opt_in(rms_mod_stream_kernel, 256 + int(kRmsStreamSmem), opt_in);
+    const int grid = int(std::min<int64_t>(num_sms(), (int64_t(p.rows) + nw - 1) / nw));
+    rms_mod_stream_kernel<<<grid, nw * 32, smem, s>>>(p);
     H3_CUDA(cudaGetLastError());
 }
 

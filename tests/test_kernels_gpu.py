@@ -197,8 +197,10 @@ def test_gemm_swiglu_epilogue(cuda):
 
 # ----------------------------------------------------------------------------------------------- row kernels
 
-def test_rms_mod_rows(cuda):
-    M, d = 333, 1024
+@pytest.mark.parametrize("M,d", [(333, 1024), (2000, 5120), (1777, 5376)])
+def test_rms_mod_rows(cuda, M, d):
+    """The modulated RMS norm (a persistent kernel streaming rows through shared memory; the larger cases give every
+    warp several rows, so its two row slots are reused) against the fp32 restatement; int8 output bit for bit."""
     x = torch.randn(M, d, device=cuda) * 3
     w = 1 + 0.1 * torch.randn(d, device=cuda)
     mod = torch.randn(6, 6, d, device=cuda) * 0.2

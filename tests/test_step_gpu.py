@@ -148,6 +148,29 @@ def test_step_is_deterministic_and_reuses_begin(cuda):
     assert not np.array_equal(a[0], c[0])
 
 
+def test_set_sparse_after_begin_takes_effect(cuda):
+    """H3::set_sparse between begin and step (or between steps) switches the attention: the same bits as a model
+    created with that ratio, and back to the dense model's bits at ratio 0."""
+    lay, text, video, audio = inputs(MINI_LAYOUT, MINI)
+
+    def run(create_ratio, then=None):
+        m = H.Model(MINI, seed=4, sparse_ratio=create_ratio, sparse_local=1)
+        m.begin(text, lay)
+        outs = [m.step(video, audio, 0.7, 0.4)]
+        for r in then or ():
+            m.set_sparse(r, 1)
+            outs.append(m.step(video, audio, 0.7, 0.4))
+        m.close()
+        return outs
+
+    dense, sparse = run(0.0)[0], run(0.3)[0]
+    assert not np.array_equal(dense[0], sparse[0])
+    switched = run(0.0, then=[0.3, 0.0])
+    for got, want in zip(switched, (dense, sparse, dense)):
+        np.testing.assert_array_equal(got[0], want[0])
+        np.testing.assert_array_equal(got[1], want[1])
+
+
 def test_step_errors(cuda):
     m = H.Model(MINI, seed=4)
     lay, text, video, audio = inputs(MINI_LAYOUT, MINI)
