@@ -435,15 +435,18 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
     const int warp = warp_id();
-    // Launches are 1-D, head by head, so that a head's keys and values are read from HBM about once and then served
-    // from L2 to all of its tiles: first the head's dense-row query tiles (which see every key, several times a video
-    // tile's work, so they start first), then its video tiles.
+    // Launches are 1-D and longest first: the dense-row query tiles (which see every key, several times a video
+    // tile's work) of every head, then each head's video tiles together (they share the head's keys in L2). Grouping
+    // each head's dense-row tiles with its video tiles instead halves the HBM reads (1.03 against 2.42 GB a 768p
+    // launch) but was measured 9% slower: the long tiles then finish last.
     int tile, head;
     {
         const int vt = (p.grid.cubes() + 1) / 2, dt = p.q_tiles - vt;
-        head = blockIdx.x / p.q_tiles;
-        const int r = blockIdx.x - head * p.q_tiles;
-        tile = r < dt ? vt + r : r - dt;
+        const int id = blockIdx.x;
+        if (id < p.heads * dt)
+            head = id % p.heads, tile = vt + id / p.heads;
+        else
+            head = (id - p.heads * dt) / vt, tile = (id - p.heads * dt) % vt;
     }
     int nkv = p.nblocks[head * p.q_tiles + tile];
     const bool every = nkv < 0; // a dense-row tile: one M = 128 tile over every key

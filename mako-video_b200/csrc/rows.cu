@@ -41,118 +41,167 @@ __device__ __forceinline__ float block_max(float v, float* red)
     return t;
 }
 
-constexpr size_t kRmsStreamSmem = 172032; // row slots of the streaming kernel: 4 warps x 2 rows of 5376 floats
 
-// y = RMSNorm(x) * w * (1 + scale[r]) + shift[r] per row, bf16, fp32 or int8 (+ row scale) out. A persistent kernel
-// that streams rows through shared memory: each warp owns two row slots
-// and keeps the next row's bulk copy in flight while it works on the current one (eight rows of HBM reads in flight
-// per SM with four warps), reads the row twice from shared memory (sum of squares, then the output) and the shift,
-// scale and weight vectors through L1 (consecutive rows share them). Rows r = (CTA x warps + warp) + i x grid x warps.
-// Shared memory: [warps][2] mbarriers (256 bytes), then [warps][2][d] fp32 row slots.
-__global__ void __launch_bounds__(256) rms_mod_stream_kernel(const RmsModParams p)
+// y = RMSNorm(x) * w * (1 + scale[r]) + shift[r] per row, bf16, fp32 or int8 (+ row scale) out.
+// A persistent kernel: CTA b owns a contiguous range of rows and walks it in batches of up to RM_BATCH rows,
+// double-buffered in shared memory by bulk copies (the next batch streams in while this one is worked on). The
+// columns are split across the CTA's eight warps: each lane keeps w (1 + scale) and shift of its columns in registers,
+// reloading them only when a row's modulation index changes (the boundaries of the packed row order's segments), so
+// a row is read from HBM once and from shared memory twice (sum of squares, then the output), and the modulation
+// vectors are not re-read per row. A row's sum of squares (and, for int8, its maximum) is combined from the warps'
+// partials through shared memory in a fixed order.
+// Shared memory: two mbarriers, the partials [RM_BATCH][RM_WARPS] (sum) and [RM_BATCH][RM_WARPS] (max), then at byte
+// 1024 the row buffers [2][batch][d] fp32.
+constexpr int RM_WARPS = 8, RM_BATCH = 4, RM_MAXJ = 8; // RM_MAXJ float4 per lane: rows up to 8 x 32 x 8 x 4 = 8192 wide
+constexpr size_t kRmsRowSmem = 172032;                 // row buffers: 2 x 4 rows of 5376 floats
+
+__global__ void __launch_bounds__(RM_WARPS * 32, 1) rms_mod_kernel(const RmsModParams p, int nb, int rows_per_cta)
 {
     extern __shared__ __align__(128) uint8_t rm_smem[];
-    const int nw = blockDim.x >> 5, w = warp_id(), lane = lane_id();
+    uint64_t* full = reinterpret_cast<uint64_t*>(rm_smem);
+    float* part = reinterpret_cast<float*>(rm_smem + 64);
+    float* pmax = part + RM_BATCH * RM_WARPS;
+    float* rows = reinterpret_cast<float*>(rm_smem + 1024);
+    const int w = warp_id(), lane = lane_id();
+    const int n4 = p.d >> 2, nw4 = (n4 + RM_WARPS - 1) / RM_WARPS;
+    const int r0 = blockIdx.x * rows_per_cta, r1 = min(p.rows, r0 + rows_per_cta);
+    if (r0 >= r1)
+        return;
+    const int batches = (r1 - r0 + nb - 1) / nb;
     const uint32_t row_bytes = uint32_t(p.d) * 4;
-    uint64_t* bar = reinterpret_cast<uint64_t*>(rm_smem) + 2 * w;
-    float* buf = reinterpret_cast<float*>(rm_smem + 256) + size_t(2 * w) * p.d;
-    const int stride = gridDim.x * nw;
-    const int first = blockIdx.x * nw + w;
-    if (lane == 0) {
-        mbar_init(&bar[0], 1);
-        mbar_init(&bar[1], 1);
+    auto issue = [&](int b) { // one thread: the bulk copies of batch b into buffer b & 1
+        const int first = r0 + b * nb, n = min(nb, r1 - first);
+        float* dst = rows + size_t(b & 1) * nb * p.d;
+        mbar_arrive_expect_tx(&full[b & 1], uint32_t(n) * row_bytes);
+        for (int i = 0; i < n; ++i)
+            bulk_load(dst + size_t(i) * p.d, p.x + size_t(first + i) * p.ldx, row_bytes, &full[b & 1]);
+    };
+    if (threadIdx.x == 0) {
+        mbar_init(&full[0], 1);
+        mbar_init(&full[1], 1);
         fence_barrier_init();
-        for (int k = 0; k < 2; ++k) {
-            const int r = first + k * stride;
-            if (r < p.rows) {
-                mbar_arrive_expect_tx(&bar[k], row_bytes);
-                bulk_load(buf + size_t(k) * p.d, p.x + size_t(r) * p.ldx, row_bytes, &bar[k]);
-            }
-        }
+        issue(0);
+        if (batches > 1)
+            issue(1);
     }
-    __syncwarp();
-    const int n4 = p.d >> 2;
-    int it = 0;
-    bool ok = true;
-    for (int r = first; r < p.rows; r += stride, ++it) {
-        const int slot = it & 1;
-        float4* x4 = reinterpret_cast<float4*>(buf + size_t(slot) * p.d);
-        if (!(ok = mbar_wait(&bar[slot], (it >> 1) & 1)))
-            break;
-        float ss0 = 0.f, ss1 = 0.f;
-        int c = lane;
-        for (; c + 32 < n4; c += 64) {
-            const float4 a = x4[c], b = x4[c + 32];
-            ss0 += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w;
-            ss1 += b.x * b.x + b.y * b.y + b.z * b.z + b.w * b.w;
-        }
-        if (c < n4) {
-            const float4 a = x4[c];
-            ss0 += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w;
-        }
-        const float rinv = rsqrtf(warp_sum(ss0 + ss1) / float(p.d) + p.eps);
-        const int m = p.mod_idx ? p.mod_idx[r] : 0;
+    __syncthreads();
+    // this lane's columns: float4 index col(j) = w nw4 + lane + 32 j, where lane + 32 j < nw4 and col(j) < n4
+    auto col = [&](int j) { return w * nw4 + lane + 32 * j; };
+    auto valid = [&](int j) { return lane + 32 * j < nw4 && col(j) < n4; };
+    float4 wa[RM_MAXJ], sh[RM_MAXJ];
+    int m_cur = -1;
+    auto load_mod = [&](int m) {
         const float4* sh4 = reinterpret_cast<const float4*>(p.mod + (size_t(m) * p.mod_slots + p.shift_slot) * p.d);
         const float4* sc4 = reinterpret_cast<const float4*>(p.mod + (size_t(m) * p.mod_slots + p.scale_slot) * p.d);
         const float4* w4 = reinterpret_cast<const float4*>(p.w);
-        auto y_of = [&](int c) {
-            const float4 v = x4[c], sh = __ldg(sh4 + c), sc = __ldg(sc4 + c);
-            const float4 wt = p.w ? __ldg(w4 + c) : make_float4(1.f, 1.f, 1.f, 1.f);
-            return make_float4(v.x * rinv * wt.x * (1.f + sc.x) + sh.x, v.y * rinv * wt.y * (1.f + sc.y) + sh.y,
-                               v.z * rinv * wt.z * (1.f + sc.z) + sh.z, v.w * rinv * wt.w * (1.f + sc.w) + sh.w);
-        };
-        if (p.out_kind == RowOut::bf16) {
-            uint2* o = reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(p.out) + size_t(r) * p.ldo);
-#pragma unroll 4
-            for (int c = lane; c < n4; c += 32) {
-                const float4 y = y_of(c);
-                o[c] = make_uint2(pack_bf16x2(y.x, y.y), pack_bf16x2(y.z, y.w));
-            }
-        } else if (p.out_kind == RowOut::f32) {
-            float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + size_t(r) * p.ldo);
-#pragma unroll 4
-            for (int c = lane; c < n4; c += 32)
-                o[c] = y_of(c);
-        } else {
-            // the GEMM input is the bf16 rounding of y (as in the bf16 path), quantised per row: y's bf16 values go
-            // back into the slot, then a third pass quantises them by the row's maximum
-            auto r16 = [](float a) { return __bfloat162float(__float2bfloat16_rn(a)); };
-            float amax = 0.f;
-#pragma unroll 4
-            for (int c = lane; c < n4; c += 32) {
-                float4 y = y_of(c);
-                y = make_float4(r16(y.x), r16(y.y), r16(y.z), r16(y.w));
-                amax = fmaxf(amax, fmaxf(fmaxf(fabsf(y.x), fabsf(y.y)), fmaxf(fabsf(y.z), fabsf(y.w))));
-                x4[c] = y;
-            }
-            amax = warp_max(amax);
-            const float inv = amax > 0.f ? 127.0f / amax : 0.f;
+#pragma unroll
+        for (int j = 0; j < RM_MAXJ; ++j) {
+            if (!valid(j))
+                continue;
+            const float4 sc = __ldg(sc4 + col(j));
+            const float4 wt = p.w ? __ldg(w4 + col(j)) : make_float4(1.f, 1.f, 1.f, 1.f);
+            wa[j] = make_float4(wt.x * (1.f + sc.x), wt.y * (1.f + sc.y), wt.z * (1.f + sc.z), wt.w * (1.f + sc.w));
+            sh[j] = __ldg(sh4 + col(j));
+        }
+        m_cur = m;
+    };
+    auto r16 = [](float a) { return __bfloat162float(__float2bfloat16_rn(a)); };
+    bool ok = true;
+    int b = 0;
+    for (; b < batches; ++b) {
+        const int first = r0 + b * nb, n = min(nb, r1 - first);
+        const float* buf = rows + size_t(b & 1) * nb * p.d;
+        if (!(ok = mbar_wait(&full[b & 1], (b >> 1) & 1)))
+            break;
+        for (int i = 0; i < n; ++i) {
+            const float4* x4 = reinterpret_cast<const float4*>(buf + size_t(i) * p.d);
+            float ss = 0.f;
+#pragma unroll
+            for (int j = 0; j < RM_MAXJ; ++j)
+                if (valid(j)) {
+                    const float4 v = x4[col(j)];
+                    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+                }
+            ss = warp_sum(ss);
             if (lane == 0)
-                p.out_scale[r] = amax / 127.0f;
-            __syncwarp();
-            auto q = [&](float b) { return static_cast<signed char>(fminf(fmaxf(rintf(b * inv), -127.f), 127.f)); };
-            char4* o = reinterpret_cast<char4*>(reinterpret_cast<int8_t*>(p.out) + size_t(r) * p.ldo);
-            for (int c = lane; c < n4; c += 32) {
-                const float4 y = x4[c];
-                o[c] = make_char4(q(y.x), q(y.y), q(y.z), q(y.w));
+                part[i * RM_WARPS + w] = ss;
+        }
+        __syncthreads();
+        float amax_local[RM_BATCH];
+        for (int i = 0; i < n; ++i) {
+            float ss = 0.f;
+#pragma unroll
+            for (int k = 0; k < RM_WARPS; ++k)
+                ss += part[i * RM_WARPS + k];
+            const float rinv = rsqrtf(ss / float(p.d) + p.eps);
+            const int r = first + i;
+            const int m = p.mod_idx ? p.mod_idx[r] : 0;
+            if (m != m_cur)
+                load_mod(m);
+            const float4* x4 = reinterpret_cast<const float4*>(buf + size_t(i) * p.d);
+            float am = 0.f;
+#pragma unroll
+            for (int j = 0; j < RM_MAXJ; ++j) {
+                if (!valid(j))
+                    continue;
+                const float4 v = x4[col(j)];
+                const float4 y = make_float4(v.x * rinv * wa[j].x + sh[j].x, v.y * rinv * wa[j].y + sh[j].y,
+                                             v.z * rinv * wa[j].z + sh[j].z, v.w * rinv * wa[j].w + sh[j].w);
+                if (p.out_kind == RowOut::bf16) {
+                    reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(p.out) + size_t(r) * p.ldo)[col(j)] =
+                        make_uint2(pack_bf16x2(y.x, y.y), pack_bf16x2(y.z, y.w));
+                } else if (p.out_kind == RowOut::f32) {
+                    reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + size_t(r) * p.ldo)[col(j)] = y;
+                } else {
+                    am = fmaxf(am, fmaxf(fmaxf(fabsf(r16(y.x)), fabsf(r16(y.y))), fmaxf(fabsf(r16(y.z)), fabsf(r16(y.w)))));
+                }
+            }
+            amax_local[i] = am;
+        }
+        if (p.out_kind == RowOut::s8) {
+            // the GEMM input is the bf16 rounding of y (as in the bf16 path), quantised per row by its maximum
+            for (int i = 0; i < n; ++i) {
+                const float am = warp_max(amax_local[i]);
+                if (lane == 0)
+                    pmax[i * RM_WARPS + w] = am;
+            }
+            __syncthreads();
+            for (int i = 0; i < n; ++i) {
+                float amax = 0.f, ss = 0.f;
+#pragma unroll
+                for (int k = 0; k < RM_WARPS; ++k)
+                    amax = fmaxf(amax, pmax[i * RM_WARPS + k]), ss += part[i * RM_WARPS + k];
+                const float rinv = rsqrtf(ss / float(p.d) + p.eps);
+                const int r = first + i;
+                const int m = p.mod_idx ? p.mod_idx[r] : 0;
+                if (m != m_cur)
+                    load_mod(m);
+                const float inv = amax > 0.f ? 127.0f / amax : 0.f;
+                if (threadIdx.x == 0)
+                    p.out_scale[r] = amax / 127.0f;
+                auto q = [&](float y) { return static_cast<signed char>(fminf(fmaxf(rintf(r16(y) * inv), -127.f), 127.f)); };
+                const float4* x4 = reinterpret_cast<const float4*>(buf + size_t(i) * p.d);
+                char4* o = reinterpret_cast<char4*>(reinterpret_cast<int8_t*>(p.out) + size_t(r) * p.ldo);
+#pragma unroll
+                for (int j = 0; j < RM_MAXJ; ++j) {
+                    if (!valid(j))
+                        continue;
+                    const float4 v = x4[col(j)];
+                    o[col(j)] = make_char4(q(v.x * rinv * wa[j].x + sh[j].x), q(v.y * rinv * wa[j].y + sh[j].y),
+                                           q(v.z * rinv * wa[j].z + sh[j].z), q(v.w * rinv * wa[j].w + sh[j].w));
+                }
             }
         }
-        // the slot's reads (and the int8 pass's writes) come before the next bulk copy into it
+        // every read of the buffer is done: refill it with batch b + 2
         fence_proxy_async_smem();
-        __syncwarp();
-        const int next = r + 2 * stride;
-        if (lane == 0 && next < p.rows) {
-            mbar_arrive_expect_tx(&bar[slot], row_bytes);
-            bulk_load(buf + size_t(slot) * p.d, p.x + size_t(next) * p.ldx, row_bytes, &bar[slot]);
-        }
+        __syncthreads();
+        if (threadIdx.x == 0 && b + 2 < batches)
+            issue(b + 2);
     }
-    if (!ok && lane == 0) {
-        // a wait ran out: let this warp's copies still in flight land before the CTA's shared memory is released
-        for (int k = 1; k < 3; ++k) {
-            const int r = first + (it + k - 1) * stride;
-            if (r < p.rows)
-                mbar_wait(&bar[(it + k - 1) & 1], ((it + k - 1) >> 1) & 1, 100000000ll);
-        }
+    if (!ok && threadIdx.x == 0) {
+        // a wait ran out: let the copies still in flight land before the CTA's shared memory is released
+        for (int k = b; k < min(b + 2, batches); ++k)
+            mbar_wait(&full[k & 1], (k >> 1) & 1, 100000000ll);
     }
 }
 
@@ -418,9 +467,9 @@ int grid_for(size_t work, int threads)
 
 void rms_mod_rows(const RmsModParams& p, cudaStream_t s)
 {
-    const size_t slot_bytes = size_t(p.d) * 4;
-    const int nw = int(std::min<size_t>(4, kRmsStreamSmem / (2 * std::max<size_t>(slot_bytes, 16))));
-    if (p.d <= 0 || p.d % 4 || nw < 1 || !p.x || !p.mod || !p.out || (p.out_kind == RowOut::s8 && !p.out_scale))
+    const size_t row_bytes = size_t(p.d) * 4;
+    if (p.d <= 0 || p.d % 4 || p.d > RM_WARPS * 32 * RM_MAXJ * 4 || !p.x || !p.mod || !p.out ||
+        (p.out_kind == RowOut::s8 && !p.out_scale))
         throw CudaError("rms_mod_rows: bad arguments");
     // 16-byte aligned rows for the bulk copies and the vector loads and stores
     if (reinterpret_cast<uintptr_t>(p.x) % 16 || p.ldx % 4 || reinterpret_cast<uintptr_t>(p.out) % 16 || p.ldo % 4 ||
@@ -428,11 +477,13 @@ void rms_mod_rows(const RmsModParams& p, cudaStream_t s)
         throw CudaError("rms_mod_rows: rows and vectors must start on 16-byte boundaries");
     if (p.rows == 0)
         return;
-    const int smem = 256 + int(nw * 2 * slot_bytes);
+    const int nb = int(std::min<size_t>(RM_BATCH, kRmsRowSmem / (2 * row_bytes)));
+    const int per = std::max(1, (p.rows + num_sms() - 1) / num_sms());
+    const int grid = (p.rows + per - 1) / per;
+    const int smem = 1024 + int(2 * nb * row_bytes);
     static std::atomic<uint64_t> opt_in;
-    smem_opt_in(rms_mod_stream_kernel, 256 + int(kRmsStreamSmem), opt_in);
-    const int grid = int(std::min<int64_t>(num_sms(), (int64_t(p.rows) + nw - 1) / nw));
-    rms_mod_stream_kernel<<<grid, nw * 32, smem, s>>>(p);
+    smem_opt_in(rms_mod_kernel, 1024 + int(kRmsRowSmem), opt_in);
+    rms_mod_kernel<<<grid, RM_WARPS * 32, smem, s>>>(p, nb, per);
     H3_CUDA(cudaGetLastError());
 }
 
