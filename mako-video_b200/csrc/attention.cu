@@ -436,9 +436,7 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
 
     const int warp = warp_id();
     // Launches are 1-D and longest first: the dense-row query tiles (which see every key, several times a video
-    // tile's work) of every head, then each head's video tiles together (they share the head's keys in L2). Grouping
-    // each head's dense-row tiles with its video tiles instead halves the HBM reads (1.03 against 2.42 GB a 768p
-    // launch) but was measured 9% slower: the long tiles then finish last.
+    // tile's work) of every head, then each head's video tiles together (they share the head's keys in L2).
     int tile, head;
     {
         const int vt = (p.grid.cubes() + 1) / 2, dt = p.q_tiles - vt;
@@ -456,8 +454,6 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
     const int4* entries = p.blocks + (size_t(head) * p.q_tiles + tile) * p.max_blocks;
     // step j's keys for query unit x
     auto entry = [&](int j, int x) -> int4 { return every ? every_row_block(j, p.rows) : entries[2 * j + x]; };
-    // a step whose keys both query units see (or a dense-row tile's step): one ring item for the two, else one each
-    auto one_item = [&](int j) -> bool { return every || entries[2 * j].w != 0; };
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
@@ -494,21 +490,15 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
         mbar_arrive_expect_tx(q_full, TILE);
         load_rows(smem + A3_OFF_Q, 0, qr.x, head, &maps.q, q_full);
         load_rows(smem + A3_OFF_Q, 1, qr.y < 0 ? qr.x : qr.y, head, &maps.q, q_full);
-        // Ring items in step order: one per query unit of a step, or one for a step both units share (a dense-row
-        // tile's steps, or entries flagged shared); K runs ahead of V by up to the depth of its ring. A padding entry
-        // (no key unit) loads row 0: the keys are masked.
-        int jk = 0, xk = 0, jv = 0, xv = 0; // the next K and V items: step and query unit
-        int ik = 0, iv = 0;                 // items issued
-        auto advance = [&](int& j, int& x) {
-            if (x == 0 && !one_item(j))
-                x = 1;
-            else
-                x = 0, ++j;
-        };
+        // Ring items i = 2 j + x (step j, query unit x), or i = j for a dense-row tile: K runs ahead of V by up to the
+        // depth of its ring. A padding entry (no key unit) loads row 0: the keys are masked.
+        const int items = every ? nkv : 2 * nkv;
+        int ik = 0, iv = 0;
         bool ok = true;
-        while (ok && jv < nkv) {
-            const bool k_turn = jk < nkv && ik < iv + A3_KST;
-            const int4 e = k_turn ? entry(jk, xk) : entry(jv, xv);
+        while (ok && iv < items) {
+            const bool k_turn = ik < items && ik < iv + A3_KST;
+            const int i = k_turn ? ik : iv;
+            const int4 e = every ? every_row_block(i, p.rows) : entry(i >> 1, i & 1);
             const int r0 = e.x < 0 ? 0 : e.x, r1 = e.y < 0 ? r0 : e.y;
             if (k_turn) {
                 const int s = ik % A3_KST;
@@ -518,7 +508,6 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
                 load_rows(smem + A3_OFF_K + s * TILE, 0, r0, head, &maps.k, &k_full[s]);
                 load_rows(smem + A3_OFF_K + s * TILE, 1, r1, head, &maps.k, &k_full[s]);
                 ++ik;
-                advance(jk, xk);
             } else {
                 const int s = iv % A3_VST;
                 if (!(ok = mbar_wait(&v_empty[s], ((iv / A3_VST) & 1) ^ 1)))
@@ -527,7 +516,6 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
                 load_rows(smem + A3_OFF_V + s * TILE, 0, r0, head, &maps.v, &v_full[s]);
                 load_rows(smem + A3_OFF_V + s * TILE, 1, r1, head, &maps.v, &v_full[s]);
                 ++iv;
-                advance(jv, xv);
             }
         }
     } else if (nkv > 0 && warp == 1 && elect_one_lane()) {
@@ -535,17 +523,13 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
         const uint32_t id_s = idesc_bf16(64, 128), id_s128 = idesc_bf16(128, 128);
         const uint32_t id_pv = idesc_bf16(64, 128, false, true), id_pv128 = idesc_bf16(128, 128, false, true);
         const uint32_t sq = smem_u32(smem + A3_OFF_Q);
-        // Ring items are consumed in the producer's order: K items by the S MMAs (steps ascending), V items by the PV
-        // MMAs (steps ascending); a step both units share takes one item of each for the two units.
-        int ik = 0, iv = 0;
         // S(j) for both query units (unit x: query rows at 8192 x within each dim half, lanes at 16 x), or for the
         // whole 128-row tile of a dense-row tile
         auto issue_s = [&](int j) -> bool {
             if (every) {
-                const int s = ik % A3_KST;
-                if (!mbar_wait(&k_full[s], (ik / A3_KST) & 1))
+                const int s = j % A3_KST;
+                if (!mbar_wait(&k_full[s], (j / A3_KST) & 1))
                     return false;
-                ++ik;
                 tc_fence_after();
                 const uint32_t sk = smem_u32(smem + A3_OFF_K + s * TILE);
 #pragma unroll
@@ -557,16 +541,11 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
                 mma_commit(&s_full[j & 1]);
                 return true;
             }
-            const bool one = one_item(j);
-            int s = 0;
             for (int x = 0; x < 2; ++x) {
-                if (x == 0 || !one) {
-                    s = ik % A3_KST;
-                    if (!mbar_wait(&k_full[s], (ik / A3_KST) & 1))
-                        return false;
-                    ++ik;
-                    tc_fence_after();
-                }
+                const int i = 2 * j + x, s = i % A3_KST;
+                if (!mbar_wait(&k_full[s], (i / A3_KST) & 1))
+                    return false;
+                tc_fence_after();
                 const uint32_t sk = smem_u32(smem + A3_OFF_K + s * TILE);
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
@@ -574,8 +553,7 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
                     mma_bf16_ss(tmem + (j & 1) * 128 + (x ? LANE16 : 0u), sdesc_sw128(sq + x * 8192 + off, 16, 1024),
                                 sdesc_sw128(sk + off, 16, 1024), id_s, kk > 0);
                 }
-                if (x == 1 || !one)
-                    mma_commit(&k_empty[s]);
+                mma_commit(&k_empty[s]);
             }
             mma_commit(&s_full[j & 1]);
             return true;
@@ -587,36 +565,28 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
             if (!(ok = mbar_wait(&p_full[j & 1], (j >> 1) & 1)))
                 break;
             if (every) {
-                const int sv = iv % A3_VST;
-                if (!(ok = mbar_wait(&v_full[sv], (iv / A3_VST) & 1)))
+                const int sv = j % A3_VST;
+                if (!(ok = mbar_wait(&v_full[sv], (j / A3_VST) & 1)))
                     break;
-                ++iv;
                 tc_fence_after();
                 const uint32_t vb = smem_u32(smem + A3_OFF_V + sv * TILE);
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk)
                     mma_bf16_ts(tmem + T_O, tmem + (j & 1) * 128 + kk * 8, sdesc_sw128(vb + kk * 2048, HALF, 1024), id_pv128, (j | kk) != 0);
                 mma_commit(&v_empty[sv]);
-            } else {
-                const bool one = one_item(j);
-                int sv = 0;
-                for (int x = 0; x < 2 && ok; ++x) {
-                    if (x == 0 || !one) {
-                        sv = iv % A3_VST;
-                        if (!(ok = mbar_wait(&v_full[sv], (iv / A3_VST) & 1)))
-                            break;
-                        ++iv;
-                        tc_fence_after();
-                    }
-                    const uint32_t vb = smem_u32(smem + A3_OFF_V + sv * TILE);
-                    const uint32_t lane = x ? LANE16 : 0u;
+            }
+            for (int x = 0; x < 2 && ok && !every; ++x) {
+                const int i = 2 * j + x, sv = i % A3_VST;
+                if (!(ok = mbar_wait(&v_full[sv], (i / A3_VST) & 1)))
+                    break;
+                tc_fence_after();
+                const uint32_t vb = smem_u32(smem + A3_OFF_V + sv * TILE);
+                const uint32_t lane = x ? LANE16 : 0u;
 #pragma unroll
-                    for (int kk = 0; kk < 8; ++kk)
-                        mma_bf16_ts(tmem + T_O + lane, tmem + (j & 1) * 128 + lane + kk * 8, sdesc_sw128(vb + kk * 2048, HALF, 1024), id_pv,
-                                    (j | kk) != 0);
-                    if (x == 1 || !one)
-                        mma_commit(&v_empty[sv]);
-                }
+                for (int kk = 0; kk < 8; ++kk)
+                    mma_bf16_ts(tmem + T_O + lane, tmem + (j & 1) * 128 + lane + kk * 8, sdesc_sw128(vb + kk * 2048, HALF, 1024), id_pv,
+                                (j | kk) != 0);
+                mma_commit(&v_empty[sv]);
             }
             if (!ok)
                 break;

@@ -43,22 +43,23 @@ __device__ __forceinline__ float block_max(float v, float* red)
 
 
 // y = RMSNorm(x) * w * (1 + scale[r]) + shift[r] per row, bf16, fp32 or int8 (+ row scale) out.
-// A persistent kernel: CTA b owns a contiguous range of rows and walks it in batches of up to RM_BATCH rows,
-// double-buffered in shared memory by bulk copies (the next batch streams in while this one is worked on). The
+// A persistent kernel: CTA b owns a contiguous range of rows and walks it in batches of nb rows through a ring of
+// nbufs shared-memory buffers filled by bulk copies (as many as fit in ~200 KB: the following batches stream in while
+// one is worked on; the bytes in flight per SM set the bandwidth). The
 // columns are split across the CTA's eight warps: each lane keeps w (1 + scale) and shift of its columns in registers,
 // reloading them only when a row's modulation index changes (the boundaries of the packed row order's segments), so
 // a row is read from HBM once and from shared memory twice (sum of squares, then the output), and the modulation
 // vectors are not re-read per row. A row's sum of squares (and, for int8, its maximum) is combined from the warps'
 // partials through shared memory in a fixed order.
-// Shared memory: two mbarriers, the partials [RM_BATCH][RM_WARPS] (sum) and [RM_BATCH][RM_WARPS] (max), then at byte
-// 1024 the row buffers [2][batch][d] fp32.
-constexpr int RM_WARPS = 8, RM_BATCH = 4, RM_MAXJ = 8; // RM_MAXJ float4 per lane: rows up to 8 x 32 x 8 x 4 = 8192 wide
-constexpr size_t kRmsRowSmem = 172032;                 // row buffers: 2 x 4 rows of 5376 floats
+// Shared memory: nbufs mbarriers, the partials [RM_BATCH][RM_WARPS] (sum) and [RM_BATCH][RM_WARPS] (max), then at
+// byte 1024 the row buffers [nbufs][nb][d] fp32.
+constexpr int RM_WARPS = 8, RM_BATCH = 4, RM_MAXBUFS = 6, RM_MAXJ = 8; // RM_MAXJ float4 per lane: rows up to 8192 wide
+constexpr size_t kRmsRowSmem = 204800;                                 // row buffers: 2 x 4 rows of 5120 floats
 
-__global__ void __launch_bounds__(RM_WARPS * 32, 1) rms_mod_kernel(const RmsModParams p, int nb, int rows_per_cta)
+__global__ void __launch_bounds__(RM_WARPS * 32, 1) rms_mod_kernel(const RmsModParams p, int nb, int nbufs, int rows_per_cta)
 {
     extern __shared__ __align__(128) uint8_t rm_smem[];
-    uint64_t* full = reinterpret_cast<uint64_t*>(rm_smem);
+    uint64_t* full = reinterpret_cast<uint64_t*>(rm_smem); // [nbufs]
     float* part = reinterpret_cast<float*>(rm_smem + 64);
     float* pmax = part + RM_BATCH * RM_WARPS;
     float* rows = reinterpret_cast<float*>(rm_smem + 1024);
@@ -69,20 +70,19 @@ __global__ void __launch_bounds__(RM_WARPS * 32, 1) rms_mod_kernel(const RmsModP
         return;
     const int batches = (r1 - r0 + nb - 1) / nb;
     const uint32_t row_bytes = uint32_t(p.d) * 4;
-    auto issue = [&](int b) { // one thread: the bulk copies of batch b into buffer b & 1
+    auto issue = [&](int b) { // one thread: the bulk copies of batch b into buffer b % nbufs
         const int first = r0 + b * nb, n = min(nb, r1 - first);
-        float* dst = rows + size_t(b & 1) * nb * p.d;
-        mbar_arrive_expect_tx(&full[b & 1], uint32_t(n) * row_bytes);
+        float* dst = rows + size_t(b % nbufs) * nb * p.d;
+        mbar_arrive_expect_tx(&full[b % nbufs], uint32_t(n) * row_bytes);
         for (int i = 0; i < n; ++i)
-            bulk_load(dst + size_t(i) * p.d, p.x + size_t(first + i) * p.ldx, row_bytes, &full[b & 1]);
+            bulk_load(dst + size_t(i) * p.d, p.x + size_t(first + i) * p.ldx, row_bytes, &full[b % nbufs]);
     };
     if (threadIdx.x == 0) {
-        mbar_init(&full[0], 1);
-        mbar_init(&full[1], 1);
+        for (int k = 0; k < nbufs; ++k)
+            mbar_init(&full[k], 1);
         fence_barrier_init();
-        issue(0);
-        if (batches > 1)
-            issue(1);
+        for (int k = 0; k < nbufs && k < batches; ++k)
+            issue(k);
     }
     __syncthreads();
     // this lane's columns: float4 index col(j) = w nw4 + lane + 32 j, where lane + 32 j < nw4 and col(j) < n4
@@ -110,8 +110,8 @@ __global__ void __launch_bounds__(RM_WARPS * 32, 1) rms_mod_kernel(const RmsModP
     int b = 0;
     for (; b < batches; ++b) {
         const int first = r0 + b * nb, n = min(nb, r1 - first);
-        const float* buf = rows + size_t(b & 1) * nb * p.d;
-        if (!(ok = mbar_wait(&full[b & 1], (b >> 1) & 1)))
+        const float* buf = rows + size_t(b % nbufs) * nb * p.d;
+        if (!(ok = mbar_wait(&full[b % nbufs], (b / nbufs) & 1)))
             break;
         for (int i = 0; i < n; ++i) {
             const float4* x4 = reinterpret_cast<const float4*>(buf + size_t(i) * p.d);
@@ -192,16 +192,16 @@ __global__ void __launch_bounds__(RM_WARPS * 32, 1) rms_mod_kernel(const RmsModP
                 }
             }
         }
-        // every read of the buffer is done: refill it with batch b + 2
+        // every read of the buffer is done: refill it with batch b + nbufs
         fence_proxy_async_smem();
         __syncthreads();
-        if (threadIdx.x == 0 && b + 2 < batches)
-            issue(b + 2);
+        if (threadIdx.x == 0 && b + nbufs < batches)
+            issue(b + nbufs);
     }
     if (!ok && threadIdx.x == 0) {
         // a wait ran out: let the copies still in flight land before the CTA's shared memory is released
-        for (int k = b; k < min(b + 2, batches); ++k)
-            mbar_wait(&full[k & 1], (k >> 1) & 1, 100000000ll);
+        for (int k = b; k < min(b + nbufs, batches); ++k)
+            mbar_wait(&full[k % nbufs], (k / nbufs) & 1, 100000000ll);
     }
 }
 
@@ -477,13 +477,15 @@ void rms_mod_rows(const RmsModParams& p, cudaStream_t s)
         throw CudaError("rms_mod_rows: rows and vectors must start on 16-byte boundaries");
     if (p.rows == 0)
         return;
-    const int nb = int(std::min<size_t>(RM_BATCH, kRmsRowSmem / (2 * row_bytes)));
+    // batches of up to RM_BATCH rows, as many buffers as fit (at least two)
+    const int nb = int(std::max<size_t>(1, std::min<size_t>(RM_BATCH, kRmsRowSmem / (2 * row_bytes))));
+    const int nbufs = int(std::min<size_t>(RM_MAXBUFS, kRmsRowSmem / (nb * row_bytes)));
     const int per = std::max(1, (p.rows + num_sms() - 1) / num_sms());
     const int grid = (p.rows + per - 1) / per;
-    const int smem = 1024 + int(2 * nb * row_bytes);
+    const int smem = 1024 + int(nbufs * nb * row_bytes);
     static std::atomic<uint64_t> opt_in;
     smem_opt_in(rms_mod_kernel, 1024 + int(kRmsRowSmem), opt_in);
-    rms_mod_kernel<<<grid, RM_WARPS * 32, smem, s>>>(p, nb, per);
+    rms_mod_kernel<<<grid, RM_WARPS * 32, smem, s>>>(p, nb, nbufs, per);
     H3_CUDA(cudaGetLastError());
 }
 

@@ -253,83 +253,34 @@ __global__ void build_passes_kernel(const int32_t* sel, const int32_t* nsel, int
         nblocks[idx] = -1; // dense query rows attend every row
         return;
     }
-    // Each cube of the tile gets its own list of key units, two a step. The units both cubes see (every dense unit,
-    // and the cubes both selected) come first, in the same order in both lists, so that the leading steps are the same
-    // for both cubes: those steps load their keys once for the two (entry .w = 1 on both). Then each cube's own
-    // selected cubes, ascending; the shorter list is padded with empty entries.
+    // Each cube of the tile gets its own list: its selected cubes (ascending) then every dense unit, two units a
+    // step; the shorter list is padded with empty entries.
     const int max_steps = max_blocks / 2;
     int4* out = blocks + size_t(idx) * max_blocks;
-    const int ca = 2 * t, cb = 2 * t + 1;
-    const bool has_b = cb < nc;
-    const int32_t* L[2] = {sel + (size_t(h) * nc + ca) * kcap, has_b ? sel + (size_t(h) * nc + cb) * kcap : nullptr};
-    const int n[2] = {nsel[size_t(h) * nc + ca], has_b ? nsel[size_t(h) * nc + cb] : 0};
-    // cubes in both selections (both lists ascending)
-    int common = 0;
-    if (has_b)
-        for (int i = 0, j = 0; i < n[0] && j < n[1];) {
-            const int u = L[0][i], v = L[1][j];
-            common += u == v;
-            i += u <= v;
-            j += v <= u;
-        }
-    // shared units rounded down to whole steps (an odd one is left to each cube's own part)
-    const int shared = has_b ? ((nd + common) & ~1) : 0;
-    const int dense_shared = min(nd, shared), common_used = max(shared - nd, 0);
-    int pos[2] = {0, 0};
-    int2 pend[2] = {make_int2(-1, 0), make_int2(-1, 0)};
-    auto put = [&](int x, int st, int2 a, int2 b) {
-        if (st < max_steps)
-            out[2 * st + x] = make_int4(a.x, b.x, a.y | (b.y << 8), 2 * st + 1 < shared ? 1 : 0);
-    };
-    auto emit = [&](int x, int u) {
-        const int2 sp = span_of(u, g);
-        const int p = pos[x]++;
-        if (p & 1)
-            put(x, p >> 1, pend[x], sp);
-        else
-            pend[x] = sp;
-    };
-    const int xs = has_b ? 2 : 1;
-    // the shared part: dense units, then the first common_used common cubes, identical in both lists
-    for (int i = 0; i < dense_shared; ++i)
-        for (int x = 0; x < xs; ++x)
-            emit(x, nc + i);
-    for (int i = 0, j = 0, used = 0; used < common_used && i < n[0] && j < n[1];) {
-        const int u = L[0][i], v = L[1][j];
-        if (u == v) {
-            emit(0, u);
-            emit(1, u);
-            ++used;
-        }
-        i += u <= v;
-        j += v <= u;
-    }
-    // each cube's own part: the dense units left over, then its selected cubes outside the shared common ones
-    for (int x = 0; x < xs; ++x) {
-        for (int i = dense_shared; i < nd; ++i)
-            emit(x, nc + i);
-        const int32_t* own = L[x];
-        const int32_t* other = L[x ^ 1];
-        const int no = has_b ? n[x ^ 1] : 0;
-        for (int i = 0, j = 0, used = 0; i < n[x]; ++i) {
-            const int u = own[i];
-            while (j < no && other[j] < u)
-                ++j;
-            if (j < no && other[j] == u && used < common_used) {
-                ++used;
-                continue;
+    int steps = 0;
+    for (int x = 0; x < 2; ++x) {
+        const int c = 2 * t + x;
+        const int32_t* L = c < nc ? sel + (size_t(h) * nc + c) * kcap : nullptr;
+        const int n = c < nc ? nsel[size_t(h) * nc + c] : -nd; // a missing cube gets no units at all
+        const int len = n + nd;
+        const int st = (len + 1) / 2;
+        steps = max(steps, st);
+        for (int s2 = 0; s2 < min(st, max_steps); ++s2) {
+            int2 sp[2];
+            for (int k = 0; k < 2; ++k) {
+                const int i = 2 * s2 + k;
+                sp[k] = i < len ? span_of(i < n ? L[i] : nc + (i - n), g) : make_int2(-1, 0);
             }
-            emit(x, u);
-        }
-        if (pos[x] & 1) {
-            put(x, pos[x] >> 1, pend[x], make_int2(-1, 0));
-            ++pos[x];
+            out[2 * s2 + x] = make_int4(sp[0].x, sp[1].x, sp[0].y | (sp[1].y << 8), 0);
         }
     }
-    const int steps = min(max(pos[0], pos[1]) / 2, max_steps);
-    for (int x = 0; x < 2; ++x)
-        for (int st = pos[x] / 2; st < steps; ++st)
-            out[2 * st + x] = make_int4(-1, -1, 0, 0);
+    steps = min(steps, max_steps);
+    for (int x = 0; x < 2; ++x) {
+        const int c = 2 * t + x;
+        const int len = (c < nc ? nsel[size_t(h) * nc + c] : -nd) + nd;
+        for (int s2 = (len + 1) / 2; s2 < steps; ++s2)
+            out[2 * s2 + x] = make_int4(-1, -1, 0, 0);
+    }
     nblocks[idx] = steps;
 }
 
