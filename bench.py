@@ -38,6 +38,8 @@ WORKLOADS = {
     "long": ("c2", "c5", 0.0, 1, 0, "C5: 15 s clip, 92736 video + 1008 keyframe + 512 text + 640 audio rows, dense"),
     "long-sparse": ("c2", "c5", 0.1, 3, 0, "C5 sparse, ratio 0.1, local 3"),
     "c1": ("c1", "c1", 0.0, 1, 0, "C1: one d=1024 block, 576 rows"),
+    "h3": ("h3", "h3", 0.0, 1, 0, "MiniMax-H3 itself: d 5376, 56 heads, SwiGLU 14336, 50 blocks, 1344x768x124 frames = 37296 video "
+                                  "+ 512 text + 414 audio rows, dense"),
 }
 
 
@@ -389,14 +391,14 @@ def run_ours(args, rank, world, local_rank):
         cfg["blocks"] = args.blocks  # a shorter stack of the same blocks (profiling cases)
     layout = H.Layout.named(lay_name)
 
-    def new_model(int8_mask, sparse_ratio, sparse_local):
+    def new_model(int8_mask, sparse_ratio, sparse_local, config=None):
         nccl_id = None
         if world > 1:
             obj = [H.nccl_unique_id() if rank == 0 else None]
             dist.broadcast_object_list(obj, src=0)
             nccl_id = obj[0]
-        return H.Model(cfg, seed=0, int8_mask=int8_mask, sparse_ratio=sparse_ratio, sparse_local=sparse_local, rank=rank, world=world,
-                       nccl_id=nccl_id, device=local_rank)
+        return H.Model(config or cfg, seed=0, int8_mask=int8_mask, sparse_ratio=sparse_ratio, sparse_local=sparse_local, rank=rank,
+                       world=world, nccl_id=nccl_id, device=local_rank)
 
     model = new_model(int8, ratio, local)
     run = Runner(H, torch, dist, model, layout, cfg, rank, world, local_rank)
@@ -428,22 +430,23 @@ def run_ours(args, rank, world, local_rank):
     ks, kw = min(args.steps, 5), 3
     # int8 last: it needs its own model (int8 weights); the others run on the dense model's weights
     extras = [] if args.extras == "none" or args.workload != "dense" else (
-        ["sparse"] + (["long", "long-sparse"] if world > 1 else []) + ["int8"])
+        ["sparse"] + (["long", "long-sparse"] if world > 1 else []) + ["int8", "h3"])
     run_layout = lay_name
     for name in extras:
-        _, lname, r2, l2, i2, d2 = WORKLOADS[name]
+        c2name, lname, r2, l2, i2, d2 = WORKLOADS[name]
         lay2 = H.Layout.named(lname)
-        if i2:
+        cfg2 = dict(H.CONFIGS[c2name])
+        if i2 or cfg2 != cfg:
             model.close()
-            model = new_model(i2, r2, l2)
-            run = Runner(H, torch, dist, model, lay2, cfg, rank, world, local_rank)
+            model = new_model(i2, r2, l2, cfg2)
+            run = Runner(H, torch, dist, model, lay2, cfg2, rank, world, local_rank)
         else:
             model.set_sparse(r2, l2)
             if lname != run_layout:
                 run = Runner(H, torch, dist, model, lay2, cfg, rank, world, local_rank)
         run_layout = lname
         m2 = run.measure(ks, kw, ks)
-        part = _line_part(m2, cfg, lay2, r2, world, peaks, name, i2)
+        part = _line_part(m2, cfg2, lay2, r2, world, peaks, name, i2)
         part.update({"workload": d2, "rows": lay2.rows, "steps": ks, "warmup": kw, "gpu_launches": m2["launches"] * ks})
         line[name.replace("-", "_")] = part
     if "sparse" in line:
@@ -488,6 +491,10 @@ def main():
     if world > 1:
         import datetime
 
+        # NCCL's communicator set-up lines (ranks, transports) on stderr: the library's own communicator carries the
+        # barriers and all-gathers; the all-to-all data moves as NVLink peer stores from the kernels' epilogues
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         import torch
         import torch.distributed as dist
 

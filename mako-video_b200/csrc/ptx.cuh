@@ -112,7 +112,7 @@ __device__ __forceinline__ void tma_load_5d(void* smem_dst, const void* tmap, ui
 }
 
 // Untiled bulk copy of `bytes` from global to this CTA's shared memory, completing on `bar` (both addresses 16-byte
-// aligned, bytes a multiple of 16; no multicast).
+// aligned, bytes a multiple of 16; into this CTA only).
 __device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar)
 {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(smem_dst)),

@@ -35,6 +35,9 @@ LAYOUTS = {
     "c2": dict(text=512, frames=32, h=48, w=84, audio=128, cond_frames=0),
     # long clip: 92 frames + one keyframe (1008 rows at t = 0.999) + 512 text + 640 audio rows
     "c5": dict(text=512, frames=92, h=48, w=84, audio=320, cond_frames=1),
+    # MiniMax-H3's own 1344 x 768 x 124 frames: 37 latent frames of 24 x 42 patches, 512 text rows, 2 x 207 audio rows
+    # (docs/architecture.md:28-33; tests/geometry_test.cpp:24-26 of the reference)
+    "h3": dict(text=512, frames=37, h=48, w=84, audio=207, cond_frames=0),
 }
 
 

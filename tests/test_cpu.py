@@ -157,7 +157,7 @@ def test_library_exports_every_declared_symbol():
     assert declared <= set(h3b200.SIGNATURES), sorted(declared - set(h3b200.SIGNATURES))
 
 
-@pytest.mark.parametrize("name", ["c1", "c2", "c5"])
+@pytest.mark.parametrize("name", ["c1", "c2", "c5", "h3"])
 def test_layout_rows_match_oracle(name):
     lay = h3b200.Layout.named(name)
     pos, tags, roles = h3b200.rows(lay)
