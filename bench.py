@@ -379,6 +379,62 @@ def _line_part(m, cfg, layout, ratio, world, peaks, args_workload_key, int8):
     }
 
 
+def vae_flops(cfg, h, w):
+    """One clip of the video decoder: its blocks' GEMMs (2 M N K) and attention (4 T^2 d per tile), M = tiles x T rows,
+    plus the token embedding and the pixel projection."""
+    import h3b200 as H
+    ty, tx = len(H.vae_tile_starts(h)), len(H.vae_tile_starts(w))
+    th, tw = min(16, h), min(16, w)
+    T = cfg["clip"] * th * tw + cfg["registers"] + 1
+    M, d, F = ty * tx * T, cfg["dim"], cfg["ffn"]
+    gemm = cfg["blocks"] * 2 * M * d * (3 * d + d + 2 * F + F) + 2 * M * d * (64 + 3 * 4 * 16 * 16)
+    attn = cfg["blocks"] * ty * tx * 4 * T * T * d
+    return gemm, attn, ty * tx, T
+
+
+def measure_vae(torch, H, peaks, clips=3, warmup=2):
+    """The video VAE decoder at MiniMax-H3's size on 768p latents: device seconds per clip (latents and canvas in
+    HBM), and a whole 1344 x 768 x 124-frame video (37 latent frames, 7 clips) through h3vae_decode from host latents
+    to host frames (the reference's 69 s on an M5 Max, docs/performance.md:19)."""
+    cfg = H.VAE_CONFIGS["h3"]
+    h, w = 48, 84
+    m = H.VideoDecoder(cfg, seed=0)
+    rng = np.random.default_rng(0)
+    lat = torch.from_numpy(rng.standard_normal((cfg["clip"], h, w, cfg["channels"]), dtype=np.float32)).cuda()
+    canvas = torch.empty((cfg["clip"] * 4, h * 16, w * 16, 3), dtype=torch.float32, device="cuda")
+    ext = torch.cuda.ExternalStream(m.stream, device=canvas.device)
+    for _ in range(warmup):
+        m.decode_clip_device(lat.data_ptr(), h, w, canvas.data_ptr())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(ext):
+        e0.record()
+        for _ in range(clips):
+            m.decode_clip_device(lat.data_ptr(), h, w, canvas.data_ptr())
+        e1.record()
+    torch.cuda.synchronize()
+    clip_s = e0.elapsed_time(e1) / clips * 1e-3
+    launches = m.last_launches()
+    video = rng.standard_normal((37, h, w, cfg["channels"]), dtype=np.float32)
+    count = [0]
+    t0 = time.perf_counter()
+    m.decode(video, sink=lambda i, a: count.__setitem__(0, count[0] + 1))
+    e2e = time.perf_counter() - t0
+    m.close()
+    gemm, attn, tiles, T = vae_flops(cfg, h, w)
+    peak = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
+    tflops = (gemm + attn) / clip_s / 1e12
+    return {"metric": "s per 768p clip of the video VAE decoder (7 latent frames -> 28 frames)", "value": clip_s, "unit": "s",
+            "config": {"model": "MiniMax-H3 video VAE decoder: d 2048, 32 heads of 64, SwiGLU 8192, 36 blocks (random-init bf16)",
+                       "latents": [cfg["clip"], h, w, cfg["channels"]], "tiles": tiles, "tokens_per_tile": T},
+            "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak, "unit": "TFLOP/s", "frac": tflops / peak,
+                         "flops_per_clip": gemm + attn, "peak_kind": "measured bf16 sustained (MEASURED_PEAKS.json)"},
+            "e2e": {"value": e2e, "unit": "s per 1344x768x124 video (37 latent frames, 7 clips)", "frames": count[0],
+                    "h2d_bytes": int(video.nbytes), "d2h_bytes": int(count[0] * h * 16 * w * 16 * 3 * 4),
+                    "reference_m5max_s": 69.0},
+            "gpu_launches_per_clip": launches, "steps": clips, "warmup": warmup}
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -456,6 +512,8 @@ def run_ours(args, rank, world, local_rank):
     model.close()
     if rank != 0:
         return
+    if world == 1 and args.extras == "all" and args.workload == "dense":
+        line["vae_decode"] = measure_vae(torch, H, peaks)
     if world == 1 and not args.no_cpu_baseline and cfg_name == "c2":
         v, b, r, desc, _ = cpu_step_sample(cfg, layout)
         line["cpu_baseline"] = {"value": v, "unit": "s", "cores": os.cpu_count(), "kind": "port", "sample": desc,
@@ -493,8 +551,9 @@ def main():
 
         # NCCL's communicator set-up lines (ranks, transports) on stderr: the library's own communicator carries the
         # barriers and all-gathers; the all-to-all data moves as NVLink peer stores from the kernels' epilogues
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        if os.environ.get("NCCL_DEBUG", "").upper() not in ("INFO", "TRACE"):
+            os.environ["NCCL_DEBUG"] = "INFO"
+            os.environ["NCCL_DEBUG_SUBSYS"] = "INIT"
         import torch
         import torch.distributed as dist
 

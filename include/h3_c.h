@@ -316,6 +316,55 @@ int h3k_wait_selftest(uint64_t budget_cycles, void* stream);
 /* Waits for `stream` and reports a device-side failure (bounded wait ran out) as H3_ERR_DEVICE. */
 int h3k_check(void* stream);
 
+/* ------------------------------------------------------------------------------------------ video VAE decoder
+ * MiniMax-H3's ViT video decoder (models::H3Vae, driven clip by clip by video::VideoVae, src/video/video_vae.hpp:16-27,
+ * video_vae.cpp:17-50; architecture in docs/architecture.md:80-92). Latents are voxels [frames][h][w][channels], the
+ * transformer's normalized latents; frames come out [16 h][16 w][3] RGB. */
+typedef struct h3vae_config {
+    uint32_t dim;       /* 2048 */
+    uint32_t heads;     /* 32 (of 64 dims) */
+    uint32_t ffn;       /* SwiGLU hidden, 8192 */
+    uint32_t blocks;    /* 36 */
+    uint32_t channels;  /* latent channels, 24 */
+    uint32_t registers; /* register tokens, 4 */
+    uint32_t clip;      /* latent frames a clip decodes, 7 */
+    uint32_t tile;      /* latents a tile spans, 16 (256 pixels) */
+    uint32_t overlap;   /* latents tiles overlap at least, 4 (64 pixels) */
+    float eps;          /* norms' epsilon (0: 1e-6) */
+} h3vae_config;
+
+typedef struct h3vae_model h3vae_model;
+/* A decoded frame: its index in the video and its pixels [16 h][16 w][3] in [0, 1] (count floats, host memory valid
+ * during the call) -- VideoVae::FrameSink (video_vae.hpp:22). */
+typedef void (*h3vae_frame_fn)(void* user, uint32_t index, const float* rgb, uint64_t count);
+
+/* VideoVae(dir, ctx, telemetry) (video_vae.cpp:9-15): weights "synthetic:SEED" (random-init, the decoder's checkpoint
+ * tensor names being in the absent mako-common sources). On `device`. */
+int h3vae_create(const h3vae_config* cfg, const char* weights, int32_t device, h3vae_model** out);
+/* VideoVae::decode(latents, frames, h, w, sink) (video_vae.cpp:17-50): frames = 5 n + 2; clips of 7 latent frames 5
+ * apart, each 28 pixel frames of which 17 are emitted after 3 of padding, the first 5 cross-faded linearly from the
+ * previous clip's last 5; ImageNet-normalized RGB reverted and clamped to [0, 1]; 17 n + 5 frames in order. */
+int h3vae_decode(h3vae_model* m, const float* latents, uint32_t frames, uint32_t h, uint32_t w, h3vae_frame_fn sink, void* user);
+/* H3Vae's decode of one clip (video_vae.cpp:33, decode_normalized): latents [clip][h][w][channels] (host) ->
+ * canvas [4 clip][16 h][16 w][3] ImageNet-normalized RGB (host). The _device form takes and fills device memory. */
+int h3vae_decode_clip(h3vae_model* m, const float* latents, uint32_t h, uint32_t w, float* canvas);
+int h3vae_decode_clip_device(h3vae_model* m, const float* latents, uint32_t h, uint32_t w, float* canvas);
+/* The tile layout along an axis of n latents (host; no counterpart in the reference's public interface). */
+int h3vae_tile_starts(uint32_t n, uint32_t tile, uint32_t overlap, uint32_t* starts, uint32_t cap, uint32_t* count);
+/* The rotary table of a tile's tokens [T][24][2] (cos, sin), T = frames th tw + specials (host). */
+int h3vae_rope_table(uint32_t frames, uint32_t th, uint32_t tw, uint32_t specials, float* out);
+int32_t h3vae_last_launches(h3vae_model* m);
+void* h3vae_stream(h3vae_model* m);
+void h3vae_destroy(h3vae_model* m);
+
+/* Kernel level, for the decoder's parity tests: dense attention with heads of head_dim (64 or 128) over independent
+ * segments (seg_rows rows every seg_stride rows; rows a multiple of seg_stride); the decoder's q/k norm and rotary on
+ * qkv [rows][3][heads][64] in place (rope [T][24][2], token = row mod T); a layer norm to bf16. */
+int h3k_attention_segments(const void* q, const void* k, const void* v, int64_t row_stride, int32_t heads, int32_t head_dim, int32_t rows,
+                           int32_t seg_rows, int32_t seg_stride, void* out, int64_t out_row_stride, void* stream);
+int h3k_vae_heads(void* qkv, int32_t rows, int32_t heads, int32_t T, const float* rope, float eps, void* stream);
+int h3k_layer_norm(const float* x, int32_t rows, int32_t d, const float* w, const float* b, float eps, void* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -28,27 +28,29 @@ struct Maps {
     CUtensorMap q, k, v; // (dim, head, row), box 64 x 1 x 64
 };
 
-// Issue the TMA loads of the 64 rows from `row` into rows [64 * half, 64 * half + 64) of a 128-row tile (both dim
-// halves). Rows past the tensor read as zeros.
+// Issue the TMA loads of the 64 rows from `row` into rows [64 * half, 64 * half + 64) of a 128-row tile (every 64-dim
+// half of a head of HD dims). Rows past the tensor read as zeros.
+template <int HD = 128>
 __device__ __forceinline__ void load_rows(uint8_t* tile, int half, int row, int head, const CUtensorMap* map, uint64_t* bar)
 {
 #pragma unroll
-    for (int hh = 0; hh < 2; ++hh)
+    for (int hh = 0; hh < HD / 64; ++hh)
         tma_load_3d(tile + hh * HALF + half * 8192, map, bar, hh * 64, head, row);
 }
 
 // Where query row `row`'s output (head `head`, dims from `d0`) goes: this rank's buffer, or straight to the row's
 // owner when the sequence-parallel exchange is fused into the epilogue (the stores are performed when the kernel
 // completes; the barrier that follows it on the stream orders them before any reader). Null for padding rows.
+template <int HD = 128>
 __device__ __forceinline__ __nv_bfloat16* out_ptr(const AttnParams& p, int row, int head, int d0)
 {
     if (row < 0)
         return nullptr;
     if (!p.peer_out[0])
-        return reinterpret_cast<__nv_bfloat16*>(p.out) + size_t(row) * p.out_row_stride + head * 128 + d0;
+        return reinterpret_cast<__nv_bfloat16*>(p.out) + size_t(row) * p.out_row_stride + head * HD + d0;
     const int owner = row / p.rows_per_rank, local = row - owner * p.rows_per_rank;
     return reinterpret_cast<__nv_bfloat16*>(p.peer_out[owner]) +
-           (size_t(p.my_rank) * p.rows_per_rank + local) * (size_t(p.heads) * 128) + head * 128 + d0;
+           (size_t(p.my_rank) * p.rows_per_rank + local) * (size_t(p.heads) * HD) + head * HD + d0;
 }
 
 // Key block j of a query unit that sees every row: rows [128 j, 128 j + 128) as two 64-row key units, in the pass
@@ -60,12 +62,15 @@ __device__ __forceinline__ int4 every_row_block(int j, int rows)
 }
 
 // ------------------------------------------------------------------------------------------------------------
-// Dense attention, two query tiles per CTA (256 query rows of one head) sharing every K/V tile.
+// Dense attention, two query tiles per CTA (256 query rows of one head) sharing every K/V tile. Heads of HD = 128 or
+// 64 dims. The rows may form several independent segments (seg_rows rows every seg_stride rows, e.g. the tiles of
+// a decoder batch): each CTA then takes query rows and keys of one segment only.
 //   warp 0      TMA: Q0 and Q1 once, then K_j and V_j (2-stage ring each)
 //   warp 1      MMA, in the order S0(0) S1(0) | PV0(j) S0(j+1) PV1(j) S1(j+1) | ...: while one tile's softmax runs
 //               the tensor core works on the other tile
 //   warps 2..5  softmax of tile 0, warps 6..9 softmax of tile 1 (thread = query row)
-// TMEM (512 columns): S0 | S1 | O0 | O1, 128 each. P_t (bf16, two per column) is written back over the first 64
+// TMEM (512 columns): S0 | S1 | O0 | O1 (128 columns each for S, HD for O). P_t (bf16, two per column) is written back
+// over the first 64
 // columns of S_t and the PV MMA reads it from TMEM (A operand in TMEM), so P never touches shared memory. The
 // tensor core executes one thread's MMAs in issue order, so S_t(j+1) overwrites P_t(j) only after PV_t(j) read it;
 // and s_full_t(j) tracks every earlier MMA, so once S_t(j) is complete, PV_t(j-1) is too and the softmax may write
@@ -73,16 +78,23 @@ __device__ __forceinline__ int4 every_row_block(int j, int rows)
 constexpr int A2_SPLIT = 1;        // warps sharing a query row in the softmax (2 measured no faster)
 constexpr int NT2 = 64 + 256 * A2_SPLIT;
 constexpr int A2_KST = 3, A2_VST = 2; // K is freed once both S MMAs read it, V after both PV MMAs
-constexpr int A2_OFF_Q = 0;           // Q0, Q1
-constexpr int A2_OFF_K = 2 * TILE;
-constexpr int A2_OFF_V = A2_OFF_K + A2_KST * TILE;
-constexpr int A2_OFF_BAR = A2_OFF_V + A2_VST * TILE;
-constexpr int A2_OFF_RED = A2_OFF_BAR + 256; // row maxima and sums exchanged between a row's warps
-constexpr int A2_SMEM = A2_OFF_RED + (A2_SPLIT > 1 ? 2 * 3 * A2_SPLIT * 128 * 4 : 0) + 1024;
+template <int HD>
+struct A2Smem {
+    static constexpr int TL = 128 * HD * 2; // a 128-row tile of one head
+    static constexpr int OFF_Q = 0;         // Q0, Q1
+    static constexpr int OFF_K = 2 * TL;
+    static constexpr int OFF_V = OFF_K + A2_KST * TL;
+    static constexpr int OFF_BAR = OFF_V + A2_VST * TL;
+    static constexpr int OFF_RED = OFF_BAR + 256; // row maxima and sums exchanged between a row's warps
+    static constexpr int TOTAL = OFF_RED + (A2_SPLIT > 1 ? 2 * 3 * A2_SPLIT * 128 * 4 : 0) + 1024;
+};
 
-template <int SPLIT>
+template <int SPLIT, int HD>
 __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid_constant__ Maps maps, const AttnParams p)
 {
+    using SM = A2Smem<HD>;
+    constexpr int TL = SM::TL, A2_OFF_Q = SM::OFF_Q, A2_OFF_K = SM::OFF_K, A2_OFF_V = SM::OFF_V, A2_OFF_BAR = SM::OFF_BAR,
+                  A2_OFF_RED = SM::OFF_RED;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t* smem = smem_raw + (((raw + 1023) & ~1023u) - raw);
@@ -100,9 +112,14 @@ __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xchg + 2);
 
     const int warp = warp_id();
-    const int pair = blockIdx.x, head = blockIdx.y;
-    // keys: 128-row blocks [kv0, kv0 + nkv), all of them or this CTA's part of a split launch (gridDim.z parts)
-    const int nkv_all = (p.rows + 127) / 128, per = (nkv_all + gridDim.z - 1) / gridDim.z;
+    const int head = blockIdx.y;
+    // the segment of this CTA's query rows and keys: rows [seg0, seg0 + seg_rows)
+    const int seg_rows = p.seg_rows > 0 ? p.seg_rows : p.rows;
+    const int pairs_per_seg = (seg_rows + 255) / 256;
+    const int seg = blockIdx.x / pairs_per_seg, pair = blockIdx.x - seg * pairs_per_seg;
+    const int seg0 = int(seg * (p.seg_rows > 0 ? p.seg_stride : 0));
+    // keys: 128-row blocks [kv0, kv0 + nkv) of the segment, all of them or this CTA's part of a split launch (gridDim.z)
+    const int nkv_all = (seg_rows + 127) / 128, per = (nkv_all + gridDim.z - 1) / gridDim.z;
     const int kv0 = blockIdx.z * per;
     const int nkv = min(nkv_all, kv0 + per) - kv0;
 
@@ -136,9 +153,9 @@ __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid
 
     if (warp == 0 && elect_one_lane()) {
         // ------------------------------------------------------------------------------------------ TMA
-        mbar_arrive_expect_tx(q_full, 2 * TILE);
+        mbar_arrive_expect_tx(q_full, 2 * TL);
         for (int u = 0; u < 4; ++u)
-            load_rows(smem + A2_OFF_Q + (u >> 1) * TILE, u & 1, (4 * pair + u) * 64, head, &maps.q, q_full);
+            load_rows<HD>(smem + A2_OFF_Q + (u >> 1) * TL, u & 1, seg0 + (4 * pair + u) * 64, head, &maps.q, q_full);
         // K runs ahead of V by up to the depth of its ring
         int jk = 0, jv = 0;
         while (jv < nkv) {
@@ -146,30 +163,30 @@ __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid
                 const int s = jk % A2_KST;
                 if (!mbar_wait(&k_empty[s], ((jk / A2_KST) & 1) ^ 1))
                     break;
-                mbar_arrive_expect_tx(&k_full[s], TILE);
-                load_rows(smem + A2_OFF_K + s * TILE, 0, 128 * (kv0 + jk), head, &maps.k, &k_full[s]);
-                load_rows(smem + A2_OFF_K + s * TILE, 1, 128 * (kv0 + jk) + 64, head, &maps.k, &k_full[s]);
+                mbar_arrive_expect_tx(&k_full[s], TL);
+                load_rows<HD>(smem + A2_OFF_K + s * TL, 0, seg0 + 128 * (kv0 + jk), head, &maps.k, &k_full[s]);
+                load_rows<HD>(smem + A2_OFF_K + s * TL, 1, seg0 + 128 * (kv0 + jk) + 64, head, &maps.k, &k_full[s]);
                 ++jk;
             } else {
                 const int s = jv % A2_VST;
                 if (!mbar_wait(&v_empty[s], ((jv / A2_VST) & 1) ^ 1))
                     break;
-                mbar_arrive_expect_tx(&v_full[s], TILE);
-                load_rows(smem + A2_OFF_V + s * TILE, 0, 128 * (kv0 + jv), head, &maps.v, &v_full[s]);
-                load_rows(smem + A2_OFF_V + s * TILE, 1, 128 * (kv0 + jv) + 64, head, &maps.v, &v_full[s]);
+                mbar_arrive_expect_tx(&v_full[s], TL);
+                load_rows<HD>(smem + A2_OFF_V + s * TL, 0, seg0 + 128 * (kv0 + jv), head, &maps.v, &v_full[s]);
+                load_rows<HD>(smem + A2_OFF_V + s * TL, 1, seg0 + 128 * (kv0 + jv) + 64, head, &maps.v, &v_full[s]);
                 ++jv;
             }
         }
     } else if (warp == 1 && elect_one_lane()) {
         // ------------------------------------------------------------------------------------------ MMA
         const uint32_t id_s = idesc_bf16(128, 128);
-        const uint32_t id_pv = idesc_bf16(128, 128, false, true);
+        const uint32_t id_pv = idesc_bf16(128, HD, false, true);
         auto issue_s = [&](int t, int j) {
             const int ks = j % A2_KST;
-            const uint32_t sq = smem_u32(smem + A2_OFF_Q + t * TILE);
-            const uint32_t sk = smem_u32(smem + A2_OFF_K + ks * TILE);
+            const uint32_t sq = smem_u32(smem + A2_OFF_Q + t * TL);
+            const uint32_t sk = smem_u32(smem + A2_OFF_K + ks * TL);
 #pragma unroll
-            for (int kk = 0; kk < 8; ++kk) {
+            for (int kk = 0; kk < HD / 16; ++kk) {
                 const uint32_t off = (kk >> 2) * HALF + (kk & 3) * 32;
                 mma_bf16_ss(tmem + t * 128, sdesc_sw128(sq + off, 16, 1024), sdesc_sw128(sk + off, 16, 1024), id_s, kk > 0);
             }
@@ -179,10 +196,10 @@ __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid
         };
         auto issue_pv = [&](int t, int j) {
             const int vs = j % A2_VST;
-            const uint32_t sv = smem_u32(smem + A2_OFF_V + vs * TILE);
+            const uint32_t sv = smem_u32(smem + A2_OFF_V + vs * TL);
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk)
-                mma_bf16_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8, sdesc_sw128(sv + kk * 2048, HALF, 1024), id_pv, (j | kk) != 0);
+                mma_bf16_ts(tmem + 256 + t * HD, tmem + t * 128 + kk * 8, sdesc_sw128(sv + kk * 2048, HALF, 1024), id_pv, (j | kk) != 0);
             mma_commit(&pv_done[t]);
             if (t == 1)
                 mma_commit(&v_empty[vs]); // both tiles' PV MMAs have read V_j
@@ -218,14 +235,15 @@ __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid
         // -------------------------------------------------------------------------------------- softmax
         // SPLIT warps share each row: the warps of (tile t, slice hc) handle keys [hc NC, hc NC + NC) of their rows
         // and agree on the row maximum through shared memory.
-        constexpr int NC = 128 / SPLIT;
+        constexpr int NC = 128 / SPLIT; // keys of a step this slice handles
+        constexpr int OC = HD / SPLIT;  // output columns this slice rescales and stores
         const int t = (warp - 2) / (4 * SPLIT);
         const int hc = ((warp - 2) % (4 * SPLIT)) / 4;
         const int quarter = warp & 3;
         const int row = quarter * 32 + lane_id();
         const uint32_t lane_base = uint32_t(quarter * 32) << 16;
         const uint32_t tS = tmem + lane_base + t * 128;
-        const uint32_t tO = tmem + lane_base + 256 + t * 128 + hc * NC;
+        const uint32_t tO = tmem + lane_base + 256 + t * HD + hc * OC;
         float* red = reinterpret_cast<float*>(smem + A2_OFF_RED) + t * (3 * SPLIT * 128); // [3 slots][SPLIT][128 rows]
         const float sl2 = p.scale * 1.4426950408889634f;
         float m = -INFINITY, l = 0.f;
@@ -247,7 +265,7 @@ __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid
                     for (int i = 0; i < 32; ++i)
                         s[c * 32 + i] = __uint_as_float(r[c][i]);
             }
-            const int left = p.rows - (kv0 + j) * 128 - hc * NC;
+            const int left = seg_rows - (kv0 + j) * 128 - hc * NC;
             if (left < NC) {
 #pragma unroll
                 for (int c = 0; c < NC; ++c)
@@ -300,7 +318,7 @@ __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid
             if (j > 0 && __any_sync(0xffffffffu, need)) {
                 // O_t holds PV_t(0..j-1), complete (S_t(j) was issued after PV_t(j-1)); each slice rescales its columns
 #pragma unroll 1
-                for (int c = 0; c < NC / 32; ++c) {
+                for (int c = 0; c < OC / 32; ++c) {
                     uint32_t o[32];
                     tmem_ld32(tO + c * 32, o);
                     tmem_wait_ld();
@@ -342,12 +360,12 @@ __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid
             const int out_row = pair * 256 + t * 128 + row;
             const size_t item = (size_t(blockIdx.z) * p.rows + out_row) * p.heads + head;
 #pragma unroll 1
-            for (int c = 0; c < NC / 32; ++c) {
+            for (int c = 0; c < OC / 32; ++c) {
                 uint32_t o[32];
                 tmem_ld32(tO + c * 32, o);
                 tmem_wait_ld();
                 if (out_row < p.rows) {
-                    float4* d4 = reinterpret_cast<float4*>(p.part_o + item * 128 + hc * NC + c * 32);
+                    float4* d4 = reinterpret_cast<float4*>(p.part_o + item * 128 + hc * OC + c * 32);
 #pragma unroll
                     for (int i = 0; i < 8; ++i)
                         d4[i] = make_float4(__uint_as_float(o[4 * i]), __uint_as_float(o[4 * i + 1]), __uint_as_float(o[4 * i + 2]),
@@ -358,11 +376,12 @@ __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid
                 *reinterpret_cast<float2*>(p.part_ml + item * 2) = make_float2(m, l);
         } else if (done) {
             tc_fence_after();
-            const int out_row = pair * 256 + t * 128 + row;
+            const int in_seg = pair * 256 + t * 128 + row;
+            const int out_row = seg0 + in_seg;
             const float inv = l > 0.f ? 1.f / l : 0.f;
-            __nv_bfloat16* dst = out_ptr(p, out_row < p.rows ? out_row : -1, head, hc * NC);
+            __nv_bfloat16* dst = in_seg < seg_rows && out_row < p.rows ? out_ptr<HD>(p, out_row, head, hc * OC) : nullptr;
 #pragma unroll 1
-            for (int c = 0; c < NC / 32; ++c) {
+            for (int c = 0; c < OC / 32; ++c) {
                 uint32_t o[32];
                 tmem_ld32(tO + c * 32, o);
                 tmem_wait_ld();
@@ -787,10 +806,10 @@ bool split_dense(int rows, int heads)
     return (rows + 127) / 128 >= 4 && ctas < 6LL * num_sms();
 }
 
-CUtensorMap rows_map(const void* base, int heads, int rows, int64_t row_stride)
+CUtensorMap rows_map(const void* base, int heads, int rows, int64_t row_stride, int head_dim = 128)
 {
-    const uint64_t dims[3] = {128, uint64_t(heads), uint64_t(rows > 0 ? rows : 1)};
-    const uint64_t str[2] = {256, uint64_t(row_stride) * 2};
+    const uint64_t dims[3] = {uint64_t(head_dim), uint64_t(heads), uint64_t(rows > 0 ? rows : 1)};
+    const uint64_t str[2] = {uint64_t(head_dim) * 2, uint64_t(row_stride) * 2};
     const uint32_t box[3] = {64, 1, 64};
     return make_tmap(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, str, box);
 }
@@ -811,28 +830,38 @@ int attention(const AttnParams& p, cudaStream_t s)
     const bool sparse = p.blocks != nullptr;
     if (sparse && (p.grid.cubes() <= 0 || !p.nblocks || !p.q_rows || p.q_tiles <= 0 || p.rows != p.grid.rows()))
         throw CudaError("attention: bad sparse arguments");
+    if (p.head_dim != 128 && (p.head_dim != 64 || sparse || p.peer_out[0] || p.part_o))
+        throw CudaError("attention: heads of 64 dims are for dense attention on one rank only");
+    if (p.seg_rows < 0 || (p.seg_rows > 0 && (sparse || p.part_o || p.seg_stride < p.seg_rows || p.rows % p.seg_stride)))
+        throw CudaError("attention: segments must tile the rows (rows a multiple of seg_stride >= seg_rows; dense, unsplit)");
     if (p.rows <= 0)
         return 0;
     Maps maps;
-    maps.q = rows_map(p.q, p.heads, p.rows, p.row_stride);
-    maps.k = rows_map(p.k, p.heads, p.rows, p.row_stride);
-    maps.v = rows_map(p.v, p.heads, p.rows, p.row_stride);
-    static std::atomic<uint64_t> opt_in[2];
-    if (sparse)
-        smem_opt_in(attn3_kernel, A3_SMEM, opt_in[1]);
-    else
-        smem_opt_in(attn2_kernel<A2_SPLIT>, A2_SMEM, opt_in[0]);
-    // Dense: two query tiles per CTA share every K/V tile (half the shared-memory traffic per FLOP). Sparse: query
-    // tiles have their own key lists, so one tile per CTA with double-buffered scores.
+    maps.q = rows_map(p.q, p.heads, p.rows, p.row_stride, p.head_dim);
+    maps.k = rows_map(p.k, p.heads, p.rows, p.row_stride, p.head_dim);
+    maps.v = rows_map(p.v, p.heads, p.rows, p.row_stride, p.head_dim);
+    static std::atomic<uint64_t> opt_in[3];
     if (sparse) {
+        // Query tiles have their own key lists, so one tile per CTA with double-buffered scores.
+        smem_opt_in(attn3_kernel, A3_SMEM, opt_in[1]);
         attn3_kernel<<<p.q_tiles * p.heads, NT3, A3_SMEM, s>>>(maps, p);
         H3_CUDA(cudaGetLastError());
         return 1;
     }
+    // Dense: two query tiles per CTA share every K/V tile (half the shared-memory traffic per FLOP).
+    const int segs = p.seg_rows > 0 ? p.rows / int(p.seg_stride) : 1;
+    const int pairs = ((p.seg_rows > 0 ? p.seg_rows : p.rows) + 255) / 256;
+    if (p.head_dim == 64) {
+        smem_opt_in(attn2_kernel<A2_SPLIT, 64>, A2Smem<64>::TOTAL, opt_in[2]);
+        attn2_kernel<A2_SPLIT, 64><<<dim3(pairs * segs, p.heads, 1), NT2, A2Smem<64>::TOTAL, s>>>(maps, p);
+        H3_CUDA(cudaGetLastError());
+        return 1;
+    }
+    smem_opt_in(attn2_kernel<A2_SPLIT, 128>, A2Smem<128>::TOTAL, opt_in[0]);
     // A launch of few waves (several ranks leave each a few heads) loses much of its last wave; splitting every CTA's
     // keys in two, given scratch for the halves, doubles the CTAs, and a combine kernel merges them.
-    const int parts = p.part_o && p.part_ml && split_dense(p.rows, p.heads) ? 2 : 1;
-    attn2_kernel<A2_SPLIT><<<dim3((p.rows + 255) / 256, p.heads, parts), NT2, A2_SMEM, s>>>(maps, p);
+    const int parts = segs == 1 && p.part_o && p.part_ml && split_dense(p.rows, p.heads) ? 2 : 1;
+    attn2_kernel<A2_SPLIT, 128><<<dim3(pairs * segs, p.heads, parts), NT2, A2Smem<128>::TOTAL, s>>>(maps, p);
     H3_CUDA(cudaGetLastError());
     if (parts == 1)
         return 1;

@@ -57,21 +57,26 @@ struct CubeGrid {
 };
 
 struct AttnParams {
-    // q, k, v: element (row, head, dim) at base + row * row_stride + head * 128 + dim (bf16), rows in model order
+    // q, k, v: element (row, head, dim) at base + row * row_stride + head * head_dim + dim (bf16), rows in model order
     const void* q = nullptr;
     const void* k = nullptr;
     const void* v = nullptr;
     int64_t row_stride = 0; // elements between consecutive rows of q, k and v
     int heads = 0;          // heads addressed by the q/k/v tensors
     int rows = 0;           // query and key rows (sparse mode: grid.rows())
-    void* out = nullptr;    // o: (row, head, dim) at out + row * out_row_stride + head * 128 + dim
+    int head_dim = 128;     // 128, or 64 (dense mode only; the video decoder's heads)
+    // Dense mode: the rows as independent segments of seg_rows rows, one every seg_stride rows (0: one segment of
+    // `rows`); queries see the keys of their own segment only.
+    int seg_rows = 0;
+    int64_t seg_stride = 0;
+    void* out = nullptr;    // o: (row, head, dim) at out + row * out_row_stride + head * head_dim + dim
     int64_t out_row_stride = 0;
     // Sequence parallel with the exchange fused into the epilogue: row R's output goes straight to its owner
     // R / rows_per_rank, into that rank's [P][rows_per_rank][heads x 128] buffer (block my_rank), mapped into this
     // process (peer_out[0] null: write `out`).
     void* peer_out[8] = {};
     int rows_per_rank = 0, my_rank = 0;
-    float scale = 0.08838834764831845f; // 1 / sqrt(128)
+    float scale = 0.08838834764831845f; // 1 / sqrt(head_dim)
     // Dense mode, launches of few waves: scratch for a key range split in two (null: never split). part_o
     // [2][rows][heads][128] fp32 receives each half's unnormalised output and part_ml [2][rows][heads][2] its row
     // maximum (log2 units) and sum; a combine kernel merges the halves into `out`. Sized by attention_split_bytes.

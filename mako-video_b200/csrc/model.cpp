@@ -3,6 +3,7 @@
 #include "model.hpp"
 
 #include "common.hpp"
+#include "devbuf.hpp"
 #include "embed.cuh"
 #include "gemm.cuh"
 #include "rows.cuh"
@@ -186,51 +187,7 @@ bool parse_int8(const std::string& s, uint32_t& mask)
     return true;
 }
 
-// -------------------------------------------------------------------------------------------------- buffers
 namespace {
-
-struct DevBuf {
-    void* p = nullptr;
-    size_t bytes = 0;
-    DevBuf() = default;
-    DevBuf(const DevBuf&) = delete;
-    DevBuf& operator=(const DevBuf&) = delete;
-    DevBuf(DevBuf&& o) noexcept : p(o.p), bytes(o.bytes) { o.p = nullptr, o.bytes = 0; }
-    DevBuf& operator=(DevBuf&& o) noexcept
-    {
-        if (this != &o) {
-            release();
-            p = o.p, bytes = o.bytes;
-            o.p = nullptr, o.bytes = 0;
-        }
-        return *this;
-    }
-    ~DevBuf() { release(); }
-    void release()
-    {
-        if (p)
-            cudaFree(p);
-        p = nullptr;
-        bytes = 0;
-    }
-    void ensure(size_t n)
-    {
-        if (n <= bytes)
-            return;
-        release();
-        H3_CUDA(cudaMalloc(&p, n));
-        // The legacy-stream memset is not ordered with the model's non-blocking stream: finish it before anything is
-        // queued there (growth is rare: the first step of a layout or of more noise levels).
-        H3_CUDA(cudaMemset(p, 0, n));
-        H3_CUDA(cudaDeviceSynchronize());
-        bytes = n;
-    }
-    template <class T>
-    T* as() const
-    {
-        return static_cast<T*>(p);
-    }
-};
 
 // Synthetic tensor ids (fixed: the CPU oracle regenerates the same values from them).
 enum : uint32_t {

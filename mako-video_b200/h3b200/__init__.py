@@ -86,7 +86,20 @@ class h3k_cube_grid(ctypes.Structure):
     _fields_ = [("dense_rows", ctypes.c_int32), ("frames", ctypes.c_int32), ("ph", ctypes.c_int32), ("pw", ctypes.c_int32)]
 
 
+class h3vae_config(ctypes.Structure):
+    _fields_ = [("dim", ctypes.c_uint32), ("heads", ctypes.c_uint32), ("ffn", ctypes.c_uint32), ("blocks", ctypes.c_uint32),
+                ("channels", ctypes.c_uint32), ("registers", ctypes.c_uint32), ("clip", ctypes.c_uint32), ("tile", ctypes.c_uint32),
+                ("overlap", ctypes.c_uint32), ("eps", ctypes.c_float)]
+
+
+# The video VAE decoder's shapes: MiniMax-H3's (docs/architecture.md:80-92 of the reference) and a small one for tests.
+VAE_CONFIGS = {
+    "h3": dict(dim=2048, heads=32, ffn=8192, blocks=36, channels=24, registers=4, clip=7, tile=16, overlap=4),
+    "small": dict(dim=256, heads=4, ffn=512, blocks=2, channels=24, registers=4, clip=7, tile=16, overlap=4),
+}
+
 PROGRESS_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32)
+FRAME_FN = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_uint32, ctypes.POINTER(ctypes.c_float), ctypes.c_uint64)
 PROBE_FN = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_char_p, ctypes.c_int32, ctypes.POINTER(ctypes.c_float), ctypes.c_uint64)
 
 # Every exported symbol and its signature (restype, argtypes). Tests check the library exports each of them.
@@ -138,6 +151,18 @@ SIGNATURES = {
     "h3k_adaln": (ctypes.c_int, [_P, _P, _P, _I32, _I32, _I32, _I32, _P, _P]),
     "h3k_heads": (ctypes.c_int, [_P, _I64, _I32, _P, _P, _I32, _I32, _P, _I64, _P]),
     "h3k_check": (ctypes.c_int, [_P]),
+    "h3vae_create": (ctypes.c_int, [ctypes.POINTER(h3vae_config), ctypes.c_char_p, _I32, _P]),
+    "h3vae_decode": (ctypes.c_int, [_P, _P, _U32, _U32, _U32, FRAME_FN, _P]),
+    "h3vae_decode_clip": (ctypes.c_int, [_P, _P, _U32, _U32, _P]),
+    "h3vae_decode_clip_device": (ctypes.c_int, [_P, _P, _U32, _U32, _P]),
+    "h3vae_tile_starts": (ctypes.c_int, [_U32, _U32, _U32, _P, _U32, _P]),
+    "h3vae_rope_table": (ctypes.c_int, [_U32, _U32, _U32, _U32, _P]),
+    "h3vae_last_launches": (_I32, [_P]),
+    "h3vae_stream": (_P, [_P]),
+    "h3vae_destroy": (None, [_P]),
+    "h3k_attention_segments": (ctypes.c_int, [_P, _P, _P, _I64, _I32, _I32, _I32, _I32, _I32, _P, _I64, _P]),
+    "h3k_vae_heads": (ctypes.c_int, [_P, _I32, _I32, _I32, _P, _F, _P]),
+    "h3k_layer_norm": (ctypes.c_int, [_P, _I32, _I32, _P, _P, _F, _P, _P]),
 }
 
 _lib = None
@@ -427,3 +452,77 @@ def convert_weights(config, src, dst, renames=None, interleaved=False, eps=1e-6)
     if interleaved:
         lines.append("qkv_layout interleaved")
     check(lib().h3_convert_weights(ctypes.byref(cfg), str(src).encode(), str(dst).encode(), "\n".join(lines).encode()))
+
+
+def vae_tile_starts(n, tile=16, overlap=4):
+    """h3vae_tile_starts: the tile layout along an axis of n latents."""
+    buf = (ctypes.c_uint32 * 256)()
+    cnt = ctypes.c_uint32()
+    check(lib().h3vae_tile_starts(n, tile, overlap, buf, 256, ctypes.byref(cnt)))
+    return [buf[i] for i in range(cnt.value)]
+
+
+def vae_rope_table(frames, th, tw, specials):
+    T = frames * th * tw + specials
+    out = np.zeros((T, 24, 2), np.float32)
+    check(lib().h3vae_rope_table(frames, th, tw, specials, out.ctypes.data))
+    return out
+
+
+class VideoDecoder:
+    """The video VAE decoder (h3vae_create / h3vae_decode / h3vae_decode_clip)."""
+
+    def __init__(self, config="small", seed=0, device=0, eps=1e-6):
+        c = VAE_CONFIGS[config] if isinstance(config, str) else config
+        self.cfg = dict(c)
+        self.c = h3vae_config(c["dim"], c["heads"], c["ffn"], c["blocks"], c["channels"], c["registers"], c["clip"], c["tile"],
+                              c["overlap"], eps)
+        self.h = ctypes.c_void_p()
+        check(lib().h3vae_create(ctypes.byref(self.c), f"synthetic:{seed}".encode(), device, ctypes.byref(self.h)))
+
+    def close(self):
+        if self.h:
+            lib().h3vae_destroy(self.h)
+            self.h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def decode_clip(self, latents):
+        """latents [clip][h][w][channels] -> canvas [4 clip][16 h][16 w][3] (ImageNet-normalized)."""
+        lat = np.ascontiguousarray(latents, dtype=np.float32)
+        clip, h, w, _ = lat.shape
+        out = np.zeros((clip * 4, h * 16, w * 16, 3), np.float32)
+        check(lib().h3vae_decode_clip(self.h, lat.ctypes.data, h, w, out.ctypes.data))
+        return out
+
+    def decode_clip_device(self, lat_ptr, h, w, out_ptr):
+        check(lib().h3vae_decode_clip_device(self.h, lat_ptr, h, w, out_ptr))
+
+    def decode(self, latents, sink=None):
+        """latents [5 n + 2][h][w][channels] -> the 17 n + 5 frames [16 h][16 w][3] in [0, 1] (a list, or each handed to
+        sink(index, frame))."""
+        lat = np.ascontiguousarray(latents, dtype=np.float32)
+        frames, h, w, _ = lat.shape
+        got = []
+
+        def cb(user, index, rgb, count):
+            a = np.ctypeslib.as_array(rgb, shape=(count,)).reshape(h * 16, w * 16, 3)
+            if sink is None:
+                got.append(a.copy())
+            else:
+                sink(int(index), a)
+
+        fn = FRAME_FN(cb)
+        check(lib().h3vae_decode(self.h, lat.ctypes.data, frames, h, w, fn, None))
+        return got
+
+    @property
+    def stream(self):
+        return lib().h3vae_stream(self.h)
+
+    def last_launches(self):
+        return int(lib().h3vae_last_launches(self.h))

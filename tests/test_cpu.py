@@ -491,3 +491,29 @@ def test_h3_tensor_shapes_and_768p_rows_match_the_reference_prose():
     lay = h3b200.Layout(text=300, frames=37, h=48, w=84, audio=207, cond_frames=0)
     assert lay.video_rows == 37296 and lay.audio_rows == 414
     assert h3b200.lib().h3_layout_rows(ctypes.byref(lay.c)) == 300 + 414 + 37296
+
+
+# ------------------------------------------------------------------------------------------- video VAE decoder
+
+@pytest.mark.parametrize("n", [1, 7, 16, 17, 20, 24, 29, 48, 84, 135, 240])
+def test_vae_tile_layout_matches_oracle(n):
+    """Tiles of 16 latents overlapping by at least 4 (64 pixels), the slack spread over the overlaps: the library's
+    layout equals the oracle's, covers the axis exactly, and 768p decodes as 4 x 7 tiles a clip
+    (docs/architecture.md:91-92)."""
+    from oracle import vae_oracle as V
+    got = h3b200.vae_tile_starts(n)
+    assert got == V.tile_starts(n)
+    size = min(16, n)
+    assert got[0] == 0 and got[-1] + size == n
+    for a, b in zip(got, got[1:]):
+        assert 4 <= a + 16 - b < 16
+    if n == 48:
+        assert len(got) == 4
+    if n == 84:
+        assert len(got) == 7
+
+
+def test_vae_rope_table_matches_oracle():
+    from oracle import vae_oracle as V
+    for frames, th, tw in ((7, 16, 16), (7, 9, 16), (3, 5, 4)):
+        np.testing.assert_array_equal(h3b200.vae_rope_table(frames, th, tw, 5), V.rope_table(frames, th, tw, 5))
