@@ -1,6 +1,7 @@
 // Compiles the drop-in header the way the reference's sampler would use it (mako::models::H3) and exercises its
 // host-side members, which need no GPU: parse_int8, rows, and the refusal of a missing checkpoint.
 #include "models/h3.hpp"
+#include "video/video_vae.hpp"
 
 #include <cstddef>
 #include <cstdio>
@@ -49,6 +50,16 @@ int main()
     check(threw, "a missing checkpoint is refused with a message");
     check(H3::check_weights("/models/minimax-h3/FL2VA/transformer").find("cannot open") != std::string::npos,
           "check_weights reports a missing checkpoint");
+    // The video decoder's drop-in: the engine's call shapes compile; a real model directory is refused with a message.
+    check(mako::video::VideoVae::pixel_frames(37) == 124 && mako::video::VideoVae::pixel_frames(7) == 22, "VideoVae::pixel_frames");
+    bool vae_threw = false;
+    try {
+        mako::mtl::Context ctx;
+        mako::video::VideoVae vae("/models/minimax-h3/video_vae", ctx, mako::gpu::Telemetry::off);
+    } catch (const std::runtime_error& e) {
+        vae_threw = std::string(e.what()).find("synthetic") != std::string::npos;
+    }
+    check(vae_threw, "VideoVae refuses a checkpoint directory with a message");
     // The C ABI's struct layouts, for the bindings' own declarations to be checked against (tests/test_cpp_dropin.py).
     std::printf("abi h3_config %zu %zu %zu\n", sizeof(h3_config), offsetof(h3_config, refiner_blocks), offsetof(h3_config, curve_dims));
     std::printf("abi h3_layout %zu %zu %zu\n", sizeof(h3_layout), offsetof(h3_layout, refs), offsetof(h3_layout, n_refs));
@@ -56,5 +67,6 @@ int main()
     std::printf("abi h3_world %zu %zu\n", sizeof(h3_world), offsetof(h3_world, nccl_id));
     std::printf("abi h3k_gemm_args %zu %zu\n", sizeof(h3k_gemm_args), offsetof(h3k_gemm_args, b_scale));
     std::printf("abi h3k_cube_grid %zu\n", sizeof(h3k_cube_grid));
+    std::printf("abi h3vae_config %zu %zu\n", sizeof(h3vae_config), offsetof(h3vae_config, eps));
     return failures ? 1 : 0;
 }

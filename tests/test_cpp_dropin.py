@@ -1,4 +1,4 @@
-"""The C++ drop-in header (include/models/h3.hpp) compiles against the reference's usage and its host-side members
+"""The C++ drop-in headers (include/models/h3.hpp, include/video/video_vae.hpp) compile against the reference's usage and its host-side members
 work through libh3b200.so (no GPU needed)."""
 import ctypes
 import os
@@ -28,5 +28,6 @@ def test_dropin_header_compiles_and_runs(tmp_path):
         "h3_world": [ctypes.sizeof(H.h3_world), H.h3_world.nccl_id.offset],
         "h3k_gemm_args": [ctypes.sizeof(H.h3k_gemm_args), H.h3k_gemm_args.b_scale.offset],
         "h3k_cube_grid": [ctypes.sizeof(H.h3k_cube_grid)],
+        "h3vae_config": [ctypes.sizeof(H.h3vae_config), H.h3vae_config.eps.offset],
     }
     assert abi == want, (abi, want)
