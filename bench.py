@@ -38,6 +38,7 @@ WORKLOADS = {
     "long": ("c2", "c5", 0.0, 1, 0, "C5: 15 s clip, 92736 video + 1008 keyframe + 512 text + 640 audio rows, dense"),
     "long-sparse": ("c2", "c5", 0.1, 3, 0, "C5 sparse, ratio 0.1, local 3"),
     "c1": ("c1", "c1", 0.0, 1, 0, "C1: one d=1024 block, 576 rows"),
+    "vae": (None, None, 0.0, 1, 0, "MiniMax-H3's video VAE decoder on 768p latents"),
     "h3": ("h3", "h3", 0.0, 1, 0, "MiniMax-H3 itself: d 5376, 56 heads, SwiGLU 14336, 50 blocks, 1344x768x124 frames = 37296 video "
                                   "+ 512 text + 414 audio rows, dense"),
 }
@@ -195,6 +196,9 @@ def run_reference(args, rank, world):
     if rank != 0:
         return
     import h3b200 as H
+    if args.workload == "vae":
+        emit(reference_vae(H))
+        return
     cfg_name, lay_name, ratio, local, int8, wdesc = WORKLOADS[args.workload]
     cfg = dict(H.CONFIGS[cfg_name])
     layout = H.Layout.named(lay_name)
@@ -392,6 +396,61 @@ def vae_flops(cfg, h, w):
     return gemm, attn, ty * tx, T
 
 
+def reference_vae(H):
+    """The decoder's CPU restatement (oracle/vae_oracle.py) on one 16 x 16-latent tile of a clip with ONE block of
+    MiniMax-H3's decoder width, the block scaled to 36 and the tile to the 28 tiles of a 768p clip."""
+    import torch
+    from oracle import vae_oracle as V
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    cfg = dict(H.VAE_CONFIGS["h3"])
+    one, none = dict(cfg, blocks=1), dict(cfg, blocks=0)
+    w1 = V.make_weights(one, 0)
+    w0 = dict(w1, blocks=[])
+    lat = np.random.default_rng(0).standard_normal((cfg["clip"], 16, 16, cfg["channels"]), dtype=np.float32)
+    t0 = time.perf_counter()
+    V.decode_clip(none, w0, lat)
+    rest = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    V.decode_clip(one, w1, lat)
+    block = time.perf_counter() - t0 - rest
+    clip_s = 28 * (rest + cfg["blocks"] * block)
+    return {"metric": "s per 768p clip of the video VAE decoder (7 latent frames -> 28 frames)", "value": clip_s, "unit": "s",
+            "impl": "reference", "n_gpus": 0, "steps": 1, "warmup": 0, "ms_per_step": (rest + block) * 1e3,
+            "ms_per_step_is": "one timed sample: one tile with one block, plus one tile without blocks",
+            "extrapolated_from": "1 tile x 28, 1 block x 36", "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "cpu_baseline": {"value": clip_s, "unit": "s", "cores": threads, "kind": "port",
+                             "sample": f"oracle/vae_oracle.py decode_clip on one 16 x 16-latent tile, d 2048, one block ({block:.2f} s) "
+                                       f"and the rest ({rest:.2f} s); {threads} host threads"},
+            "e2e": {"value": clip_s, "unit": "s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def run_vae(args, rank):
+    """--workload vae: the decoder alone (one line with its metric; --profile: warm-up + steps clip decodes, nothing
+    timed, for ncu)."""
+    import torch
+    import h3b200 as H
+
+    if rank != 0:
+        return
+    if args.profile:
+        cfg = H.VAE_CONFIGS["h3"]
+        m = H.VideoDecoder(cfg, seed=0)
+        lat = torch.randn(cfg["clip"], 48, 84, cfg["channels"], device="cuda")
+        canvas = torch.empty((cfg["clip"] * 4, 48 * 16, 84 * 16, 3), device="cuda")
+        for _ in range(args.warmup + args.steps):
+            m.decode_clip_device(lat.data_ptr(), 48, 84, canvas.data_ptr())
+        m.close()
+        return
+    peaks, _ = load_peaks()
+    r = measure_vae(torch, H, peaks, clips=args.steps, warmup=max(args.warmup, 1))
+    r.update({"n_gpus": 1, "ms_per_step": r["value"] * 1e3, "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+              "dtype": "bf16", "data": "synthetic (seeded normal latents, hash-generated weights)"})
+    emit(r)
+
+
 def measure_vae(torch, H, peaks, clips=3, warmup=2):
     """The video VAE decoder at MiniMax-H3's size on 768p latents: device seconds per clip (latents and canvas in
     HBM), and a whole 1344 x 768 x 124-frame video (37 latent frames, 7 clips) through h3vae_decode from host latents
@@ -545,6 +604,12 @@ def main():
     os.dup2(2, 1)
     if args.impl == "reference":
         run_reference(args, rank, world)
+        return
+    if args.workload == "vae":
+        import torch
+
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+        run_vae(args, rank)
         return
     if world > 1:
         import datetime
