@@ -52,9 +52,11 @@ __device__ __forceinline__ float block_max(float v, float* red)
 // vectors are not re-read per row. A row's sum of squares (and, for int8, its maximum) is combined from the warps'
 // partials through shared memory in a fixed order.
 // Shared memory: nbufs mbarriers, the partials [RM_BATCH][RM_WARPS] (sum) and [RM_BATCH][RM_WARPS] (max), then at
-// byte 1024 the row buffers [nbufs][nb][d] fp32.
-constexpr int RM_WARPS = 8, RM_BATCH = 4, RM_MAXBUFS = 6, RM_MAXJ = 8; // RM_MAXJ float4 per lane: rows up to 8192 wide
-constexpr size_t kRmsRowSmem = 204800;                                 // row buffers: 2 x 4 rows of 5120 floats
+// byte RM_ROWS_OFF the row buffers [nbufs][nb][d] fp32. Batches hold as many rows as two buffers fit (each batch costs
+// two CTA barriers, so narrow rows take bigger batches).
+constexpr int RM_WARPS = 8, RM_BATCH = 16, RM_MAXBUFS = 6, RM_MAXJ = 8; // RM_MAXJ float4 per lane: rows up to 8192 wide
+constexpr int RM_ROWS_OFF = 64 + 2 * RM_BATCH * RM_WARPS * 4;           // after the barriers and the partials
+constexpr size_t kRmsRowSmem = 204800;                                  // row buffers: 2 x 5 rows of 5120 floats
 
 __global__ void __launch_bounds__(RM_WARPS * 32, 1) rms_mod_kernel(const RmsModParams p, int nb, int nbufs, int rows_per_cta)
 {
@@ -62,7 +64,7 @@ __global__ void __launch_bounds__(RM_WARPS * 32, 1) rms_mod_kernel(const RmsModP
     uint64_t* full = reinterpret_cast<uint64_t*>(rm_smem); // [nbufs]
     float* part = reinterpret_cast<float*>(rm_smem + 64);
     float* pmax = part + RM_BATCH * RM_WARPS;
-    float* rows = reinterpret_cast<float*>(rm_smem + 1024);
+    float* rows = reinterpret_cast<float*>(rm_smem + RM_ROWS_OFF);
     const int w = warp_id(), lane = lane_id();
     const int n4 = p.d >> 2, nw4 = (n4 + RM_WARPS - 1) / RM_WARPS;
     const int r0 = blockIdx.x * rows_per_cta, r1 = min(p.rows, r0 + rows_per_cta);
@@ -482,9 +484,9 @@ void rms_mod_rows(const RmsModParams& p, cudaStream_t s)
     const int nbufs = int(std::min<size_t>(RM_MAXBUFS, kRmsRowSmem / (nb * row_bytes)));
     const int per = std::max(1, (p.rows + num_sms() - 1) / num_sms());
     const int grid = (p.rows + per - 1) / per;
-    const int smem = 1024 + int(nbufs * nb * row_bytes);
+    const int smem = RM_ROWS_OFF + int(nbufs * nb * row_bytes);
     static std::atomic<uint64_t> opt_in;
-    smem_opt_in(rms_mod_kernel, 1024 + int(kRmsRowSmem), opt_in);
+    smem_opt_in(rms_mod_kernel, RM_ROWS_OFF + int(kRmsRowSmem), opt_in);
     rms_mod_kernel<<<grid, RM_WARPS * 32, smem, s>>>(p, nb, nbufs, per);
     H3_CUDA(cudaGetLastError());
 }
