@@ -258,6 +258,11 @@ int h3k_heads_partial(void* qkv, int32_t rows, int32_t heads, const float* qn_w,
 /* flash_attn_coop_128_32: dense bidirectional attention over `rows` rows and `heads` heads of 128. */
 int h3k_attention(const void* q, const void* k, const void* v, int64_t row_stride, int32_t heads, int32_t rows, void* out,
                   int64_t out_row_stride, void* stream);
+/* The same given a bound on every score, q.k / sqrt(128) * log2(e) <= score_bound (at most 60; see
+ * h3k_sparse_attention_bounded): the softmax takes it for the row maximum. 0 means unknown (as h3k_attention). It
+ * stands for the same reference kernel (flash_attn_coop_128_32). */
+int h3k_attention_bounded(const void* q, const void* k, const void* v, int64_t row_stride, int32_t heads, int32_t rows,
+                          float score_bound, void* out, int64_t out_row_stride, void* stream);
 
 /* The sparse attention's cube grid: dense_rows rows (text, keyframe, audio) then frames x ph x pw generated video
  * rows (a row is a 2x2 patch), cut into 4x4x4 cubes (cubes at the far edges cut short). The h3k_sparse_* calls take
@@ -284,6 +289,16 @@ int h3k_cube_topk(const float* scores, int32_t heads, const h3k_cube_grid* g, fl
 /* The whole sparse attention (selection, pass lists, flash_attn_sparse_128); scratch is allocated per call. */
 int h3k_sparse_attention(const void* q, const void* k, const void* v, int64_t row_stride, int32_t heads, const h3k_cube_grid* g,
                          float ratio, int32_t local, void* out, int64_t out_row_stride, void* stream);
+
+/* The same sparse attention given a bound on every score: q.k / sqrt(128) * log2(e) <= score_bound for all rows and
+ * heads (at most 60; q and k RMS-normed per head with weights of magnitude at most wq and wk give 16.3222 wq wk, as
+ * the step uses). The softmax then takes the bound for the row maximum: no running maximum, no exchange of it between
+ * a row's warps, no rescaling. 0 means unknown (as h3k_sparse_attention). A bound below the true maximum gives wrong
+ * results, not an error. Same scratch and synchronisation as h3k_sparse_attention; it stands for the same reference
+ * kernel (flash_attn_sparse_128). */
+int h3k_sparse_attention_bounded(const void* q, const void* k, const void* v, int64_t row_stride, int32_t heads,
+                                 const h3k_cube_grid* g, float ratio, int32_t local, float score_bound, void* out,
+                                 int64_t out_row_stride, void* stream);
 
 /* The same sparse attention without any device allocation (no counterpart in the reference, whose Metal runtime
  * owns its buffers). For callers that cannot call cudaMalloc around an attention call: a serving stack that has

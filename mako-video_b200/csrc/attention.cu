@@ -89,9 +89,10 @@ struct A2Smem {
     static constexpr int TOTAL = OFF_RED + (A2_SPLIT > 1 ? 2 * 3 * A2_SPLIT * 128 * 4 : 0) + 1024;
 };
 
-template <int SPLIT, int HD>
+template <int SPLIT, int HD, bool STATIC>
 __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid_constant__ Maps maps, const AttnParams p)
 {
+    static_assert(!STATIC || SPLIT == 1, "a known score bound needs no maximum shared between a row's warps");
     using SM = A2Smem<HD>;
     constexpr int TL = SM::TL, A2_OFF_Q = SM::OFF_Q, A2_OFF_K = SM::OFF_K, A2_OFF_V = SM::OFF_V, A2_OFF_BAR = SM::OFF_BAR,
                   A2_OFF_RED = SM::OFF_RED;
@@ -246,7 +247,8 @@ __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid
         const uint32_t tO = tmem + lane_base + 256 + t * HD + hc * OC;
         float* red = reinterpret_cast<float*>(smem + A2_OFF_RED) + t * (3 * SPLIT * 128); // [3 slots][SPLIT][128 rows]
         const float sl2 = p.scale * 1.4426950408889634f;
-        float m = -INFINITY, l = 0.f;
+        // STATIC: every score is at most p.static_max (log2 units), which then serves as the row maximum throughout
+        float m = STATIC ? p.static_max : -INFINITY, l = 0.f;
         bool ok = true;
         for (int j = 0; j < nkv; ++j) {
             if (!(ok = mbar_wait(&s_full[t], j & 1)))
@@ -274,16 +276,19 @@ __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid
             }
             // Row maximum over 8 independent chains of three-input maxima (a single chain would serialise the
             // latencies); the exponent arguments and the row sum as packed fp32 pairs.
-            float mp[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-                mp[i] = fmaxf(s[2 * i], s[2 * i + 1]);
-#pragma unroll
-            for (int c = 16; c < NC; c += 16)
+            float mx = -INFINITY;
+            if constexpr (!STATIC) {
+                float mp[8];
 #pragma unroll
                 for (int i = 0; i < 8; ++i)
-                    mp[i] = max3f(mp[i], s[c + 2 * i], s[c + 2 * i + 1]);
-            float mx = max3f(max3f(mp[0], mp[1], mp[2]), max3f(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7]));
+                    mp[i] = fmaxf(s[2 * i], s[2 * i + 1]);
+#pragma unroll
+                for (int c = 16; c < NC; c += 16)
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        mp[i] = max3f(mp[i], s[c + 2 * i], s[c + 2 * i + 1]);
+                mx = max3f(max3f(mp[0], mp[1], mp[2]), max3f(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7]));
+            }
             if constexpr (SPLIT > 1) {
                 // Every slice has loaded its scores once this exchange completes, so P may then overwrite them.
                 float* slot = red + (j & 1) * SPLIT * 128;
@@ -299,7 +304,7 @@ __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid
                         mx = fmaxf(mx, slot[o * 128 + row]);
             }
             const float m_cand = mx * sl2;
-            const bool need = m_cand > m + kRescaleThreshold;
+            const bool need = !STATIC && m_cand > m + kRescaleThreshold;
             const float m_use = need ? m_cand : m;
             const float alpha = need ? ex2_approx(m - m_use) : 1.f;
             const float msub = m_use == -INFINITY ? 0.f : m_use;
@@ -315,7 +320,7 @@ __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid
             }
             const float2 s01 = add2(add2(sp[0], sp[1]), add2(sp[2], sp[3]));
             const float rs = s01.x + s01.y;
-            if (j > 0 && __any_sync(0xffffffffu, need)) {
+            if (!STATIC && j > 0 && __any_sync(0xffffffffu, need)) {
                 // O_t holds PV_t(0..j-1), complete (S_t(j) was issued after PV_t(j-1)); each slice rescales its columns
 #pragma unroll 1
                 for (int c = 0; c < OC / 32; ++c) {
@@ -416,7 +421,8 @@ __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid
 //   warp 1      MMA: S(0), S(1) up front; then per step PV_a(j), PV_b(j) (A = P from TMEM) and S(j+2) into the S
 //               buffer step j leaves, so S(j+1) is ready when the softmax finishes step j
 //   warps 2..9  softmax: two warps per 32-lane quarter, each over one 64-key half of the step (hc = 0, 1), agreeing on
-//               the row maximum through shared memory; P (bf16) written back over S's first 64 columns
+//               the row maximum through shared memory (unless a bound on the scores stands in for it); each half's P
+//               (bf16) written back over the first 32 of its own 64 score columns
 // TMEM: S buffer 0 | S buffer 1 | O (128 columns each). S(j+2) overwrites P(j) only after PV(j) read it (one thread
 // issues both, and the tensor core runs them in order). The softmax of step j may rescale O only once PV(j-1) is
 // done (it waits for that only when a rescale is needed).
@@ -433,6 +439,11 @@ constexpr int A3_OFF_RED = A3_OFF_BAR + 256;
 constexpr int A3_SMEM = A3_OFF_RED + 3 * 2 * 128 * 4 + 1024;
 constexpr uint32_t LANE16 = 16u << 16; // TMEM address of lane 16: unit b's half of each subpartition
 
+// TMEM column (from an S buffer's first) of P's K = 16 slice kk: each 64-key half's P (bf16 pairs, 32 columns) is
+// written over the first half of that half's own scores, so neither slice overwrites scores the other has yet to load.
+__device__ __forceinline__ uint32_t p_col(int kk) { return uint32_t(kk * 8 + (kk >= 4 ? 32 : 0)); }
+
+template <bool STATIC>
 __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ Maps maps, const AttnParams p)
 {
     extern __shared__ uint8_t smem_raw[];
@@ -591,7 +602,7 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
                 const uint32_t vb = smem_u32(smem + A3_OFF_V + sv * TILE);
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk)
-                    mma_bf16_ts(tmem + T_O, tmem + (j & 1) * 128 + kk * 8, sdesc_sw128(vb + kk * 2048, HALF, 1024), id_pv128, (j | kk) != 0);
+                    mma_bf16_ts(tmem + T_O, tmem + (j & 1) * 128 + p_col(kk), sdesc_sw128(vb + kk * 2048, HALF, 1024), id_pv128, (j | kk) != 0);
                 mma_commit(&v_empty[sv]);
             }
             for (int x = 0; x < 2 && ok && !every; ++x) {
@@ -603,7 +614,7 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
                 const uint32_t lane = x ? LANE16 : 0u;
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk)
-                    mma_bf16_ts(tmem + T_O + lane, tmem + (j & 1) * 128 + lane + kk * 8, sdesc_sw128(vb + kk * 2048, HALF, 1024), id_pv,
+                    mma_bf16_ts(tmem + T_O + lane, tmem + (j & 1) * 128 + lane + p_col(kk), sdesc_sw128(vb + kk * 2048, HALF, 1024), id_pv,
                                 (j | kk) != 0);
                 mma_commit(&v_empty[sv]);
             }
@@ -628,7 +639,9 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
         const uint32_t tO = tmem + lane_base + T_O + hc * 64;
         float* red = reinterpret_cast<float*>(smem + A3_OFF_RED); // [3 slots][2 slices][128 rows]
         const float sl2 = p.scale * 1.4426950408889634f;
-        float m_run = -INFINITY, l = 0.f;
+        // STATIC: every score is at most p.static_max (log2 units), the row maximum throughout, so the two slices of a
+        // row exchange nothing per step and O is never rescaled
+        float m_run = STATIC ? p.static_max : -INFINITY, l = 0.f;
         bool ok = true;
         int4 e_next = entry(0, x);
         for (int j = 0; j < nkv; ++j) {
@@ -664,19 +677,21 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
                         if (c >= n)
                             s[c] = -INFINITY;
                 }
-                float mp[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i)
-                    mp[i] = fmaxf(s[2 * i], s[2 * i + 1]);
-#pragma unroll
-                for (int c = 16; c < 64; c += 16)
+                if constexpr (!STATIC) {
+                    float mp[8];
 #pragma unroll
                     for (int i = 0; i < 8; ++i)
-                        mp[i] = max3f(mp[i], s[c + 2 * i], s[c + 2 * i + 1]);
-                mx = max3f(max3f(mp[0], mp[1], mp[2]), max3f(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7]));
+                        mp[i] = fmaxf(s[2 * i], s[2 * i + 1]);
+#pragma unroll
+                    for (int c = 16; c < 64; c += 16)
+#pragma unroll
+                        for (int i = 0; i < 8; ++i)
+                            mp[i] = max3f(mp[i], s[c + 2 * i], s[c + 2 * i + 1]);
+                    mx = max3f(max3f(mp[0], mp[1], mp[2]), max3f(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7]));
+                }
             }
-            {
-                // Both slices have loaded their scores once this exchange completes, so P may then overwrite them.
+            if constexpr (!STATIC) {
+                // the row maximum over both slices
                 float* slot = red + (j & 1) * 256;
                 slot[hc * 128 + row] = mx;
                 __syncwarp();
@@ -687,7 +702,7 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
                 mx = fmaxf(mx, slot[(hc ^ 1) * 128 + row]);
             }
             const float m_cand = mx * sl2;
-            const bool need = m_cand > m_run + kRescaleThreshold;
+            const bool need = !STATIC && m_cand > m_run + kRescaleThreshold;
             const float m_use = need ? m_cand : m_run;
             const float alpha = need ? ex2_approx(m_run - m_use) : 1.f;
             const float msub = m_use == -INFINITY ? 0.f : m_use;
@@ -710,7 +725,7 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
                 for (int c = 0; c < 32; ++c)
                     pk[c] = 0u;
             }
-            if (j > 0 && __any_sync(0xffffffffu, need)) {
+            if (!STATIC && j > 0 && __any_sync(0xffffffffu, need)) {
                 // O holds PV(0..j-2) for sure; wait for PV(j-1) before scaling it
                 if (!(ok = mbar_wait(pv_done, (j - 1) & 1)))
                     break;
@@ -728,7 +743,7 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
             }
             l = l * alpha + rs;
             m_run = m_use;
-            tmem_st32(tS + hc * 32, pk);
+            tmem_st32(tS + hc * 64, pk);
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
@@ -741,7 +756,7 @@ __global__ void __launch_bounds__(NT3, 1) attn3_kernel(const __grid_constant__ M
             __syncwarp();
             if (elect_one_lane())
                 mbar_arrive(xchg);
-            ok = mbar_wait(xchg, nkv & 1);
+            ok = mbar_wait(xchg, STATIC ? 0 : nkv & 1);
             l = slot[row] + slot[128 + row];
         }
         // The last two PVs may both be pending here (S(j) completing implies only PV(j - 2) did), which a parity wait
@@ -840,28 +855,46 @@ int attention(const AttnParams& p, cudaStream_t s)
     maps.q = rows_map(p.q, p.heads, p.rows, p.row_stride, p.head_dim);
     maps.k = rows_map(p.k, p.heads, p.rows, p.row_stride, p.head_dim);
     maps.v = rows_map(p.v, p.heads, p.rows, p.row_stride, p.head_dim);
-    static std::atomic<uint64_t> opt_in[3];
+    static std::atomic<uint64_t> opt_in[6];
     if (sparse) {
         // Query tiles have their own key lists, so one tile per CTA with double-buffered scores.
-        smem_opt_in(attn3_kernel, A3_SMEM, opt_in[1]);
-        attn3_kernel<<<p.q_tiles * p.heads, NT3, A3_SMEM, s>>>(maps, p);
+        if (p.static_max > 0.f && p.static_max <= kMaxStaticBound) {
+            smem_opt_in(attn3_kernel<true>, A3_SMEM, opt_in[5]);
+            attn3_kernel<true><<<p.q_tiles * p.heads, NT3, A3_SMEM, s>>>(maps, p);
+        } else {
+            smem_opt_in(attn3_kernel<false>, A3_SMEM, opt_in[1]);
+            attn3_kernel<false><<<p.q_tiles * p.heads, NT3, A3_SMEM, s>>>(maps, p);
+        }
         H3_CUDA(cudaGetLastError());
         return 1;
     }
     // Dense: two query tiles per CTA share every K/V tile (half the shared-memory traffic per FLOP).
     const int segs = p.seg_rows > 0 ? p.rows / int(p.seg_stride) : 1;
     const int pairs = ((p.seg_rows > 0 ? p.seg_rows : p.rows) + 255) / 256;
+    const bool bounded = p.static_max > 0.f && p.static_max <= kMaxStaticBound;
     if (p.head_dim == 64) {
-        smem_opt_in(attn2_kernel<A2_SPLIT, 64>, A2Smem<64>::TOTAL, opt_in[2]);
-        attn2_kernel<A2_SPLIT, 64><<<dim3(pairs * segs, p.heads, 1), NT2, A2Smem<64>::TOTAL, s>>>(maps, p);
+        const dim3 grid(pairs * segs, p.heads, 1);
+        if (bounded) {
+            smem_opt_in(attn2_kernel<A2_SPLIT, 64, true>, A2Smem<64>::TOTAL, opt_in[4]);
+            attn2_kernel<A2_SPLIT, 64, true><<<grid, NT2, A2Smem<64>::TOTAL, s>>>(maps, p);
+        } else {
+            smem_opt_in(attn2_kernel<A2_SPLIT, 64, false>, A2Smem<64>::TOTAL, opt_in[2]);
+            attn2_kernel<A2_SPLIT, 64, false><<<grid, NT2, A2Smem<64>::TOTAL, s>>>(maps, p);
+        }
         H3_CUDA(cudaGetLastError());
         return 1;
     }
-    smem_opt_in(attn2_kernel<A2_SPLIT, 128>, A2Smem<128>::TOTAL, opt_in[0]);
     // A launch of few waves (several ranks leave each a few heads) loses much of its last wave; splitting every CTA's
     // keys in two, given scratch for the halves, doubles the CTAs, and a combine kernel merges them.
     const int parts = segs == 1 && p.part_o && p.part_ml && split_dense(p.rows, p.heads) ? 2 : 1;
-    attn2_kernel<A2_SPLIT, 128><<<dim3(pairs * segs, p.heads, parts), NT2, A2Smem<128>::TOTAL, s>>>(maps, p);
+    const dim3 grid(pairs * segs, p.heads, parts);
+    if (bounded) {
+        smem_opt_in(attn2_kernel<A2_SPLIT, 128, true>, A2Smem<128>::TOTAL, opt_in[3]);
+        attn2_kernel<A2_SPLIT, 128, true><<<grid, NT2, A2Smem<128>::TOTAL, s>>>(maps, p);
+    } else {
+        smem_opt_in(attn2_kernel<A2_SPLIT, 128, false>, A2Smem<128>::TOTAL, opt_in[0]);
+        attn2_kernel<A2_SPLIT, 128, false><<<grid, NT2, A2Smem<128>::TOTAL, s>>>(maps, p);
+    }
     H3_CUDA(cudaGetLastError());
     if (parts == 1)
         return 1;

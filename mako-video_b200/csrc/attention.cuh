@@ -95,7 +95,25 @@ struct AttnParams {
     int q_tiles = 0;
     int max_blocks = 0;
     CubeGrid grid;
+    // A bound on every score q.k scale log2(e) when one is known (q and k RMS-normed per head: qk_score_bound), at
+    // most kMaxStaticBound. The softmax then takes it for the row maximum: no running maximum, no exchange of it between
+    // a row's warps, no rescaling of O. 0: unknown (the online maximum).
+    float static_max = 0.f;
 };
+
+// The largest score bound (log2 units) the transposed sparse kernel takes: P = 2^(s - bound) stays a normal fp32 number
+// down to s = -bound.
+constexpr float kMaxStaticBound = 60.f;
+
+// The score bound of q and k RMS-normed per head of head_dim dims with weights of largest magnitudes wq and wk (1 for
+// an unweighted norm): |q| <= sqrt(head_dim) wq and |k| <= sqrt(head_dim) wk (the rotary embedding preserves norms),
+// so q.k / sqrt(head_dim) <= sqrt(head_dim) wq wk; times log2(e), with room for the bf16 rounding of q and k. 0 when
+// it is above kMaxStaticBound.
+inline float qk_score_bound(float wq, float wk, int head_dim = 128)
+{
+    const float b = (head_dim == 64 ? 11.5416f : 16.3222f) * wq * wk * 1.02f + 0.05f; // sqrt(head_dim) log2(e)
+    return b <= kMaxStaticBound ? b : 0.f;
+}
 
 // Launches the attention; returns the number of kernels launched.
 int attention(const AttnParams& p, cudaStream_t s);

@@ -667,6 +667,20 @@ int h3k_attention(const void* q, const void* k, const void* v, int64_t row_strid
     });
 }
 
+int h3k_attention_bounded(const void* q, const void* k, const void* v, int64_t row_stride, int32_t heads, int32_t rows,
+                          float score_bound, void* out, int64_t out_row_stride, void* stream)
+{
+    return guarded([&] {
+        if (!(score_bound >= 0.f && score_bound <= h3::kMaxStaticBound))
+            throw ArgError("h3k_attention_bounded: the score bound must be in [0, 60]");
+        device_ptrs("h3k_attention_bounded", {q, k, v, out});
+        h3::AttnParams p;
+        p.q = q, p.k = k, p.v = v, p.row_stride = row_stride, p.heads = heads, p.rows = rows, p.out = out;
+        p.out_row_stride = out_row_stride, p.static_max = score_bound;
+        h3::attention(p, st(stream));
+    });
+}
+
 int h3k_sparse_sizes(const h3k_cube_grid* g, float ratio, int32_t local, int32_t* cubes, int32_t* kcap, int32_t* q_tiles,
                      int32_t* max_blocks)
 {
@@ -737,14 +751,18 @@ int h3k_cube_topk(const float* scores, int32_t heads, const h3k_cube_grid* g, fl
     });
 }
 
-int h3k_sparse_attention(const void* q, const void* k, const void* v, int64_t row_stride, int32_t heads, const h3k_cube_grid* g, float ratio,
-                         int32_t local, void* out, int64_t out_row_stride, void* stream)
+namespace {
+int sparse_attention_call(const char* name, const void* q, const void* k, const void* v, int64_t row_stride, int32_t heads,
+                          const h3k_cube_grid* g, float ratio, int32_t local, float score_bound, void* out, int64_t out_row_stride,
+                          void* stream)
 {
     return guarded([&] {
         const h3::CubeGrid c = to_grid(g);
         if (!q || !k || !v || !out)
-            throw ArgError("h3k_sparse_attention: null argument");
-        device_ptrs("h3k_sparse_attention", {q, k, v, out});
+            throw ArgError(std::string(name) + ": null argument");
+        if (!(score_bound >= 0.f && score_bound <= h3::kMaxStaticBound))
+            throw ArgError(std::string(name) + ": the score bound must be in [0, 60]");
+        device_ptrs(name, {q, k, v, out});
         h3::SparseBuffers b;
         h3::sparse_sizes(c, ratio, local, b.kcap, b.q_tiles, b.max_blocks);
         Scratch sc;
@@ -760,9 +778,24 @@ int h3k_sparse_attention(const void* q, const void* k, const void* v, int64_t ro
         h3::AttnParams p;
         p.q = q, p.k = k, p.v = v, p.row_stride = row_stride, p.heads = heads, p.rows = c.dense_rows + c.frames * c.ph * c.pw;
         p.out = out, p.out_row_stride = out_row_stride;
+        p.static_max = score_bound;
         h3::sparse_attention(p, c, ratio, local, b, st(stream));
         H3_CUDA(cudaStreamSynchronize(st(stream)));
     });
+}
+} // namespace
+
+int h3k_sparse_attention(const void* q, const void* k, const void* v, int64_t row_stride, int32_t heads, const h3k_cube_grid* g, float ratio,
+                         int32_t local, void* out, int64_t out_row_stride, void* stream)
+{
+    return sparse_attention_call("h3k_sparse_attention", q, k, v, row_stride, heads, g, ratio, local, 0.f, out, out_row_stride, stream);
+}
+
+int h3k_sparse_attention_bounded(const void* q, const void* k, const void* v, int64_t row_stride, int32_t heads, const h3k_cube_grid* g,
+                                 float ratio, int32_t local, float score_bound, void* out, int64_t out_row_stride, void* stream)
+{
+    return sparse_attention_call("h3k_sparse_attention_bounded", q, k, v, row_stride, heads, g, ratio, local, score_bound, out,
+                                 out_row_stride, stream);
 }
 
 int h3k_fill_synthetic(void* dst, int32_t is_bf16, uint64_t n, uint64_t seed, uint32_t tensor_id, float mean, float stdev, void* stream)

@@ -214,6 +214,9 @@ struct Model::Impl {
     struct Block {
         DevBuf norm1, qkv_w, qkv_b, qn, kn, out_w, out_b, norm2, fc1_w, fc1_b, fc2_w, fc2_b;
         DevBuf qkv_q, qkv_s, out_q, out_s, fc1_q, fc1_s, fc2_q, fc2_s; // int8 rows and scales
+        // bound on the block's attention scores (log2 units) from its q/k norm weights, 0 when above the attention's
+        // limit for one (set at load; LoRA leaves the norm weights as they are)
+        float qk_bound = 0.f;
     };
     std::vector<Block> blocks;
     std::vector<Block> refiner; // token refiner blocks (bf16 only; no AdaLN)
@@ -665,6 +668,25 @@ void Model::init(WeightSource& src)
     H3_CUDA(cudaStreamSynchronize(s));
     if (take_device_error(s))
         throw CudaError("device error during weight set-up");
+    // Every block's score bound: q and k are RMS-normed per head with these weights, so |q.k| / sqrt(128) is at most
+    // sqrt(128) max|w_q| max|w_k|. H3_ATTN_ONLINE=1 keeps the online row maximum instead (for comparison).
+    const char* online = std::getenv("H3_ATTN_ONLINE");
+    const bool bounded = !(online && std::string(online) == "1");
+    std::vector<float> wq(128), wk(128);
+    std::vector<Impl::Block*> all;
+    for (auto& b : d_->blocks)
+        all.push_back(&b);
+    for (auto& b : d_->refiner)
+        all.push_back(&b);
+    for (Impl::Block* bp : all) {
+        Impl::Block& b = *bp;
+        H3_CUDA(cudaMemcpy(wq.data(), b.qn.p, 128 * sizeof(float), cudaMemcpyDeviceToHost));
+        H3_CUDA(cudaMemcpy(wk.data(), b.kn.p, 128 * sizeof(float), cudaMemcpyDeviceToHost));
+        float mq = 0.f, mk = 0.f;
+        for (int i = 0; i < 128; ++i)
+            mq = std::max(mq, std::fabs(wq[i])), mk = std::max(mk, std::fabs(wk[i]));
+        b.qk_bound = bounded && std::isfinite(mq) && std::isfinite(mk) ? qk_score_bound(mq, mk) : 0.f;
+    }
 }
 
 void Model::save(const std::string& path)
@@ -981,7 +1003,7 @@ void Model::refine_text(int T)
         const __nv_bfloat16* q = qkv.as<__nv_bfloat16>();
         AttnParams ap;
         ap.q = q, ap.k = q + H * 128, ap.v = q + 2 * H * 128, ap.row_stride = 3 * H * 128, ap.heads = H, ap.rows = T;
-        ap.out = o.p, ap.out_row_stride = inner;
+        ap.out = o.p, ap.out_row_stride = inner, ap.static_max = B.qk_bound;
         attention(ap, s);
         GemmParams go;
         go.M = T, go.N = d, go.K = inner;
@@ -1305,12 +1327,14 @@ void Model::step(const float* video, const float* audio, float t_video, float t_
             mark("select");
             ap.blocks = b.blocks, ap.nblocks = b.nblocks, ap.q_rows = b.q_rows, ap.q_tiles = b.q_tiles;
             ap.max_blocks = b.max_blocks, ap.grid = grid;
+            ap.static_max = B.qk_bound;
             launches_ += 4 + attention(ap, s);
         } else {
             if (d_->attn_split_bytes) {
                 ap.part_o = d_->attn_part.as<float>();
                 ap.part_ml = ap.part_o + size_t(2) * S_ * Hp * 128;
             }
+            ap.static_max = B.qk_bound;
             launches_ += attention(ap, s);
         }
         mark("attn");

@@ -196,6 +196,7 @@ void VideoDecoder::run_clip(const float* lat, int h, int w)
         const __nv_bfloat16* q = qkv_.as<__nv_bfloat16>();
         ap.q = q, ap.k = q + d, ap.v = q + 2 * d, ap.row_stride = 3 * d, ap.heads = H, ap.rows = M, ap.head_dim = VaeConfig::head_dim;
         ap.seg_rows = t.T, ap.seg_stride = t.T, ap.out = o_.p, ap.out_row_stride = d, ap.scale = 0.125f;
+        ap.static_max = qk_score_bound(1.f, 1.f, VaeConfig::head_dim); // q and k RMS-normed without weights
         launches_ += attention(ap, s);
         GemmParams go;
         go.M = M, go.N = d, go.K = d, go.x = x_.as<float>(), go.ldx = d, go.bias = B.out_b.as<float>(), go.mod = B.mods.as<float>();

@@ -140,11 +140,13 @@ SIGNATURES = {
     "h3k_quant_weight": (ctypes.c_int, [_P, _I32, _I32, _P, _P, _P]),
     "h3k_heads_partial": (ctypes.c_int, [_P, _I32, _I32, _P, _P, _P, _F, _P]),
     "h3k_attention": (ctypes.c_int, [_P, _P, _P, _I64, _I32, _I32, _P, _I64, _P]),
+    "h3k_attention_bounded": (ctypes.c_int, [_P, _P, _P, _I64, _I32, _I32, _F, _P, _I64, _P]),
     "h3k_sparse_sizes": (ctypes.c_int, [ctypes.POINTER(h3k_cube_grid), _F, _I32, _P, _P, _P, _P]),
     "h3k_sparse_select": (ctypes.c_int, [_P, _P, _I64, _I32, ctypes.POINTER(h3k_cube_grid), _F, _I32, _P, _P, _P, _P, _P, _P]),
     "h3k_cube_topk": (ctypes.c_int, [_P, _I32, ctypes.POINTER(h3k_cube_grid), _F, _I32, _P, _P, _P]),
     "h3k_video_order": (ctypes.c_int, [ctypes.POINTER(h3k_cube_grid), _P]),
     "h3k_sparse_attention": (ctypes.c_int, [_P, _P, _P, _I64, _I32, ctypes.POINTER(h3k_cube_grid), _F, _I32, _P, _I64, _P]),
+    "h3k_sparse_attention_bounded": (ctypes.c_int, [_P, _P, _P, _I64, _I32, ctypes.POINTER(h3k_cube_grid), _F, _I32, _F, _P, _I64, _P]),
     "h3k_sparse_attention_noalloc": (ctypes.c_int, [_P, _P, _P, _I64, _I32, ctypes.POINTER(h3k_cube_grid), _F, _I32, _P, _I64, _P]),
     "h3k_fill_synthetic": (ctypes.c_int, [_P, _I32, _U64, _U64, _U32, _F, _F, _P]),
     "h3k_gemv_f32": (ctypes.c_int, [_P, _P, _P, _I32, _I32, _I32, _I32, _P, _P, _P]),

@@ -269,14 +269,39 @@ def test_heads_partial_standalone_matches_fused(cuda):
 
 # ------------------------------------------------------------------------------------------------- attention
 
+def rms_normed_qk(qkv):
+    """q and k RMS-normed per head (unit weights), as the step's q/k/v epilogue leaves them; v as it is."""
+    x = qkv.float()
+    x[:, :2] = x[:, :2] * torch.rsqrt(x[:, :2].pow(2).mean(-1, keepdim=True) + 1e-6)
+    return x.bfloat16()
+
+
+def score_bound(qkv):
+    """max |q.k| / sqrt(128) * log2(e) over every row pair and head, from the norms (Cauchy-Schwarz), with room."""
+    qn = qkv[:, 0].float().norm(dim=-1).max().item()
+    kn = qkv[:, 1].float().norm(dim=-1).max().item()
+    return qn * kn / 128 ** 0.5 * 1.4426950408889634 * 1.01 + 0.01
+
+
 @pytest.mark.parametrize("S,Hh", [(128, 1), (300, 2), (1111, 3), (4096, 2)])
-def test_attention_dense(cuda, S, Hh):
+@pytest.mark.parametrize("bounded", [False, True])
+def test_attention_dense(cuda, S, Hh, bounded):
+    """Against fp32 softmax; bounded: q and k RMS-normed per head (as the step makes them) and their score bound
+    given, so the softmax takes the bound for the row maximum."""
     g = torch.Generator().manual_seed(S)
     qkv = torch.randn(S, 3, Hh, 128, generator=g).bfloat16()
     qkv[:, :2] *= 1.5
+    if bounded:
+        qkv = rms_normed_qk(qkv)
     t = qkv.to(cuda)
     out = torch.zeros(S, Hh, 128, device=cuda, dtype=torch.bfloat16)
-    H.check(H.lib().h3k_attention(ptr(t[:, 0]), ptr(t[:, 1]), ptr(t[:, 2]), 3 * Hh * 128, Hh, S, ptr(out), Hh * 128, stream()))
+    if bounded:
+        bound = score_bound(qkv)
+        assert bound < 20
+        H.check(H.lib().h3k_attention_bounded(ptr(t[:, 0]), ptr(t[:, 1]), ptr(t[:, 2]), 3 * Hh * 128, Hh, S, bound, ptr(out), Hh * 128,
+                                              stream()))
+    else:
+        H.check(H.lib().h3k_attention(ptr(t[:, 0]), ptr(t[:, 1]), ptr(t[:, 2]), 3 * Hh * 128, Hh, S, ptr(out), Hh * 128, stream()))
     sync()
     want = O.attention(qkv[:, 0].float(), qkv[:, 1].float(), qkv[:, 2].float())
     r = rel(out.float(), want)
@@ -378,6 +403,55 @@ def test_sparse_attention(cuda, ratio, local):
         H.check(H.lib().h3k_attention(ptr(t[:, 0]), ptr(t[:, 1]), ptr(t[:, 2]), 3 * Hh * 128, Hh, S, ptr(dense), Hh * 128, stream()))
         sync()
         assert rel(out_packed.float(), dense.float()) < 1e-2  # every cube selected = dense (tests/CMakeLists.txt:9-12)
+
+
+@pytest.mark.parametrize("ratio,local", [(0.1, 1), (0.4, 3), (1.0, 0)])
+def test_sparse_attention_bounded(cuda, ratio, local):
+    """The sparse kernel given the score bound (no running maximum, no per-step exchange between a row's warps)
+    against the masked fp32 oracle and against the online-maximum kernel on the same selection; ratio 1 against
+    dense attention."""
+    qkv, grid = sparse_case(cuda, seed=2)
+    qkv = rms_normed_qk(qkv)
+    S, _, Hh, _ = qkv.shape
+    bound = score_bound(qkv)
+    assert 10 < bound < 20
+    order, inverse = packed(grid)
+    t = qkv[order].contiguous().to(cuda)
+    L = H.lib()
+    outs = []
+    for fn, extra in ((L.h3k_sparse_attention_bounded, [bound]), (L.h3k_sparse_attention, [])):
+        o = torch.zeros(S, Hh, 128, device=cuda, dtype=torch.bfloat16)
+        H.check(fn(ptr(t[:, 0]), ptr(t[:, 1]), ptr(t[:, 2]), 3 * Hh * 128, Hh, ctypes.byref(grid), ratio, local, *extra, ptr(o), Hh * 128,
+                   stream()))
+        outs.append(o)
+    sync()
+    out = outs[0].cpu()[inverse]
+    bits = qkv.contiguous().view(torch.int16).numpy().view(np.uint16).reshape(-1)
+    mq, mk = exact.cube_pool(bits, bits[Hh * 128:], 3 * Hh * 128, Hh, grid.dense_rows, grid.frames, grid.ph, grid.pw)
+    sel, nsel = exact.cube_topk(exact.cube_scores(mq, mk), grid.frames, grid.ph, grid.pw, ratio, local)
+    allowed = allowed_mask(S, grid.dense_rows, grid.frames, grid.ph, grid.pw, sel, nsel)
+    want = O.attention(qkv[:, 0].float(), qkv[:, 1].float(), qkv[:, 2].float(), allowed)
+    assert rel(out.float(), want) < 1e-2
+    a, b = out.double().reshape(-1, 128), want.double().reshape(-1, 128)
+    assert float(((a * b).sum(-1) / (a.norm(dim=-1) * b.norm(dim=-1)).clamp_min(1e-30)).min()) > 0.999
+    assert rel(outs[0].float(), outs[1].float()) < 1e-2
+    if ratio == 1.0:
+        dense = torch.zeros_like(outs[0])
+        H.check(L.h3k_attention(ptr(t[:, 0]), ptr(t[:, 1]), ptr(t[:, 2]), 3 * Hh * 128, Hh, S, ptr(dense), Hh * 128, stream()))
+        sync()
+        assert rel(outs[0].float(), dense.float()) < 1e-2
+
+
+def test_sparse_attention_bounded_refuses_a_bound_past_its_limit(cuda):
+    qkv, grid = sparse_case(cuda)
+    S, _, Hh, _ = qkv.shape
+    t = qkv.to(cuda)
+    o = torch.zeros(S, Hh, 128, device=cuda, dtype=torch.bfloat16)
+    for bad in (61.0, -1.0, float("nan")):
+        rc = H.lib().h3k_sparse_attention_bounded(ptr(t[:, 0]), ptr(t[:, 1]), ptr(t[:, 2]), 3 * Hh * 128, Hh, ctypes.byref(grid), 0.1, 1,
+                                                  bad, ptr(o), Hh * 128, stream())
+        assert rc == H.H3_ERR_ARG
+        assert "bound" in H.lib().h3_last_error().decode()
 
 
 # ---------------------------------------------------------------------------------- time embedding and AdaLN

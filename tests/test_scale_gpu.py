@@ -338,10 +338,12 @@ def test_dense_attention_at_768p_rows(cuda):
         assert cos_min(got[:, h], want, 128) > 0.999
 
 
-def test_sparse_attention_at_768p_grid(cuda):
-    """attn3 on config 3's grid (33024 rows, 528 cubes, k = 53, local 1), 2 heads: sampled query cubes (full ones,
-    the short last column, the first and last cube) against fp32 softmax over the cube's own selection (the
-    oracle's indices) plus every dense row; sampled dense rows against softmax over every row."""
+@pytest.mark.parametrize("bounded", [False, True])
+def test_sparse_attention_at_768p_grid(cuda, bounded):
+    """The sparse kernels on config 3's grid (33024 rows, 528 cubes, k = 53, local 1), 2 heads: sampled query cubes
+    (full ones, the short last column, the first and last cube) against fp32 softmax over the cube's own selection
+    (the oracle's indices) plus every dense row; sampled dense rows against softmax over every row. bounded: q and k
+    RMS-normed per head as the step makes them, with their score bound given."""
     G = GRIDS["c3"]
     grid = H.h3k_cube_grid(G["dense"], G["frames"], G["ph"], G["pw"])
     Hh, ratio, local = 2, G["ratio"], G["local"]
@@ -352,13 +354,23 @@ def test_sparse_attention_at_768p_grid(cuda):
     base = torch.randn(S - D, Hh, 128, generator=g)
     qkv[D:, 0] += 2 * base
     qkv[D:, 1] += 2 * base.roll(7 * grid.pw, 0)
+    if bounded:
+        qkv[:, :2] = qkv[:, :2] * torch.rsqrt(qkv[:, :2].pow(2).mean(-1, keepdim=True) + 1e-6)
     qkv = qkv.bfloat16()
     order = torch.from_numpy(H.packed_order(D, grid.frames, grid.ph, grid.pw))
     inverse = torch.argsort(order)
     t = qkv[order].contiguous().to(cuda)
     out_packed = torch.zeros(S, Hh, 128, device=cuda, dtype=torch.bfloat16)
-    H.check(H.lib().h3k_sparse_attention(ptr(t[:, 0]), ptr(t[:, 1]), ptr(t[:, 2]), 3 * Hh * 128, Hh, ctypes.byref(grid), ratio, local,
-                                         ptr(out_packed), Hh * 128, stream()))
+    L = H.lib()
+    if bounded:
+        qn, kn = (qkv[:, i].float().norm(dim=-1).max().item() for i in (0, 1))
+        bound = qn * kn / 128 ** 0.5 * 1.4426950408889634 * 1.01 + 0.01
+        assert bound < 20
+        H.check(L.h3k_sparse_attention_bounded(ptr(t[:, 0]), ptr(t[:, 1]), ptr(t[:, 2]), 3 * Hh * 128, Hh, ctypes.byref(grid), ratio,
+                                               local, bound, ptr(out_packed), Hh * 128, stream()))
+    else:
+        H.check(L.h3k_sparse_attention(ptr(t[:, 0]), ptr(t[:, 1]), ptr(t[:, 2]), 3 * Hh * 128, Hh, ctypes.byref(grid), ratio, local,
+                                       ptr(out_packed), Hh * 128, stream()))
     sync()
     out = out_packed.cpu()[inverse].float()
     bits = qkv.contiguous().view(torch.int16).numpy().view(np.uint16).reshape(-1)
