@@ -75,25 +75,28 @@ __device__ __forceinline__ int4 every_row_block(int j, int rows)
 // tensor core executes one thread's MMAs in issue order, so S_t(j+1) overwrites P_t(j) only after PV_t(j) read it;
 // and s_full_t(j) tracks every earlier MMA, so once S_t(j) is complete, PV_t(j-1) is too and the softmax may write
 // P_t(j) and rescale O_t.
-constexpr int A2_SPLIT = 1;        // warps sharing a query row in the softmax (2 measured no faster)
-constexpr int NT2 = 64 + 256 * A2_SPLIT;
+// Warps sharing a query row in the softmax: with the online maximum one (two measured no faster: they must agree on the
+// row maximum every step); with a known score bound two, each over its 64-key half, exchanging only the row sums at
+// the end.
+constexpr int A2_SPLIT = 1, A2_SPLIT_BOUNDED = 2;
 constexpr int A2_KST = 3, A2_VST = 2; // K is freed once both S MMAs read it, V after both PV MMAs
-template <int HD>
+template <int HD, int SPLIT, bool STATIC>
 struct A2Smem {
     static constexpr int TL = 128 * HD * 2; // a 128-row tile of one head
     static constexpr int OFF_Q = 0;         // Q0, Q1
     static constexpr int OFF_K = 2 * TL;
     static constexpr int OFF_V = OFF_K + A2_KST * TL;
     static constexpr int OFF_BAR = OFF_V + A2_VST * TL;
-    static constexpr int OFF_RED = OFF_BAR + 256; // row maxima and sums exchanged between a row's warps
-    static constexpr int TOTAL = OFF_RED + (A2_SPLIT > 1 ? 2 * 3 * A2_SPLIT * 128 * 4 : 0) + 1024;
+    // row maxima and sums exchanged between a row's warps (with a score bound only the sums, through the tile's Q
+    // buffer once its last score MMA is done)
+    static constexpr int OFF_RED = OFF_BAR + 256;
+    static constexpr int TOTAL = OFF_RED + (SPLIT > 1 && !STATIC ? 2 * 3 * SPLIT * 128 * 4 : 0) + 1024;
 };
 
 template <int SPLIT, int HD, bool STATIC>
 __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid_constant__ Maps maps, const AttnParams p)
 {
-    static_assert(!STATIC || SPLIT == 1, "a known score bound needs no maximum shared between a row's warps");
-    using SM = A2Smem<HD>;
+    using SM = A2Smem<HD, SPLIT, STATIC>;
     constexpr int TL = SM::TL, A2_OFF_Q = SM::OFF_Q, A2_OFF_K = SM::OFF_K, A2_OFF_V = SM::OFF_V, A2_OFF_BAR = SM::OFF_BAR,
                   A2_OFF_RED = SM::OFF_RED;
     extern __shared__ uint8_t smem_raw[];
@@ -182,6 +185,9 @@ __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid
         // ------------------------------------------------------------------------------------------ MMA
         const uint32_t id_s = idesc_bf16(128, 128);
         const uint32_t id_pv = idesc_bf16(128, HD, false, true);
+        // TMEM column of P's K = 16 slice kk: with a score bound each 64-key slice's P (32 columns) lies over the first
+        // half of that slice's own scores, else P fills the first 64 columns
+        auto p_col2 = [](int kk) { return uint32_t(kk * 8 + (STATIC && SPLIT > 1 && kk >= 4 ? 32 : 0)); };
         auto issue_s = [&](int t, int j) {
             const int ks = j % A2_KST;
             const uint32_t sq = smem_u32(smem + A2_OFF_Q + t * TL);
@@ -200,7 +206,8 @@ __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid
             const uint32_t sv = smem_u32(smem + A2_OFF_V + vs * TL);
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk)
-                mma_bf16_ts(tmem + 256 + t * HD, tmem + t * 128 + kk * 8, sdesc_sw128(sv + kk * 2048, HALF, 1024), id_pv, (j | kk) != 0);
+                mma_bf16_ts(tmem + 256 + t * HD, tmem + t * 128 + p_col2(kk), sdesc_sw128(sv + kk * 2048, HALF, 1024), id_pv,
+                            (j | kk) != 0);
             mma_commit(&pv_done[t]);
             if (t == 1)
                 mma_commit(&v_empty[vs]); // both tiles' PV MMAs have read V_j
@@ -289,7 +296,7 @@ __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid
                         mp[i] = max3f(mp[i], s[c + 2 * i], s[c + 2 * i + 1]);
                 mx = max3f(max3f(mp[0], mp[1], mp[2]), max3f(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7]));
             }
-            if constexpr (SPLIT > 1) {
+            if constexpr (SPLIT > 1 && !STATIC) {
                 // Every slice has loaded its scores once this exchange completes, so P may then overwrite them.
                 float* slot = red + (j & 1) * SPLIT * 128;
                 slot[hc * 128 + row] = mx;
@@ -337,7 +344,7 @@ __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid
             m = m_use;
 #pragma unroll
             for (int c = 0; c < NC / 64; ++c)
-                tmem_st32(tS + hc * (NC / 2) + c * 32, *reinterpret_cast<uint32_t(*)[32]>(pk + c * 32));
+                tmem_st32(tS + (STATIC ? hc * NC : hc * (NC / 2)) + c * 32, *reinterpret_cast<uint32_t(*)[32]>(pk + c * 32));
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
@@ -346,12 +353,13 @@ __global__ void __launch_bounds__(64 + 256 * SPLIT, 1) attn2_kernel(const __grid
         }
         if constexpr (SPLIT > 1) {
             if (ok) {
-                float* slot = red + 2 * SPLIT * 128;
+                // S_t(nkv - 1) is done, so no MMA reads Q_t any more
+                float* slot = STATIC ? reinterpret_cast<float*>(smem + A2_OFF_Q + t * TL) : red + 2 * SPLIT * 128;
                 slot[hc * 128 + row] = l;
                 __syncwarp();
                 if (elect_one_lane())
                     mbar_arrive(&xchg[t]);
-                ok = mbar_wait(&xchg[t], nkv & 1);
+                ok = mbar_wait(&xchg[t], STATIC ? 0 : nkv & 1);
                 l = 0.f;
 #pragma unroll
                 for (int o = 0; o < SPLIT; ++o)
@@ -872,14 +880,17 @@ int attention(const AttnParams& p, cudaStream_t s)
     const int segs = p.seg_rows > 0 ? p.rows / int(p.seg_stride) : 1;
     const int pairs = ((p.seg_rows > 0 ? p.seg_rows : p.rows) + 255) / 256;
     const bool bounded = p.static_max > 0.f && p.static_max <= kMaxStaticBound;
+    constexpr int SB = A2_SPLIT_BOUNDED, NTB = 64 + 256 * SB, NTO = 64 + 256 * A2_SPLIT;
     if (p.head_dim == 64) {
         const dim3 grid(pairs * segs, p.heads, 1);
         if (bounded) {
-            smem_opt_in(attn2_kernel<A2_SPLIT, 64, true>, A2Smem<64>::TOTAL, opt_in[4]);
-            attn2_kernel<A2_SPLIT, 64, true><<<grid, NT2, A2Smem<64>::TOTAL, s>>>(maps, p);
+            using SM = A2Smem<64, SB, true>;
+            smem_opt_in(attn2_kernel<SB, 64, true>, SM::TOTAL, opt_in[4]);
+            attn2_kernel<SB, 64, true><<<grid, NTB, SM::TOTAL, s>>>(maps, p);
         } else {
-            smem_opt_in(attn2_kernel<A2_SPLIT, 64, false>, A2Smem<64>::TOTAL, opt_in[2]);
-            attn2_kernel<A2_SPLIT, 64, false><<<grid, NT2, A2Smem<64>::TOTAL, s>>>(maps, p);
+            using SM = A2Smem<64, A2_SPLIT, false>;
+            smem_opt_in(attn2_kernel<A2_SPLIT, 64, false>, SM::TOTAL, opt_in[2]);
+            attn2_kernel<A2_SPLIT, 64, false><<<grid, NTO, SM::TOTAL, s>>>(maps, p);
         }
         H3_CUDA(cudaGetLastError());
         return 1;
@@ -889,11 +900,13 @@ int attention(const AttnParams& p, cudaStream_t s)
     const int parts = segs == 1 && p.part_o && p.part_ml && split_dense(p.rows, p.heads) ? 2 : 1;
     const dim3 grid(pairs * segs, p.heads, parts);
     if (bounded) {
-        smem_opt_in(attn2_kernel<A2_SPLIT, 128, true>, A2Smem<128>::TOTAL, opt_in[3]);
-        attn2_kernel<A2_SPLIT, 128, true><<<grid, NT2, A2Smem<128>::TOTAL, s>>>(maps, p);
+        using SM = A2Smem<128, SB, true>;
+        smem_opt_in(attn2_kernel<SB, 128, true>, SM::TOTAL, opt_in[3]);
+        attn2_kernel<SB, 128, true><<<grid, NTB, SM::TOTAL, s>>>(maps, p);
     } else {
-        smem_opt_in(attn2_kernel<A2_SPLIT, 128, false>, A2Smem<128>::TOTAL, opt_in[0]);
-        attn2_kernel<A2_SPLIT, 128, false><<<grid, NT2, A2Smem<128>::TOTAL, s>>>(maps, p);
+        using SM = A2Smem<128, A2_SPLIT, false>;
+        smem_opt_in(attn2_kernel<A2_SPLIT, 128, false>, SM::TOTAL, opt_in[0]);
+        attn2_kernel<A2_SPLIT, 128, false><<<grid, NTO, SM::TOTAL, s>>>(maps, p);
     }
     H3_CUDA(cudaGetLastError());
     if (parts == 1)
