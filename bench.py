@@ -302,13 +302,17 @@ class Runner:
         ms = e0.elapsed_time(e1) / steps
         launches = self.model.last_launches()
         # end to end, interleaved with device-resident steps so that both see the same clocks: each pair is one
-        # h3_step (pinned host buffers in and out, wall clock) and one step_device (CUDA events)
+        # h3_step (pinned host buffers in and out, wall clock) and one step_device (CUDA events), in alternating order
+        # so that neither always follows the other (under the power cap the clock drifts between consecutive steps)
         e2e, dev = [], []
-        for _ in range(pairs):
+
+        def host_step():
             self.barrier()
             t0 = time.perf_counter()
             self.step_host()
             e2e.append(time.perf_counter() - t0)
+
+        def device_step():
             self.barrier()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             with torch.cuda.stream(self.ext):
@@ -317,6 +321,10 @@ class Runner:
                 b.record()
             self.model.synchronize()
             dev.append(a.elapsed_time(b) * 1e-3)
+
+        for i in range(pairs):
+            for f in ((host_step, device_step) if i % 2 == 0 else (device_step, host_step)):
+                f()
         if not np.isfinite(self.hv).all():
             raise RuntimeError("non-finite velocities")
         # per-kernel-class device times (events after each class in every block) through h3_step: the copies too
@@ -325,7 +333,10 @@ class Runner:
         classes = self.model.timing_by_class()
         self.model.set_timing(False)
         ms, e2e_s, dev_s = self.maxed([ms, statistics.mean(e2e), statistics.mean(dev)])
+        diffs = [(a - b) * 1e3 for a, b in zip(e2e, dev)]
         return {"ms": ms, "e2e_s": e2e_s, "paired_dev_s": dev_s, "launches": launches, "classes": classes,
+                "pair_diff_ms": {"mean": statistics.mean(diffs), "stdev": statistics.stdev(diffs) if len(diffs) > 1 else None,
+                                 "pairs": len(diffs)},
                 "clocks": clk.summary() if clk else None}
 
 
@@ -362,9 +373,12 @@ def _line_part(m, cfg, layout, ratio, world, peaks, args_workload_key, int8):
         "value": m["ms"] / 1e3, "unit": "s", "ms_per_step": m["ms"],
         "e2e": {"value": m["e2e_s"], "unit": "s", "h2d_bytes_per_step": int(vb + ab), "d2h_bytes_per_step": int(vb + ab),
                 "paired_device_s": m["paired_dev_s"], "h2d_ms": h2d_ms, "d2h_ms": d2h_ms,
+                "e2e_minus_device_ms": m.get("pair_diff_ms"),
                 "note": "each timed h3_step (pinned host buffers, wall clock) is paired with a device-resident step "
-                        "(CUDA events) so both see the same clocks; h2d_ms / d2h_ms are the copy stages' CUDA-event times "
-                        "inside h3_step (d2h includes the gather of the video rows back to the layout's order)"},
+                        "(CUDA events), in alternating order, so both see the same clocks; h2d_ms / d2h_ms are the copy "
+                        "stages' CUDA-event times inside h3_step (d2h includes the gather of the video rows back to the "
+                        "layout's order); e2e_minus_device_ms is the per-pair difference, whose spread (the step's clock "
+                        "drift under the power cap) exceeds the copies' ~0.6 ms"},
         "roofline": {"bound": "tensor", "kernel": "attention (attn3_kernel, tcgen05)" if ratio else "attention (attn2_kernel, tcgen05)",
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": (achieved / peak) if achieved else None,
                      "traffic": load_traffic("attention", args_workload_key) if world == 1 else None,
@@ -525,7 +539,7 @@ def run_ours(args, rank, world, local_rank):
         model.close()
         return
     peaks, _ = load_peaks()
-    m = run.measure(args.steps, args.warmup, min(args.steps, 10), clocks_gpu=local_rank)
+    m = run.measure(args.steps, args.warmup, max(4, min(args.steps, 10)), clocks_gpu=local_rank)
     head = _line_part(m, cfg, layout, ratio, world, peaks, args.workload, int8)
     line = {
         "metric": METRIC, "value": head["value"], "unit": "s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
