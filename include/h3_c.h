@@ -258,7 +258,7 @@ int h3k_heads_partial(void* qkv, int32_t rows, int32_t heads, const float* qn_w,
 /* flash_attn_coop_128_32: dense bidirectional attention over `rows` rows and `heads` heads of 128. */
 int h3k_attention(const void* q, const void* k, const void* v, int64_t row_stride, int32_t heads, int32_t rows, void* out,
                   int64_t out_row_stride, void* stream);
-/* The same given a bound on every score, q.k / sqrt(128) * log2(e) <= score_bound (at most 60; see
+/* The same given a bound on every score, q.k / sqrt(128) * log2(e) <= score_bound (at most 40; see
  * h3k_sparse_attention_bounded): the softmax takes it for the row maximum. 0 means unknown (as h3k_attention). It
  * stands for the same reference kernel (flash_attn_coop_128_32). */
 int h3k_attention_bounded(const void* q, const void* k, const void* v, int64_t row_stride, int32_t heads, int32_t rows,
@@ -291,7 +291,7 @@ int h3k_sparse_attention(const void* q, const void* k, const void* v, int64_t ro
                          float ratio, int32_t local, void* out, int64_t out_row_stride, void* stream);
 
 /* The same sparse attention given a bound on every score: q.k / sqrt(128) * log2(e) <= score_bound for all rows and
- * heads (at most 60; q and k RMS-normed per head with weights of magnitude at most wq and wk give 16.3222 wq wk, as
+ * heads (at most 40; q and k RMS-normed per head with weights of magnitude at most wq and wk give 16.3222 wq wk, as
  * the step uses). The softmax then takes the bound for the row maximum: no running maximum, no exchange of it between
  * a row's warps, no rescaling. 0 means unknown (as h3k_sparse_attention). A bound below the true maximum gives wrong
  * results, not an error. Same scratch and synchronisation as h3k_sparse_attention; it stands for the same reference

@@ -101,9 +101,10 @@ struct AttnParams {
     float static_max = 0.f;
 };
 
-// The largest score bound (log2 units) the transposed sparse kernel takes: P = 2^(s - bound) stays a normal fp32 number
-// down to s = -bound.
-constexpr float kMaxStaticBound = 60.f;
+// The largest score bound (log2 units) the attention takes in place of the row maximum. A row's largest P is
+// 2^(s_max - bound) >= 2^(-2 bound) = 2^-80, so a key is flushed to zero (P below 2^-125) only when its score is more
+// than 45 below the row's largest, where its weight is below 2^-45 of that one.
+constexpr float kMaxStaticBound = 40.f;
 
 // The score bound of q and k RMS-normed per head of head_dim dims with weights of largest magnitudes wq and wk (1 for
 // an unweighted norm): |q| <= sqrt(head_dim) wq and |k| <= sqrt(head_dim) wk (the rotary embedding preserves norms),

@@ -672,7 +672,7 @@ int h3k_attention_bounded(const void* q, const void* k, const void* v, int64_t r
 {
     return guarded([&] {
         if (!(score_bound >= 0.f && score_bound <= h3::kMaxStaticBound))
-            throw ArgError("h3k_attention_bounded: the score bound must be in [0, 60]");
+            throw ArgError("h3k_attention_bounded: the score bound must be in [0, 40]");
         device_ptrs("h3k_attention_bounded", {q, k, v, out});
         h3::AttnParams p;
         p.q = q, p.k = k, p.v = v, p.row_stride = row_stride, p.heads = heads, p.rows = rows, p.out = out;
@@ -761,7 +761,7 @@ int sparse_attention_call(const char* name, const void* q, const void* k, const 
         if (!q || !k || !v || !out)
             throw ArgError(std::string(name) + ": null argument");
         if (!(score_bound >= 0.f && score_bound <= h3::kMaxStaticBound))
-            throw ArgError(std::string(name) + ": the score bound must be in [0, 60]");
+            throw ArgError(std::string(name) + ": the score bound must be in [0, 40]");
         device_ptrs(name, {q, k, v, out});
         h3::SparseBuffers b;
         h3::sparse_sizes(c, ratio, local, b.kcap, b.q_tiles, b.max_blocks);
