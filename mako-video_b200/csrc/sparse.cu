@@ -95,46 +95,27 @@ __device__ __forceinline__ uint32_t orderable(float f)
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-constexpr int TK_NT = 256;
+// Top-k cube selection, one warp per (query cube, head) row: the row's keys (scores made order-preserving as unsigned
+// integers) in shared memory, then a radix select of 8 bits a pass over the keys that are not forced, the histogram
+// built by lanes that agree on a digit adding once. The threshold key T is the remaining-th largest; selected are the
+// forced cubes (the query cube itself, with local >= 3 also the same position one frame group before and after), every
+// key above T, and the keys equal to T among the first `remaining` such by index; written in ascending index order,
+// at most kcap of them. No CTA barrier: the warps of a CTA work on different rows.
+constexpr int TK_ROWS = 8; // warps (rows) a CTA
 
-// Block-wide exclusive prefix sum of one value per thread; returns the thread's offset, `total` gets the sum.
-__device__ __forceinline__ int block_exscan(int v, int* buf, int& total)
+__global__ void __launch_bounds__(TK_ROWS * 32) cube_topk_kernel(const float* scores, CubeGrid g, int k, int local, int32_t* sel,
+                                                               int32_t* nsel, int kcap, int rows_per_cta)
 {
-    // warp inclusive scans by shuffles, then the warps' totals (buf[0..7]) scanned by every thread
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    int x = v;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const int t = __shfl_up_sync(0xffffffffu, x, o);
-        if (lane >= o)
-            x += t;
-    }
-    if (lane == 31)
-        buf[wid] = x;
-    __syncthreads();
-    int before = 0, all = 0;
-#pragma unroll
-    for (int w = 0; w < TK_NT / 32; ++w) {
-        const int t = buf[w];
-        before += w < wid ? t : 0;
-        all += t;
-    }
-    total = all;
-    __syncthreads(); // buf is reused by the next call
-    return before + x - v;
-}
-
-__global__ void __launch_bounds__(TK_NT) cube_topk_kernel(const float* scores, CubeGrid g, int k, int local, int32_t* sel, int32_t* nsel,
-                                                           int kcap)
-{
-    extern __shared__ uint32_t keys[]; // [cubes]
-    __shared__ int hist[256];
-    __shared__ int scan[TK_NT];
-    __shared__ int sh_digit, sh_acc;
+    extern __shared__ uint32_t tk_smem[]; // per warp: keys [n], then the histogram [256]
     const int n = g.cubes();
-    const int i = blockIdx.x, h = blockIdx.y;
-    const int cx = i % g.ncx, cy = (i / g.ncx) % g.ncy, ct = i / (g.ncx * g.ncy);
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int i = blockIdx.x * rows_per_cta + w, h = blockIdx.y;
+    if (w >= rows_per_cta || i >= n)
+        return;
+    uint32_t* keys = tk_smem + size_t(w) * (n + 256);
+    int* hist = reinterpret_cast<int*>(keys + n);
     const int per_plane = g.ncx * g.ncy;
+    const int ct = i / per_plane; // the query cube's frame group
     auto forced = [&](int j) {
         if (local <= 0)
             return false;
@@ -142,80 +123,80 @@ __global__ void __launch_bounds__(TK_NT) cube_topk_kernel(const float* scores, C
             return true;
         return local >= 3 && ((ct > 0 && j == i - per_plane) || (ct + 1 < g.nct && j == i + per_plane));
     };
-    int n_forced = local <= 0 ? 0 : 1 + (local >= 3 ? int(ct > 0) + int(ct + 1 < g.nct) : 0);
+    const int n_forced = local <= 0 ? 0 : 1 + (local >= 3 ? int(ct > 0) + int(ct + 1 < g.nct) : 0);
     const float* row = scores + (size_t(h) * n + i) * n;
-    for (int j = threadIdx.x; j < n; j += TK_NT)
+    for (int j = lane; j < n; j += 32)
         keys[j] = orderable(row[j]);
-    __syncthreads();
+    __syncwarp();
     const int want = max(k, n_forced);
+    const bool pick = want - n_forced > 0;
     int remaining = want - n_forced; // to pick among the non-forced cubes
     uint32_t prefix = 0, mask = 0;
-    if (remaining > 0) {
+    if (pick) {
         for (int shift = 24; shift >= 0; shift -= 8) {
-            hist[threadIdx.x] = 0;
-            __syncthreads();
-            for (int j0 = 0; j0 < n; j0 += TK_NT) {
-                // warp-aggregated: lanes with the same digit add once
-                const int j = j0 + threadIdx.x;
+            for (int b = lane; b < 256; b += 32)
+                hist[b] = 0;
+            __syncwarp();
+            for (int j0 = 0; j0 < n; j0 += 32) {
+                const int j = j0 + lane;
                 const bool in = j < n && !forced(j) && (keys[j] & mask) == prefix;
                 const int dg = in ? int((keys[j] >> shift) & 255) : -1;
                 const unsigned same = __match_any_sync(0xffffffffu, dg);
-                if (in && (__ffs(same) - 1) == (threadIdx.x & 31))
+                if (in && (__ffs(same) - 1) == lane)
                     atomicAdd(&hist[dg], __popc(same));
             }
-            __syncthreads();
-            // The digit: the highest one whose bins from 255 down to it hold at least `remaining` keys (bin b is
-            // thread 255 - b's, so an exclusive scan over threads gives each bin the count above it).
-            const int b = TK_NT - 1 - threadIdx.x;
-            const int hb = hist[b];
-            int all;
-            const int above = block_exscan(hb, scan, all);
-            if (above < remaining && above + hb >= remaining) {
-                sh_digit = b;
-                sh_acc = above;
+            __syncwarp();
+            // Lane l holds bins 255 - 8 l - t (t < 8), so the bins run from the highest digit down across the lanes;
+            // the digit is the one whose bins from 255 down to it first hold at least `remaining` keys.
+            int c[8], sum = 0;
+#pragma unroll
+            for (int t = 0; t < 8; ++t)
+                c[t] = hist[255 - 8 * lane - t], sum += c[t];
+            int incl = sum;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o)
+                    incl += v;
             }
-            __syncthreads();
-            remaining -= sh_acc;
-            prefix |= uint32_t(sh_digit) << shift;
+            int above = incl - sum, digit = -1, acc = 0;
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+                if (digit < 0 && above < remaining && above + c[t] >= remaining)
+                    digit = 255 - 8 * lane - t, acc = above;
+                above += c[t];
+            }
+            const unsigned found = __ballot_sync(0xffffffffu, digit >= 0);
+            if (!found) // fewer candidates than wanted (k above the cubes): keep what the passes so far select
+                break;
+            const int src = __ffs(found) - 1; // exactly one lane holds the digit (the counts are non-negative)
+            digit = __shfl_sync(0xffffffffu, digit, src);
+            acc = __shfl_sync(0xffffffffu, acc, src);
+            remaining -= acc;
+            prefix |= uint32_t(digit) << shift;
             mask |= 255u << shift;
-            __syncthreads();
+            __syncwarp();
         }
     }
-    // Selected: forced; key above the threshold; or key equal to it among the first `remaining` such by index.
-    const int chunk = (n + TK_NT - 1) / TK_NT;
-    const int j0 = threadIdx.x * chunk, j1 = min(n, j0 + chunk);
-    const bool pick = want - n_forced > 0;
-    int ties = 0;
-    for (int j = j0; j < j1; ++j)
-        ties += pick && !forced(j) && keys[j] == prefix;
-    int total;
-    int tie_rank = block_exscan(ties, scan, total);
-    int count = 0;
-    for (int j = j0; j < j1; ++j) {
-        bool s = forced(j);
-        if (!s && pick) {
-            if (keys[j] > prefix)
-                s = true;
-            else if (keys[j] == prefix)
-                s = tie_rank++ < remaining;
-        }
-        count += s;
-    }
-    int out = block_exscan(count, scan, total);
-    tie_rank = block_exscan(ties, scan, total); // recompute for the write pass
     int32_t* dst = sel + (size_t(h) * n + i) * kcap;
-    for (int j = j0; j < j1; ++j) {
-        bool s = forced(j);
-        if (!s && pick) {
-            if (keys[j] > prefix)
-                s = true;
-            else if (keys[j] == prefix)
-                s = tie_rank++ < remaining;
-        }
-        if (s && out < kcap)
-            dst[out++] = j;
+    const unsigned lt = (1u << lane) - 1u;
+    int out = 0, ties_before = 0;
+    for (int j0 = 0; j0 < n; j0 += 32) {
+        const int j = j0 + lane;
+        const bool valid = j < n;
+        const bool f = valid && forced(j);
+        const uint32_t key = valid ? keys[j] : 0u;
+        const bool tie = valid && !f && pick && key == prefix;
+        const unsigned tb = __ballot_sync(0xffffffffu, tie);
+        const bool s = f || (valid && !f && pick && key > prefix) || (tie && ties_before + __popc(tb & lt) < remaining);
+        ties_before += __popc(tb);
+        const unsigned sb = __ballot_sync(0xffffffffu, s);
+        const int pos = out + __popc(sb & lt);
+        if (s && pos < kcap)
+            dst[pos] = j;
+        out += __popc(sb);
     }
-    if (threadIdx.x == 0)
+    if (lane == 0)
         nsel[size_t(h) * n + i] = min(want, kcap);
 }
 
@@ -305,12 +286,14 @@ void cube_scores(const float* mq, const float* mk, int heads, int cubes, float* 
 
 void cube_topk(const float* scores, int heads, const CubeGrid& g, int k, int local, int32_t* sel, int32_t* nsel, int kcap, cudaStream_t s)
 {
-    const size_t smem = size_t(g.cubes()) * 4;
-    if (smem > 160 * 1024)
+    const int n = g.cubes();
+    const size_t per_row = (size_t(n) + 256) * 4; // a warp's keys and histogram
+    if (per_row > 160 * 1024)
         throw CudaError("cube_topk: too many cubes");
+    const int rows = int(std::min<size_t>(TK_ROWS, (160 * 1024) / per_row));
     static std::atomic<uint64_t> opt_in;
     smem_opt_in(cube_topk_kernel, 160 * 1024, opt_in);
-    cube_topk_kernel<<<dim3(g.cubes(), heads), TK_NT, smem, s>>>(scores, g, k, local, sel, nsel, kcap);
+    cube_topk_kernel<<<dim3((n + rows - 1) / rows, heads), TK_ROWS * 32, rows * per_row, s>>>(scores, g, k, local, sel, nsel, kcap, rows);
     H3_CUDA(cudaGetLastError());
 }
 
